@@ -1,0 +1,586 @@
+"""HBM-resident cold store with page-based coarse-to-fine retrieval.
+
+Drop-in for the reference's ``ColdKVStore`` (kiv/cold_store.py:35-414): same
+constructor, ``evict_from_hot``, ``retrieve_top_kv``, ``cold_length``,
+``num_pages``, ``reset``, ``telemetry_snapshot``, ``reset_telemetry``,
+``memory_bytes`` and the ``_cached_*`` attributes outside code clears.
+
+What differs is where the data lives and who computes:
+
+* cold K/V are preallocated token slots in HBM (``[B, Hkv, capacity, D]``);
+  page summaries are written by the eviction kernel in the same pass that
+  copies the rows -- nothing is re-concatenated and nothing goes to host memory;
+* the hot window of the owning layer lives here too, as a buffer whose start
+  and length are kept in device memory next to the cold length, so the decode
+  step launches the same kernels with the same arguments every time;
+* every step of the retrieval runs in ``libkiv_b200.so`` (C ABI, ``include/
+  kiv_b200.h``); there is no CPU or PyTorch fallback, a missing library raises.
+
+The store can be one shard of a cold tier partitioned over GPUs (page p on
+shard p % shard_count); the collective steps then go through ``comm``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from . import _native as nat
+from .config import KIVConfig
+from .model_topology import ModelTopology
+from .telemetry import RetrievalTelemetry
+
+_MIN_COLD = 8192
+
+
+class ColdKVStore:
+    """Cold tier (and hot window buffer) of one independent KV layer."""
+
+    def __init__(self, kiv_config: KIVConfig, topology: ModelTopology, device: torch.device,
+                 *, shard_rank: int = 0, shard_count: int = 1, comm=None) -> None:
+        self.kiv_config = kiv_config
+        self.device = torch.device(device)
+        self._num_kv_groups = topology.num_query_heads // topology.num_kv_heads
+        self._num_kv_heads = topology.num_kv_heads
+        self._num_query_heads = topology.num_query_heads
+        self._head_dim = topology.head_dim
+        self._page_size = kiv_config.page_size
+        self._shard_rank = shard_rank
+        self._shard_count = shard_count
+        self._comm = comm
+        if shard_count > 1 and comm is None:
+            raise ValueError("a sharded ColdKVStore needs a comm")
+        self._batch: int | None = None
+        self._dtype: torch.dtype | None = None
+        self._k = self._v = self._summ = None
+        self._hk = self._hv = None
+        self._hot_cap = 0
+        self._state: torch.Tensor | None = None
+        # host mirrors of the device state (advanced by the same rules)
+        self._cold_len = 0
+        self._hot_start = 0
+        self._hot_len = 0
+        self._desc: nat.StoreDesc | None = None
+        self._ws: dict[tuple, tuple] = {}
+        self._bufs: dict[tuple, torch.Tensor] = {}
+        # shared-layer candidate reuse (attribute names of the reference)
+        self._cached_candidate_k: torch.Tensor | None = None
+        self._cached_candidate_v: torch.Tensor | None = None
+        self._cached_candidate_idx: torch.Tensor | None = None
+        self._cached_step: int = -1
+        self._cached_ws_key: tuple | None = None
+        self._telemetry = RetrievalTelemetry(kiv_config.telemetry)
+        # optional event recorder (``record(name)``) used by the benchmark to time
+        # the fine scoring kernel on its own stream
+        self._profile = None
+
+    # ------------------------------------------------------------------ sizes
+    @property
+    def cold_length(self) -> int:
+        return self._cold_len
+
+    @property
+    def num_pages(self) -> int:
+        return self._cold_len // self._page_size
+
+    @property
+    def _num_finalized(self) -> int:
+        return self.num_pages * self._page_size
+
+    @property
+    def _partial_len(self) -> int:
+        return self._cold_len % self._page_size
+
+    @property
+    def hot_length(self) -> int:
+        return self._hot_len
+
+    @property
+    def initialized(self) -> bool:
+        return self._state is not None
+
+    def _local_pages(self, n_global_pages: int) -> int:
+        r, n = self._shard_rank, self._shard_count
+        return (n_global_pages - r + n - 1) // n if n_global_pages > r else 0
+
+    # ------------------------------------------------------------ allocation
+    def _ensure_alloc(self, batch: int, dtype: torch.dtype) -> None:
+        if self._state is not None:
+            if batch != self._batch:
+                raise ValueError(f"store holds batch {self._batch}, got {batch}")
+            return
+        if self.device.type != "cuda":
+            raise nat.KIVNativeError(
+                f"ColdKVStore runs on CUDA devices only (got {self.device}); the B200 kernels "
+                "are the only implementation")
+        nat.dtype_code(dtype)
+        nat.load_library()
+        self._batch, self._dtype = batch, dtype
+        self._state = torch.zeros(nat.STATE_WORDS, dtype=torch.int64, device=self.device)
+        cap = self.kiv_config.cold_capacity or _MIN_COLD
+        self._alloc_cold(self._round_local(cap))
+
+    def _round_local(self, global_tokens: int) -> int:
+        """Local token slots that hold the pages of ``global_tokens`` cold tokens."""
+        pages = math.ceil(global_tokens / self._page_size)
+        return max(1, self._local_pages(pages)) * self._page_size
+
+    def _alloc_cold(self, cap: int) -> None:
+        B, H, D, S = self._batch, self._num_kv_heads, self._head_dim, self._page_size
+        k = torch.empty(B, H, cap, D, dtype=self._dtype, device=self.device)
+        v = torch.empty_like(k)
+        s = torch.empty(B, H, cap // S, D, dtype=self._dtype, device=self.device)
+        if self._k is not None:
+            old = self._k.shape[2]
+            k[:, :, :old].copy_(self._k)
+            v[:, :, :old].copy_(self._v)
+            s[:, :, :old // S].copy_(self._summ)
+        self._k, self._v, self._summ = k, v, s
+        self._desc = None
+        self._ws.clear()
+        self._cached_ws_key = None
+
+    def reserve(self, cold_tokens: int, hot_rows: int | None = None) -> None:
+        """Preallocate room for ``cold_tokens`` cold tokens (and a hot buffer of
+        ``hot_rows``) so later steps never reallocate (CUDA-graph capture)."""
+        if self._state is None:
+            raise RuntimeError("reserve() needs an initialized store (evict or append first)")
+        need = self._round_local(cold_tokens)
+        if need > self._k.shape[2]:
+            self._alloc_cold(need)
+        if hot_rows is not None and hot_rows > self._hot_cap:
+            self._grow_hot(hot_rows)
+
+    def _ensure_cold_room(self, new_cold_len: int) -> None:
+        need = self._round_local(new_cold_len)
+        cap = self._k.shape[2]
+        if need > cap:
+            self._alloc_cold(max(need, self._round_local(2 * self._cold_len)))
+
+    def _grow_hot(self, cap: int) -> None:
+        B, H, D = self._batch, self._num_kv_heads, self._head_dim
+        hk = torch.empty(B, H, cap, D, dtype=self._dtype, device=self.device)
+        hv = torch.empty_like(hk)
+        if self._hk is not None and self._hot_len > 0:
+            a, n = self._hot_start, self._hot_len
+            hk[:, :, :n].copy_(self._hk[:, :, a:a + n])
+            hv[:, :, :n].copy_(self._hv[:, :, a:a + n])
+        self._hk, self._hv, self._hot_cap = hk, hv, cap
+        self._set_hot_start(0)
+        self._desc = None
+        self._ws.clear()
+        self._cached_ws_key = None
+
+    def _set_hot_start(self, start: int) -> None:
+        self._hot_start = start
+        self._state[nat.ST_HOT_START].fill_(start)
+
+    def _ensure_hot_room(self, n_new: int) -> None:
+        """Keep start + len + n_new within the buffer (grow or compact)."""
+        need = self._hot_len + n_new
+        if need > self._hot_cap:
+            self._grow_hot(need + max(self.kiv_config.hot_slack, n_new) + self.kiv_config.hot_budget)
+        elif self._hot_start + need > self._hot_cap:
+            a, n = self._hot_start, self._hot_len
+            if n > 0:
+                if a >= n:
+                    self._hk[:, :, :n].copy_(self._hk[:, :, a:a + n])
+                    self._hv[:, :, :n].copy_(self._hv[:, :, a:a + n])
+                else:
+                    self._hk[:, :, :n].copy_(self._hk[:, :, a:a + n].clone())
+                    self._hv[:, :, :n].copy_(self._hv[:, :, a:a + n].clone())
+            self._set_hot_start(0)
+
+    def descriptor(self) -> nat.StoreDesc:
+        if self._desc is None:
+            self._desc = nat.StoreDesc(
+                self._batch, self._num_kv_heads, self._head_dim, self._page_size,
+                nat.dtype_code(self._dtype), self._shard_rank, self._shard_count, 0,
+                self._k.shape[2], self._hot_cap,
+                self._k.data_ptr(), self._v.data_ptr(), self._summ.data_ptr(),
+                nat.ptr(self._hk), nat.ptr(self._hv), self._state.data_ptr())
+        return self._desc
+
+    def _rows(self, x: torch.Tensor) -> torch.Tensor:
+        """New K/V rows as the kernels want them: store dtype/device, 16-byte aligned rows."""
+        if x.device != self.device or x.dtype != self._dtype:
+            x = x.to(device=self.device, dtype=self._dtype)
+        eb = x.element_size()
+        if (x.stride(-1) != 1 or x.data_ptr() % 16 or any((s * eb) % 16 for s in x.stride()[:3])):
+            x = x.contiguous()
+        return x
+
+    # ------------------------------------------------------------- eviction
+    def _invalidate_candidates(self) -> None:
+        self._cached_candidate_k = None
+        self._cached_candidate_v = None
+        self._cached_candidate_idx = None
+        self._cached_step = -1
+
+    def evict_from_hot(self, k_evicted: torch.Tensor, v_evicted: torch.Tensor) -> None:
+        """Append rows to the cold tier, building page summaries as pages fill
+        (kiv/cold_store.py:142-184).  The hot window is not touched."""
+        self._invalidate_candidates()
+        B, _, n, _ = k_evicted.shape
+        self._ensure_alloc(B, k_evicted.dtype)
+        if n == 0:
+            return
+        k, v = self._rows(k_evicted), self._rows(v_evicted)
+        self._ensure_cold_room(self._cold_len + n)
+        with torch.cuda.device(self.device):
+            nat.check(nat.lib().kiv_append_evict(
+                ctypes.byref(self.descriptor()), k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1),
+                k.stride(2), n, nat.KEEP_DIRECT, n, nat.stream_ptr(self.device)), "evict_from_hot")
+        self._cold_len += n
+
+    def append_and_evict(self, k_new: torch.Tensor | None, v_new: torch.Tensor | None,
+                         keep: int) -> int:
+        """Append new rows to the hot window, then move the oldest
+        ``max(0, hot + new - keep)`` rows to the cold tier (``keep < 0``: none).
+        One kernel launch.  Returns the number of rows evicted."""
+        if k_new is not None:
+            B, n = k_new.shape[0], k_new.shape[2]
+            self._ensure_alloc(B, k_new.dtype)
+        else:
+            n = 0
+            if self._state is None:
+                return 0
+        n_ev = 0 if keep < 0 else min(max(self._hot_len + n - keep, 0), self._hot_len + n)
+        if n == 0 and n_ev == 0:
+            return 0
+        self._ensure_hot_room(n)
+        self._ensure_cold_room(self._cold_len + n_ev)
+        if n > 0:
+            k, v = self._rows(k_new), self._rows(v_new)
+            kp, vp, sb, sh, st = k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1), k.stride(2)
+        else:
+            kp = vp = None
+            sb = sh = st = 0
+        with torch.cuda.device(self.device):
+            nat.check(nat.lib().kiv_append_evict(
+                ctypes.byref(self.descriptor()), kp, vp, sb, sh, st, n, keep, n_ev,
+                nat.stream_ptr(self.device)), "append_evict")
+        self._cold_len += n_ev
+        self._hot_start += n_ev
+        self._hot_len += n - n_ev
+        if n_ev > 0:
+            self._invalidate_candidates()
+        return n_ev
+
+    # ---------------------------------------------------------- hot window
+    def hot_keys(self) -> torch.Tensor:
+        a, n = self._hot_start, self._hot_len
+        return self._hk[:, :, a:a + n]
+
+    def hot_values(self) -> torch.Tensor:
+        a, n = self._hot_start, self._hot_len
+        return self._hv[:, :, a:a + n]
+
+    def set_hot(self, keys: torch.Tensor, values: torch.Tensor) -> None:
+        """Replace the hot window content (HF layer assignment, crop, reorder)."""
+        B, _, n, _ = keys.shape
+        self._ensure_alloc(B, keys.dtype)
+        if self._hk is not None:
+            base = self._hk.untyped_storage().data_ptr(), self._hv.untyped_storage().data_ptr()
+            if keys.untyped_storage().data_ptr() in base or values.untyped_storage().data_ptr() in base:
+                keys, values = keys.clone(), values.clone()
+        if n > self._hot_cap:
+            self._hot_len = 0
+            self._grow_hot(n + self.kiv_config.hot_slack + self.kiv_config.hot_budget)
+        self._hk[:, :, :n].copy_(keys)
+        self._hv[:, :, :n].copy_(values)
+        self._hot_len = n
+        self._set_hot_start(0)
+        self._state[nat.ST_HOT_LEN].fill_(n)
+
+    def truncate_hot(self, n: int) -> None:
+        self._hot_len = n
+        self._state[nat.ST_HOT_LEN].fill_(n)
+
+    # ------------------------------------------------------------ retrieval
+    def _query(self, query: torch.Tensor) -> torch.Tensor:
+        if query.device != self.device or query.dtype != self._dtype:
+            query = query.to(device=self.device, dtype=self._dtype)
+        eb = query.element_size()
+        if (query.stride(-1) != 1 or query.data_ptr() % 16
+                or any((s * eb) % 16 for s in query.stride()[:3])):
+            query = query.contiguous()
+        return query
+
+    def _workspace(self, qd: nat.QueryDesc, B: int, Hq: int, Q: int, top_pages: int, top_p: int):
+        key = (B, Hq, Q, top_pages, top_p)
+        ws = self._ws.get(key)
+        if ws is None:
+            desc = self.descriptor()
+            nbytes = nat.lib().kiv_workspace_bytes(ctypes.byref(desc), ctypes.byref(qd))
+            if nbytes == 0:
+                nat.check(nat.KIV_OK + 1, "workspace size")
+            # zeroed once: the page-flag array must start clear (kernels keep it clear)
+            buf = torch.zeros(nbytes + 256, dtype=torch.uint8, device=self.device)
+            off = (-buf.data_ptr()) % 256
+            buf = buf[off:off + nbytes]
+            lay = (ctypes.c_int64 * 10)()
+            nat.check(nat.lib().kiv_workspace_layout(ctypes.byref(desc), ctypes.byref(qd), lay),
+                      "workspace layout")
+            ws = (buf, tuple(lay))
+            self._ws[key] = ws
+        return key, ws
+
+    def _buffer(self, name: str, shape: tuple, dtype: torch.dtype) -> torch.Tensor:
+        key = (name,) + tuple(shape) + (dtype,)
+        t = self._bufs.get(key)
+        if t is None:
+            t = torch.empty(shape, dtype=dtype, device=self.device)
+            self._bufs[key] = t
+        return t
+
+    def _expected_P(self, top_pages: int, top_p: int) -> int | None:
+        """Selected count when it follows from host-known sizes, else None."""
+        p = min(top_p, self._cold_len)
+        guaranteed = min(top_pages, self.num_pages) * self._page_size + self._partial_len
+        return p if p <= guaranteed else None
+
+    def _select(self, query: torch.Tensor, scaling: float, kiv_config: KIVConfig, step: int,
+                softcap: float | None = None):
+        """Coarse (or reuse) + fine.  Returns (sel [B, top_p] int32, ws key, ws, qdesc)."""
+        B, Hq, Q, _ = query.shape
+        top_pages, top_p = kiv_config.top_pages, kiv_config.top_p
+        qd = nat.query_desc(query, scaling, top_pages, top_p, softcap)
+        wkey, (ws, lay) = self._workspace(qd, B, Hq, Q, top_pages, top_p)
+        desc = self.descriptor()
+        L = nat.lib()
+        s = nat.stream_ptr(self.device)
+        reuse = (step >= 0 and step == self._cached_step and self._cached_candidate_k is not None
+                 and self._cached_candidate_k.shape[0] == B and self._cached_ws_key == wkey)
+        if reuse:
+            self._telemetry.record_coarse_skipped(cold_length=self._cold_len)
+        else:
+            if self._profile is not None:
+                self._profile.record("coarse_begin")
+            if self._shard_count == 1:
+                nat.check(L.kiv_coarse_select(ctypes.byref(desc), ctypes.byref(qd), ws.data_ptr(),
+                                              ws.numel(), None, None, s), "coarse_select")
+            else:
+                self._sharded_coarse(desc, qd, ws, B * Hq * Q, top_pages, s)
+            if self.num_pages > 0:
+                uni = ws[lay[2]:lay[2] + 4 * lay[8]].view(torch.int32)
+                self._telemetry.record_coarse(state=self._state, union=uni, num_pages=self.num_pages,
+                                              cold_length=self._cold_len,
+                                              n_scores=B * Hq * Q * self._local_pages(self.num_pages))
+            else:
+                self._telemetry.record_coarse_skipped(cold_length=self._cold_len)
+            marker = self._buffer("marker", (B, 0), torch.int8)
+            self._cached_candidate_k = marker
+            self._cached_candidate_v = marker
+            self._cached_candidate_idx = ws[lay[2]:lay[2] + 4 * lay[8]].view(torch.int32)
+            self._cached_ws_key = wkey
+            if step >= 0:
+                self._cached_step = step
+        sel = self._buffer("sel", (B, top_p), torch.int32)
+        if self._shard_count == 1:
+            prof = self._profile
+            if prof is not None:
+                prof.record("fine_score_begin")
+            nat.check(L.kiv_fine_score(ctypes.byref(desc), ctypes.byref(qd), ws.data_ptr(), ws.numel(), s),
+                      "fine_score")
+            if prof is not None:
+                prof.record("fine_score_end")
+            nat.check(L.kiv_fine_topk(ctypes.byref(desc), ctypes.byref(qd), ws.data_ptr(), ws.numel(),
+                                      sel.data_ptr(), None, s), "fine_topk")
+            if prof is not None:
+                prof.record("fine_topk_end")
+            sel_local = sel
+        else:
+            sel_local = self._sharded_fine(desc, qd, ws, B, top_p, sel, s)
+        return sel, sel_local, ws, qd
+
+    def _record_fine(self, sel: torch.Tensor, P: int | None, top_p: int) -> None:
+        if self._telemetry.enabled:
+            if P is None:
+                P = self.read_state()[nat.ST_SEL]
+            self._telemetry.record_fine(state=self._state, selected=sel, actual_P=int(P),
+                                        requested_P=top_p, cold_length=self._cold_len,
+                                        n_scores=0)
+
+    def retrieve_indices(self, query: torch.Tensor, scaling: float, kiv_config: KIVConfig,
+                         step: int = -1) -> tuple[torch.Tensor, int] | None:
+        """Global token ids selected for each batch row: ``(sel [B, top_p], P)``;
+        the first P entries of each row are valid, ascending."""
+        if self._cold_len == 0:
+            return None
+        query = self._query(query)
+        with torch.cuda.device(self.device):
+            sel, _, _, _ = self._select(query, scaling, kiv_config, step)
+            P = self._expected_P(kiv_config.top_pages, kiv_config.top_p)
+            if P is None:
+                P = int(self.read_state()[nat.ST_SEL])
+            self._record_fine(sel, P, kiv_config.top_p)
+        return sel, P
+
+    def retrieve_top_kv(self, query: torch.Tensor, scaling: float, kiv_config: KIVConfig,
+                        step: int = -1) -> tuple[torch.Tensor, torch.Tensor] | tuple[None, None]:
+        """Coarse-to-fine retrieval returning the selected K and V, ``[B, Hkv, P, D]``
+        each, or ``(None, None)`` when the cold tier is empty (kiv/cold_store.py:283-371).
+        Rows come in ascending token order (the reference returns them in
+        descending-score order; attention over them does not depend on it)."""
+        r = self.retrieve_indices(query, scaling, kiv_config, step)
+        if r is None:
+            return None, None
+        sel, P = r
+        B = sel.shape[0]
+        out_k = torch.empty(B, self._num_kv_heads, P, self._head_dim, dtype=self._dtype,
+                            device=self.device)
+        out_v = torch.empty_like(out_k)
+        if self._shard_count > 1:
+            out_k.zero_()
+            out_v.zero_()
+        with torch.cuda.device(self.device):
+            nat.check(nat.lib().kiv_gather_rows(ctypes.byref(self.descriptor()), sel.data_ptr(),
+                                                sel.shape[1], P, out_k.data_ptr(), out_v.data_ptr(),
+                                                nat.stream_ptr(self.device)), "gather_rows")
+        if self._shard_count > 1:
+            self._comm.all_reduce_sum(out_k)
+            self._comm.all_reduce_sum(out_v)
+        return out_k, out_v
+
+    def attend(self, query: torch.Tensor, scaling: float, kiv_config: KIVConfig, step: int = -1,
+               *, mask_add: torch.Tensor | None = None, causal: bool = False,
+               softcap: float | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+        """Fused retrieval attention over [selected cold ; hot window]:
+        ``query [B, Hq, Q, D] -> [B, Q, Hq, D]`` (the HF attention-interface layout).
+
+        ``mask_add``: float32 additive mask over the hot rows ``[B, 1|Hq, Q, hot]``;
+        ``causal``: query position i sees hot row j iff j <= hot - Q + i.
+        Cold rows are always attendable (kiv/mask_utils.py:8-38)."""
+        query = self._query(query)
+        B, Hq, Q, D = query.shape
+        if out is None:
+            out = torch.empty(B, Q, Hq, D, dtype=self._dtype, device=self.device)
+        elif (out.shape != (B, Q, Hq, D) or out.dtype != self._dtype or not out.is_contiguous()
+              or out.device != self.device):
+            raise ValueError("out must be a contiguous [B, Q, Hq, D] tensor of the store dtype")
+        md = nat.mask_desc(mask_add, causal)
+        with torch.cuda.device(self.device):
+            s = nat.stream_ptr(self.device)
+            if self._cold_len > 0:
+                sel, sel_local, ws, qd = self._select(query, scaling, kiv_config, step, softcap)
+                if self._telemetry.enabled:
+                    self._record_fine(sel, self._expected_P(kiv_config.top_pages, kiv_config.top_p),
+                                      kiv_config.top_p)
+            else:
+                qd = nat.query_desc(query, scaling, kiv_config.top_pages, kiv_config.top_p, softcap)
+                _, (ws, _) = self._workspace(qd, B, Hq, Q, kiv_config.top_pages, kiv_config.top_p)
+                sel_local = self._buffer("sel", (B, kiv_config.top_p), torch.int32)
+                self._zero_selcounts(ws, qd)
+            L = nat.lib()
+            desc = self.descriptor()
+            desc.hot_hint = self._hot_len
+            if self._shard_count == 1:
+                nat.check(L.kiv_attend(ctypes.byref(desc), ctypes.byref(qd), ctypes.byref(md),
+                                       ws.data_ptr(), ws.numel(), sel_local.data_ptr(),
+                                       sel_local.shape[1], 0, 1, out.data_ptr(), None, s), "attend")
+                if self._profile is not None:
+                    self._profile.record("attend_end")
+            else:
+                R = B * Hq * Q
+                part = self._buffer("apart", (R, D + 4), torch.float32)
+                nat.check(L.kiv_attend(ctypes.byref(desc), ctypes.byref(qd), ctypes.byref(md),
+                                       ws.data_ptr(), ws.numel(), sel_local.data_ptr(),
+                                       sel_local.shape[1], self._shard_rank, self._shard_count,
+                                       None, part.data_ptr(), s), "attend")
+                gathered = self._buffer("apart_all", (self._shard_count, R, D + 4), torch.float32)
+                self._comm.all_gather(gathered, part)
+                nat.check(L.kiv_attend_merge(ctypes.byref(desc), ctypes.byref(qd), gathered.data_ptr(),
+                                             self._shard_count, out.data_ptr(), s), "attend_merge")
+        return out
+
+    def _zero_selcounts(self, ws: torch.Tensor, qd: nat.QueryDesc) -> None:
+        lay = (ctypes.c_int64 * 10)()
+        nat.check(nat.lib().kiv_workspace_layout(ctypes.byref(self.descriptor()), ctypes.byref(qd), lay),
+                  "workspace layout")
+        ws[lay[4]:lay[4] + 4 * self._batch].zero_()
+
+    # ---------------------------------------------------------- sharded steps
+    def _sharded_coarse(self, desc, qd, ws, R: int, K: int, s: int) -> None:
+        L = nat.lib()
+        sc = self._buffer("crow_s", (R, K), torch.float32)
+        pg = self._buffer("crow_p", (R, K), torch.int32)
+        nat.check(L.kiv_coarse_select(ctypes.byref(desc), ctypes.byref(qd), ws.data_ptr(), ws.numel(),
+                                      sc.data_ptr(), pg.data_ptr(), s), "coarse_select")
+        n = self._shard_count
+        all_s = self._buffer("crow_s_all", (n, R, K), torch.float32)
+        all_p = self._buffer("crow_p_all", (n, R, K), torch.int32)
+        self._comm.all_gather(all_s, sc)
+        self._comm.all_gather(all_p, pg)
+        nat.check(L.kiv_coarse_merge(ctypes.byref(desc), ctypes.byref(qd), ws.data_ptr(), ws.numel(),
+                                     all_s.data_ptr(), all_p.data_ptr(), n, s), "coarse_merge")
+
+    def _sharded_fine(self, desc, qd, ws, B: int, top_p: int, sel: torch.Tensor, s: int) -> torch.Tensor:
+        L = nat.lib()
+        lt = self._buffer("fl_t", (B, top_p), torch.int32)
+        ls = self._buffer("fl_s", (B, top_p), torch.float32)
+        nat.check(L.kiv_fine_select(ctypes.byref(desc), ctypes.byref(qd), ws.data_ptr(), ws.numel(),
+                                    lt.data_ptr(), ls.data_ptr(), s), "fine_select")
+        n = self._shard_count
+        all_t = self._buffer("fl_t_all", (n, B, top_p), torch.int32)
+        all_s = self._buffer("fl_s_all", (n, B, top_p), torch.float32)
+        self._comm.all_gather(all_t, lt)
+        self._comm.all_gather(all_s, ls)
+        sel_local = self._buffer("sel_local", (B, top_p), torch.int32)
+        nat.check(L.kiv_fine_merge(ctypes.byref(desc), ctypes.byref(qd), ws.data_ptr(), ws.numel(),
+                                   all_s.data_ptr(), all_t.data_ptr(), n, sel.data_ptr(),
+                                   sel_local.data_ptr(), s), "fine_merge")
+        return sel_local
+
+    # --------------------------------------------------------------- misc API
+    def read_state(self) -> list[int]:
+        """Device state words (syncs); for tests and debugging."""
+        words = (ctypes.c_int64 * nat.STATE_WORDS)()
+        with torch.cuda.device(self.device):
+            nat.check(nat.lib().kiv_read_state(ctypes.byref(self.descriptor()), words,
+                                               nat.stream_ptr(self.device)), "read_state")
+        return list(words)
+
+    def page_summaries(self) -> torch.Tensor | None:
+        """Summaries of this shard's finalized pages ``[B, Hkv, local pages, D]``."""
+        if self._summ is None:
+            return None
+        return self._summ[:, :, :self._local_pages(self.num_pages)]
+
+    def reset(self) -> None:
+        """Clear all cold storage and the hot window (buffers are kept for reuse)."""
+        self._cold_len = 0
+        self._hot_start = 0
+        self._hot_len = 0
+        if self._state is not None:
+            self._state.zero_()
+        self._invalidate_candidates()
+
+    def telemetry_snapshot(self) -> dict:
+        return self._telemetry.snapshot()
+
+    def reset_telemetry(self) -> None:
+        self._telemetry = RetrievalTelemetry(self.kiv_config.telemetry)
+
+    def memory_bytes(self) -> dict[str, int]:
+        """Bytes by tier.  The reference's keys are kept (its host tiers are
+        empty here); the HBM-resident cold K/V and reservations are added."""
+        if self._state is None:
+            return {"k_index_cpu": 0, "v_store_cpu": 0, "page_summaries_gpu": 0, "partial_gpu": 0,
+                    "cold_k_gpu": 0, "cold_v_gpu": 0, "reserved_gpu": 0}
+        e = self._k.element_size()
+        row = self._batch * self._num_kv_heads * self._head_dim * e
+        local_fin = self._local_pages(self.num_pages) * self._page_size
+        part = self._partial_len if (self.num_pages % self._shard_count) == self._shard_rank else 0
+        reserved = sum(t.numel() * t.element_size() for t in (self._k, self._v, self._summ))
+        return {
+            "k_index_cpu": 0,
+            "v_store_cpu": 0,
+            "page_summaries_gpu": self._local_pages(self.num_pages) * row,
+            "partial_gpu": 2 * part * row,
+            "cold_k_gpu": local_fin * row,
+            "cold_v_gpu": local_fin * row,
+            "reserved_gpu": reserved,
+        }

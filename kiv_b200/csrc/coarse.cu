@@ -1,0 +1,287 @@
+// Kernel (b): coarse page scoring fused with the per-row top-`top_pages`
+// select and the page union.
+//
+// Reference behaviour restated (kiv/cold_store.py:203-230):
+//   s[b,h,q,p] = scaling * <q[b,h,q], summary[b, h // G, p]>
+//   per (b,h,q): the min(top_pages, Np) best pages; union over b, h, q, sorted.
+// The reference materializes repeat_kv(summaries) (G copies) and runs a
+// GEMM; here each summary row is read once per KV head and scored against all
+// G*Q query rows of that head in registers.  Scores are written as 32-bit
+// order-preserving keys for the radix select.
+#include <algorithm>
+
+#include "common.cuh"
+#include "internal.h"
+#include "select.cuh"
+
+namespace kiv {
+
+constexpr int CS_THREADS = 128;      // coarse scoring
+constexpr int CS_PAGES = 16;         // pages per work item (one bulk copy)
+constexpr int TK_THREADS = 256;      // per-row top-k
+
+// local finalized pages of this shard given the global finalized count
+__device__ __forceinline__ int64_t local_pages(int64_t np_global, int rank, int n) {
+  return np_global > rank ? (np_global - rank + n - 1) / n : 0;
+}
+
+template <typename T, int LPR, int VPL, int RCH>
+__global__ void __launch_bounds__(CS_THREADS)
+coarse_scores_kernel(kiv_store st, kiv_query q, Workspace w) {
+  griddep_wait();
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    st.state[KIV_ST_COARSE_MAX] = 0;
+    st.state[KIV_ST_COARSE_SUM] = 0;
+  }
+  extern __shared__ __align__(128) uint8_t cs_smem[];
+  __shared__ uint64_t bar;
+  __shared__ int s_fail;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane % LPR;                    // lane within its row group
+  const int grp = lane / LPR;                  // row group within the warp
+  constexpr int GPW = 32 / LPR;                // row groups per warp
+  constexpr int NW = CS_THREADS / 32;
+  const int D = st.head_dim, H = st.num_kv_heads, S = st.page_size;
+  const int nv = D / Elem<T>::V;
+  const int G = q.num_query_heads / H, Q = q.query_len;
+  const int rows_kv = G * Q;
+  const int nchunks = (rows_kv + RCH - 1) / RCH;
+  const int64_t np_global = st_ld(st.state, KIV_ST_COLD_LEN) / S;
+  const int64_t np = local_pages(np_global, st.shard_rank, st.shard_count);
+  const int64_t nblk = (np + CS_PAGES - 1) / CS_PAGES;
+  const int64_t items = (int64_t)st.batch * H * nchunks * nblk;
+  const T *qb = reinterpret_cast<const T *>(q.q);
+  const T *summ = reinterpret_cast<const T *>(st.summaries);
+  T *tile = reinterpret_cast<T *>(cs_smem);    // [CS_PAGES][D]
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    mbar_fence_init();
+    s_fail = 0;
+  }
+  __syncthreads();
+
+  uint32_t phase = 0;
+  for (int64_t it = blockIdx.x; it < items; it += gridDim.x, phase ^= 1) {
+    const int64_t pb = it % nblk;
+    const int64_t rest = it / nblk;
+    const int ch = (int)(rest % nchunks);
+    const int bh = (int)(rest / nchunks);
+    const int b = bh / H, kvh = bh % H;
+    const int64_t p0 = pb * CS_PAGES;
+    const int npg = (int)std::min<int64_t>(CS_PAGES, np - p0);
+    if (threadIdx.x == 0) {
+      // one bulk copy: this block's summaries are contiguous
+      const uint32_t bytes = (uint32_t)npg * D * sizeof(T);
+      mbar_arrive_tx(&bar, bytes);
+      bulk_g2s(tile, summ + ((int64_t)bh * w.np_cap + p0) * D, bytes, &bar);
+    }
+    RowDot<T, LPR, VPL, RCH> dot;
+    const T *qrows[RCH];
+#pragma unroll
+    for (int r = 0; r < RCH; ++r) {
+      const int rr = ch * RCH + r;
+      if (rr < rows_kv) {
+        const int h = kvh * G + rr / Q, t = rr % Q;
+        qrows[r] = qb + b * q.stride_b + h * q.stride_h + t * q.stride_t;
+      } else {
+        qrows[r] = nullptr;
+      }
+    }
+    dot.load_query(qrows, g, nv, 1.0f);
+    if (!mbar_wait_bounded(&bar, phase)) s_fail = 1;
+    __syncthreads();
+    if (s_fail) break;
+    for (int pi0 = 0; pi0 < npg; pi0 += NW * GPW) {
+      const int pi = pi0 + warp * GPW + grp;
+      const bool valid = pi < npg;
+      float acc[RCH];
+      dot.template partial<false>(valid ? tile + (size_t)pi * D : nullptr, g, nv, acc);
+      int base = 0;
+      tr_reduce<RCH, LPR / 2>(acc, lane, base);
+      constexpr int NOUT = TrOut<RCH, LPR>::N;
+      constexpr int REPL = TrOut<RCH, LPR>::REPL;
+      if (valid && (g % REPL) == 0) {
+#pragma unroll
+        for (int i = 0; i < NOUT; ++i) {
+          const int rr = ch * RCH + base + i;
+          if (rr < rows_kv) {
+            const int h = kvh * G + rr / Q, t = rr % Q;
+            const int64_t R_idx = ((int64_t)b * q.num_query_heads + h) * Q + t;
+            w.scores[R_idx * w.np_cap + p0 + pi] = acc[i] * q.scaling;
+          }
+        }
+      }
+    }
+    __syncthreads();  // the tile is free for the next block
+  }
+  if (s_fail && threadIdx.x == 0)
+    atomicOr(reinterpret_cast<unsigned long long *>(st.state + KIV_ST_ERROR), (unsigned long long)KIV_ERRBIT_WAIT_TIMEOUT);
+}
+
+// Per-row top-k.  shard_count == 1: mark pages and let the last block build
+// the union.  shard_count > 1: write the row's local list (score, page id).
+__global__ void __launch_bounds__(TK_THREADS)
+coarse_topk_kernel(kiv_store st, kiv_query q, Workspace w, float *row_scores, int32_t *row_pages) {
+  griddep_wait();
+  extern __shared__ uint4 dyn_smem[];
+  __shared__ SelectSmem<TK_THREADS> sm;
+  const int S = st.page_size;
+  const int64_t np_global = st_ld(st.state, KIV_ST_COLD_LEN) / S;
+  const int64_t np = local_pages(np_global, st.shard_rank, st.shard_count);
+  const int row = blockIdx.x;
+  const int K = q.top_pages;
+  if (np > 0) {
+    // stage this row's keys in shared memory (converted from float bits)
+    uint32_t *keys = reinterpret_cast<uint32_t *>(dyn_smem);
+    const float *src = w.scores + (int64_t)row * w.np_cap;
+    for (int64_t i = threadIdx.x; i < np; i += TK_THREADS) keys[i] = f2key(src[i]);
+    __syncthreads();
+    block_stats<TK_THREADS>(keys, (int)np, st.state + KIV_ST_COARSE_MAX, st.state + KIV_ST_COARSE_SUM);
+    const uint32_t k = (uint32_t)(K < np ? (int64_t)K : np);
+    uint32_t T = 0, need = 0;
+    const bool all = (int64_t)k >= np;
+    if (!all) radix_threshold<TK_THREADS, 1>(keys, (int)np, k, sm, T, need);
+    const int rank = st.shard_rank, nsh = st.shard_count;
+    if (nsh == 1) {
+      ordered_emit<TK_THREADS, 1>(keys, (int)np, T, need, all, sm,
+                                  [&](int i, uint32_t) { w.flags[i] = 1; });
+    } else {
+      float *ls = row_scores + (int64_t)row * K;
+      int32_t *lpg = row_pages + (int64_t)row * K;
+      ordered_emit<TK_THREADS, 1>(keys, (int)np, T, need, all, sm, [&](int i, uint32_t pos) {
+        ls[pos] = key2f(keys[i]);
+        lpg[pos] = (int32_t)((int64_t)i * nsh + rank);
+      });
+      for (int j = (int)k + threadIdx.x; j < K; j += TK_THREADS) {
+        ls[j] = 0.f;
+        lpg[j] = -1;
+      }
+    }
+  } else if (st.shard_count > 1) {
+    for (int j = threadIdx.x; j < K; j += TK_THREADS) {
+      row_scores[(int64_t)row * K + j] = 0.f;
+      row_pages[(int64_t)row * K + j] = -1;
+    }
+  }
+  if (st.shard_count == 1) {
+    if (last_block(reinterpret_cast<unsigned long long *>(st.state + CTR_COARSE), gridDim.x)) {
+      const int64_t u = compact_flags<TK_THREADS>(w.flags, np, w.uni, w.u_cap, 1, 0, sm.scan);
+      if (threadIdx.x == 0) st.state[KIV_ST_UNION] = u;
+    }
+  }
+}
+
+// Merge gathered per-row lists [n][R][K] into the global per-row top-k and
+// keep the union pages this shard owns.  Ties at the threshold are broken by
+// the lowest page id.
+__global__ void __launch_bounds__(TK_THREADS)
+coarse_merge_kernel(kiv_store st, kiv_query q, Workspace w, const float *ls, const int32_t *lp,
+                    int32_t n) {
+  griddep_wait();
+  extern __shared__ uint4 dyn_smem[];
+  __shared__ SelectSmem<TK_THREADS> sm;
+  const int S = st.page_size;
+  const int64_t np_global = st_ld(st.state, KIV_ST_COLD_LEN) / S;
+  const int row = blockIdx.x;
+  const int K = q.top_pages;
+  const int64_t R = w.R;
+  const int m = n * K;
+  uint32_t *keys = reinterpret_cast<uint32_t *>(dyn_smem);
+  int32_t *ids = reinterpret_cast<int32_t *>(keys + m);
+  for (int i = threadIdx.x; i < m; i += TK_THREADS) {
+    const int src = i / K, j = i % K;
+    const int64_t off = ((int64_t)src * R + row) * K + j;
+    const int32_t pg = lp[off];
+    ids[i] = pg;
+    keys[i] = pg >= 0 ? f2key(ls[off]) : 0u;
+  }
+  __syncthreads();
+  const uint32_t k = (uint32_t)(K < np_global ? (int64_t)K : np_global);
+  if (k > 0) {
+    uint32_t T = 0, need = 0;
+    radix_threshold<TK_THREADS, 1>(keys, m, k, sm, T, need);
+    // entries == T: take the `need` lowest page ids
+    for (int i = threadIdx.x; i < m; i += TK_THREADS) {
+      bool take = keys[i] > T;
+      if (!take && keys[i] == T && ids[i] >= 0) {
+        uint32_t rank = 0;
+        for (int j = 0; j < m; ++j)
+          rank += (keys[j] == T && ids[j] >= 0 && ids[j] < ids[i]) ? 1u : 0u;
+        take = rank < need;
+      }
+      if (take && ids[i] >= 0 && (ids[i] % st.shard_count) == st.shard_rank)
+        w.flags[ids[i] / st.shard_count] = 1;
+    }
+  }
+  if (last_block(reinterpret_cast<unsigned long long *>(st.state + CTR_MERGE), gridDim.x)) {
+    const int64_t np = local_pages(np_global, st.shard_rank, st.shard_count);
+    const int64_t u = compact_flags<TK_THREADS>(w.flags, np, w.uni, w.u_cap, st.shard_count,
+                                                st.shard_rank, sm.scan);
+    if (threadIdx.x == 0) st.state[KIV_ST_UNION] = u;
+  }
+}
+
+template <typename T, int LPR, int VPL, int RCH>
+static void launch_cs(const kiv_store *st, const kiv_query *q, const Workspace &w, cudaStream_t s) {
+  const int H = st->num_kv_heads;
+  const int rows_kv = (q->num_query_heads / H) * q->query_len;
+  const int64_t nchunks = ceil_div(rows_kv, RCH);
+  const int64_t items = (int64_t)st->batch * H * nchunks * ceil_div(w.np_cap, CS_PAGES);
+  const int64_t grid = std::min<int64_t>(std::max<int64_t>(items, 1), (int64_t)sm_count() * 8);
+  const size_t smem = (size_t)CS_PAGES * st->head_dim * sizeof(T);
+  coarse_scores_kernel<T, LPR, VPL, RCH><<<(unsigned)grid, CS_THREADS, smem, s>>>(*st, *q, w);
+}
+
+template <typename T>
+static kiv_status dispatch_cs(const kiv_store *st, const kiv_query *q, const Workspace &w,
+                              cudaStream_t s) {
+  const int nv = st->head_dim / Elem<T>::V;
+  const int rows_kv = (q->num_query_heads / st->num_kv_heads) * q->query_len;
+  const bool small = rows_kv <= 4;
+#define KIV_CS(LPR, VPL)                                          \
+  do {                                                            \
+    if (small) launch_cs<T, LPR, VPL, 4>(st, q, w, s);            \
+    else launch_cs<T, LPR, VPL, 8>(st, q, w, s);                  \
+  } while (0)
+  if (nv <= 2) KIV_CS(2, 1);
+  else if (nv <= 4) KIV_CS(4, 1);
+  else if (nv <= 8) KIV_CS(8, 1);
+  else if (nv <= 16) KIV_CS(16, 1);
+  else if (nv <= 32) KIV_CS(32, 1);
+  else if (nv <= 64) KIV_CS(32, 2);
+  else return KIV_ERR_UNSUPPORTED;
+#undef KIV_CS
+  return KIV_OK;
+}
+
+kiv_status launch_coarse(const kiv_store *st, const kiv_query *q, const Workspace &w,
+                         float *row_scores, int32_t *row_pages, cudaStream_t s) {
+  kiv_status rc;
+  switch (st->dtype) {
+    case KIV_DTYPE_F32: rc = dispatch_cs<float>(st, q, w, s); break;
+    case KIV_DTYPE_BF16: rc = dispatch_cs<__nv_bfloat16>(st, q, w, s); break;
+    case KIV_DTYPE_F16: rc = dispatch_cs<__half>(st, q, w, s); break;
+    default: rc = KIV_ERR_UNSUPPORTED;
+  }
+  if (rc != KIV_OK) return rc;
+  const size_t smem = (size_t)w.np_cap * sizeof(uint32_t);
+  if (smem > 200 * 1024) {
+    set_error("coarse: %lld pages per shard exceed the shared-memory select (max %d)",
+              (long long)w.np_cap, 200 * 1024 / 4);
+    return KIV_ERR_CAPACITY;
+  }
+  cudaFuncSetAttribute(coarse_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  coarse_topk_kernel<<<(unsigned)w.R, TK_THREADS, smem, s>>>(*st, *q, w, row_scores, row_pages);
+  return cuda_status(cudaGetLastError(), "coarse");
+}
+
+kiv_status launch_coarse_merge(const kiv_store *st, const kiv_query *q, const Workspace &w,
+                               const float *ls, const int32_t *lp, int32_t n, cudaStream_t s) {
+  const size_t smem = (size_t)n * q->top_pages * (sizeof(uint32_t) + sizeof(int32_t));
+  if (smem > 200 * 1024) return KIV_ERR_CAPACITY;
+  cudaFuncSetAttribute(coarse_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  coarse_merge_kernel<<<(unsigned)w.R, TK_THREADS, smem, s>>>(*st, *q, w, ls, lp, n);
+  return cuda_status(cudaGetLastError(), "coarse_merge");
+}
+
+}  // namespace kiv

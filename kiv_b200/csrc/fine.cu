@@ -1,0 +1,465 @@
+// Kernel (c): fine token scoring fused with the top-`top_p` token select.
+//
+// Reference behaviour restated (kiv/cold_store.py:227-262, :301, :332-347):
+//   candidates = every token of the union pages (ascending) + the partial page;
+//   f[b,h,q,c] = scaling * <q[b,h,q], K[b, h // G, c]>;  agg[b,c] = max_{h,q} f;
+//   keep the P = min(top_p, cold_len, C) best candidates per batch row.
+// The reference gathers candidate K AND V of every union page from host
+// memory over PCIe, materializes repeat_kv(K) and runs a GEMM.  Here the cold
+// tier is HBM-resident: each candidate page tile (rows of one KV head) is
+// staged into shared memory by a 1-D TMA bulk copy (4-stage mbarrier
+// pipeline), scored against all G*Q rows of its KV head, and reduced to the
+// max over heads and positions in shared memory; V is never touched.  The
+// select runs on one thread-block cluster per batch row with the candidate
+// keys spread over the cluster's shared memory.
+#include <algorithm>
+
+#include "common.cuh"
+#include "internal.h"
+#include "select.cuh"
+
+namespace kiv {
+
+constexpr int FS_THREADS = 256;
+constexpr int FS_STAGES = 4;
+constexpr int FS_TILE_BYTES = 16384;
+constexpr int SL_THREADS = 512;
+constexpr int FM_THREADS = 512;
+
+struct FineGeom {
+  int64_t U, np_global, partial, per_b, items;
+  bool part_owned;
+};
+
+__device__ __forceinline__ FineGeom fine_geom(const kiv_store &st) {
+  FineGeom f;
+  const int S = st.page_size;
+  const int64_t cold = st_ld(st.state, KIV_ST_COLD_LEN);
+  f.U = st_ld(st.state, KIV_ST_UNION);
+  f.np_global = cold / S;
+  f.partial = cold % S;
+  f.part_owned = f.partial > 0 && (f.np_global % st.shard_count) == st.shard_rank;
+  f.per_b = f.U + (f.part_owned ? 1 : 0);
+  f.items = (int64_t)st.batch * f.per_b;
+  return f;
+}
+
+// global token id of local candidate position c
+__device__ __forceinline__ int32_t cand_token(const Workspace &w, const FineGeom &f, int S, int64_t c) {
+  const int64_t uS = f.U * S;
+  if (c < uS) return (int32_t)((int64_t)w.uni[c / S] * S + c % S);
+  return (int32_t)(f.np_global * S + (c - uS));
+}
+
+template <typename T, int LPR, int VPL, int RCH>
+__global__ void __launch_bounds__(FS_THREADS)
+fine_scores_kernel(kiv_store st, kiv_query q, Workspace w, int tr, int stage_q) {
+  griddep_wait();
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    st.state[KIV_ST_FINE_MAX] = 0;
+    st.state[KIV_ST_FINE_SUM] = 0;
+  }
+  extern __shared__ __align__(128) uint8_t fs_smem[];
+  __shared__ uint64_t bars[FS_STAGES];
+  __shared__ int s_fail;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane % LPR, grp = lane / LPR;
+  constexpr int GPW = 32 / LPR;
+  constexpr int NGROUPS = (FS_THREADS / 32) * GPW;
+  constexpr int V = Elem<T>::V;
+  const int D = st.head_dim, H = st.num_kv_heads, S = st.page_size;
+  const int nv = D / V;
+  const int Hq = q.num_query_heads, Q = q.query_len;
+  const int G = Hq / H;
+  const int rows_kv = G * Q;
+  const int nchunks = (rows_kv + RCH - 1) / RCH;
+  T *tiles = reinterpret_cast<T *>(fs_smem);
+  float *mx = reinterpret_cast<float *>(fs_smem + (size_t)FS_STAGES * tr * D * sizeof(T));
+  float *qs = mx + ((tr + 3) & ~3);   // [Hq*Q][D] fp32 query rows of the current batch row
+
+  const FineGeom f = fine_geom(st);
+  const int nrb = (S + tr - 1) / tr;
+  // work unit = (b, candidate page u, row block rb); its tiles are the H KV heads
+  const int64_t units = f.items * nrb;
+  const int64_t my_units = units > blockIdx.x ? (units - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+  const int64_t my_tiles = my_units * H;
+  const T *cold_k = reinterpret_cast<const T *>(st.cold_k);
+  const T *qb = reinterpret_cast<const T *>(q.q);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < FS_STAGES; ++s) mbar_init(&bars[s], 1);
+    mbar_fence_init();
+    s_fail = 0;
+  }
+  for (int i = threadIdx.x; i < tr; i += FS_THREADS) mx[i] = -INFINITY;
+  __syncthreads();
+
+  struct Unit { int b; int64_t u; int rb; int rows; };
+  auto unit_of = [&](int64_t t) {
+    Unit x;
+    const int64_t un = blockIdx.x + (t / H) * gridDim.x;
+    x.rb = (int)(un % nrb);
+    const int64_t item = un / nrb;
+    x.b = (int)(item / f.per_b);
+    x.u = item % f.per_b;
+    const int64_t limit = x.u < f.U ? S : f.partial;
+    x.rows = (int)std::max<int64_t>(0, std::min<int64_t>(tr, limit - (int64_t)x.rb * tr));
+    return x;
+  };
+  auto issue = [&](int64_t t) {
+    const int stage = (int)(t % FS_STAGES);
+    const Unit x = unit_of(t);
+    const int kvh = (int)(t % H);
+    const uint32_t bytes = (uint32_t)x.rows * D * sizeof(T);
+    if (bytes > 0) {
+      const int64_t page = x.u < f.U ? (int64_t)w.uni[x.u] : f.np_global;
+      const int64_t lp = page / st.shard_count;
+      const T *src = cold_k + (((int64_t)x.b * H + kvh) * st.cold_capacity + lp * S + (int64_t)x.rb * tr) * D;
+      mbar_arrive_tx(&bars[stage], bytes);
+      bulk_g2s(tiles + (size_t)stage * tr * D, src, bytes, &bars[stage]);
+    } else {
+      mbar_arrive(&bars[stage]);
+    }
+  };
+  if (threadIdx.x == 0) {
+    for (int64_t t = 0; t < std::min<int64_t>(FS_STAGES, my_tiles); ++t) issue(t);
+  }
+
+  int staged_b = -1;
+  for (int64_t t = 0; t < my_tiles; ++t) {
+    const Unit x = unit_of(t);
+    const int kvh = (int)(t % H);
+    if (stage_q && x.b != staged_b) {
+      // stage this batch row's query rows (fp32) once; reused by every tile
+      for (int e = threadIdx.x; e < Hq * Q * nv; e += FS_THREADS) {
+        const int rq = e / nv, vi = e % nv;
+        const int h = rq / Q, tq = rq % Q;
+        float fv[V];
+        Elem<T>::unpack(ld16(qb + x.b * q.stride_b + h * q.stride_h + tq * q.stride_t + vi * V), fv);
+#pragma unroll
+        for (int k = 0; k < V; ++k) qs[(size_t)rq * D + vi * V + k] = fv[k];
+      }
+      staged_b = x.b;
+    }
+    const int stage = (int)(t % FS_STAGES);
+    const uint32_t parity = (uint32_t)((t / FS_STAGES) & 1);
+    if (!mbar_wait_bounded(&bars[stage], parity)) s_fail = 1;
+    __syncthreads();
+    if (s_fail) break;
+    const T *tile = tiles + (size_t)stage * tr * D;
+    for (int ch = 0; ch < nchunks; ++ch) {
+      RowDot<T, LPR, VPL, RCH> dot;
+      if (stage_q) {
+        const float *qrows[RCH];
+#pragma unroll
+        for (int r = 0; r < RCH; ++r) {
+          const int rr = ch * RCH + r;
+          // query row (h, tq) with h = kvh*G + rr/Q is staged at index h*Q + tq
+          qrows[r] = rr < rows_kv ? qs + (size_t)((kvh * G + rr / Q) * Q + rr % Q) * D : nullptr;
+        }
+        dot.load_query_f32(qrows, g, nv);
+      } else {
+        const T *qrows[RCH];
+#pragma unroll
+        for (int r = 0; r < RCH; ++r) {
+          const int rr = ch * RCH + r;
+          qrows[r] = rr < rows_kv ? qb + x.b * q.stride_b + (kvh * G + rr / Q) * q.stride_h +
+                                        (rr % Q) * q.stride_t
+                                  : nullptr;
+        }
+        dot.load_query(qrows, g, nv, 1.0f);
+      }
+      const int my_group = warp * GPW + grp;
+      for (int r0 = 0; r0 < x.rows; r0 += NGROUPS) {
+        const int r = r0 + my_group;
+        float acc[RCH];
+        dot.template partial<false>(r < x.rows ? tile + (size_t)r * D : nullptr, g, nv, acc);
+        int base = 0;
+        tr_reduce<RCH, LPR / 2>(acc, lane, base);
+        constexpr int NOUT = TrOut<RCH, LPR>::N;
+        float m = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < NOUT; ++i) {
+          const int rr = ch * RCH + base + i;
+          if (rr < rows_kv) m = fmaxf(m, acc[i] * q.scaling);
+        }
+        m = group_max<LPR / 2>(m);
+        if (r < x.rows && g == 0) mx[r] = fmaxf(mx[r], m);
+      }
+    }
+    __syncthreads();  // stage consumed, mx updated
+    if (threadIdx.x == 0 && t + FS_STAGES < my_tiles) issue(t + FS_STAGES);
+    if (kvh == H - 1) {
+      // unit complete: publish its keys, reset the running max
+      uint32_t *dst = w.agg + (int64_t)x.b * w.c_cap + x.u * S + (int64_t)x.rb * tr;
+      for (int i = threadIdx.x; i < tr; i += FS_THREADS) {
+        if (i < x.rows) dst[i] = f2key(mx[i]);
+        mx[i] = -INFINITY;
+      }
+      __syncthreads();
+    }
+  }
+  if (s_fail && threadIdx.x == 0)
+    atomicOr(reinterpret_cast<unsigned long long *>(st.state + KIV_ST_ERROR), (unsigned long long)KIV_ERRBIT_WAIT_TIMEOUT);
+}
+
+// One cluster of CL CTAs per batch row: exact top-P over the C candidates.
+// shard_count == 1: sel[b, :P] = selected token ids (ascending).
+// shard_count > 1: sel / scores hold this shard's local list (tail -1).
+template <int CL>
+__global__ void __launch_bounds__(SL_THREADS)
+fine_select_kernel(kiv_store st, kiv_query q, Workspace w, int32_t *sel, float *scores,
+                   int chunk_cap) {
+  griddep_wait();
+  extern __shared__ uint4 sl_dyn[];
+  __shared__ SelectSmem<SL_THREADS> sm;
+  const int b = blockIdx.x / CL;
+  const int r = cl_rank<CL>();
+  const int S = st.page_size;
+  const FineGeom f = fine_geom(st);
+  const int64_t C = f.U * S + (f.part_owned ? f.partial : 0);
+  const int64_t chunk = (C + CL - 1) / CL;
+  const int64_t lo = std::min<int64_t>(C, r * chunk);
+  const int n_local = (int)(std::min<int64_t>(C, lo + chunk) - lo);
+  const uint32_t *src = w.agg + (int64_t)b * w.c_cap + lo;
+  const uint32_t *keys = src;
+  if (chunk <= chunk_cap) {
+    uint32_t *sk = reinterpret_cast<uint32_t *>(sl_dyn);
+    for (int i = threadIdx.x; i < n_local; i += SL_THREADS) sk[i] = src[i];
+    keys = sk;
+    __syncthreads();
+  }
+  block_stats<SL_THREADS>(keys, n_local, st.state + KIV_ST_FINE_MAX, st.state + KIV_ST_FINE_SUM);
+  const int64_t P = std::min<int64_t>(q.top_p, C);
+  const bool all = P >= C;
+  uint32_t T = 0, need = 0;
+  if (P > 0 && !all) radix_threshold<SL_THREADS, CL>(keys, n_local, (uint32_t)P, sm, T, need);
+  int32_t *out = sel + (int64_t)b * q.top_p;
+  float *osc = scores ? scores + (int64_t)b * q.top_p : nullptr;
+  if (P > 0) {
+    ordered_emit<SL_THREADS, CL>(keys, n_local, T, need, all, sm, [&](int i, uint32_t pos) {
+      out[pos] = cand_token(w, f, S, lo + i);
+      if (osc) osc[pos] = key2f(keys[i]);
+    });
+  }
+  if (r == 0) {
+    if (st.shard_count > 1) {
+      for (int64_t j = P + threadIdx.x; j < q.top_p; j += SL_THREADS) {
+        out[j] = -1;
+        if (osc) osc[j] = 0.f;
+      }
+    }
+    if (threadIdx.x == 0) {
+      w.selcnt[b] = (int32_t)P;
+      if (b == 0) {
+        st.state[KIV_ST_CAND] = C;
+        st.state[KIV_ST_SEL] = P;
+        st.state[KIV_ST_SEL_LOCAL] = P;
+      }
+    }
+  }
+}
+
+// lower_bound over the first n entries of an ascending id list
+__device__ __forceinline__ int lower_bound_ids(const int32_t *ids, int n, int32_t x) {
+  int lo = 0, hi = n;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (ids[mid] < x) lo = mid + 1;
+    else hi = mid;
+  }
+  return lo;
+}
+
+// per-list exclusive prefix of flags: pre[j*(L+1) + a] = #flags in list j before a
+__device__ void list_prefix(const uint8_t *flag, int n, int L, int32_t *pre) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int j = warp; j < n; j += nw) {
+    const int per = (L + 31) / 32;
+    const int a0 = min(L, lane * per), a1 = min(L, a0 + per);
+    int c = 0;
+    for (int a = a0; a < a1; ++a) c += flag[j * L + a];
+    int incl = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(KIV_FULL_MASK, incl, o);
+      if (lane >= o) incl += y;
+    }
+    int run = incl - c;
+    for (int a = a0; a < a1; ++a) {
+      pre[j * (L + 1) + a] = run;
+      run += flag[j * L + a];
+    }
+    if (lane == 31) pre[j * (L + 1) + L] = incl;
+  }
+}
+
+// Merge n gathered lists [n][B][top_p] (ascending ids, tail -1) into the
+// global top-P of each batch row; sel gets all of them (ascending ids),
+// sel_local the ones this shard owns (list index == shard rank).
+__global__ void __launch_bounds__(FM_THREADS)
+fine_merge_kernel(kiv_store st, kiv_query q, Workspace w, const float *ls, const int32_t *lt,
+                  int32_t n, int32_t *sel, int32_t *sel_local) {
+  griddep_wait();
+  extern __shared__ uint4 fm_dyn[];
+  __shared__ SelectSmem<FM_THREADS> sm;
+  __shared__ int s_valid[64];
+  const int b = blockIdx.x;
+  const int L = q.top_p, B = st.batch;
+  const int m = n * L;
+  uint32_t *keys = reinterpret_cast<uint32_t *>(fm_dyn);
+  int32_t *ids = reinterpret_cast<int32_t *>(keys + m);
+  int32_t *pre_eq = ids + m;
+  int32_t *pre_sel = pre_eq + n * (L + 1);
+  uint8_t *fl = reinterpret_cast<uint8_t *>(pre_sel + n * (L + 1));
+  for (int i = threadIdx.x; i < m; i += FM_THREADS) {
+    const int j = i / L, a = i % L;
+    const int64_t off = ((int64_t)j * B + b) * L + a;
+    ids[i] = lt[off];
+    keys[i] = lt[off] >= 0 ? f2key(ls[off]) : 0u;
+  }
+  if (threadIdx.x < 64) s_valid[threadIdx.x] = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < m; i += FM_THREADS)
+    if (ids[i] >= 0) atomicAdd(&s_valid[i / L], 1);
+  __syncthreads();
+  int valid = 0;
+  for (int j = 0; j < n; ++j) valid += s_valid[j];
+  const int P = min(L, valid);
+  uint32_t T = 0, need = 0;
+  const bool all = P >= valid;
+  if (P > 0 && !all) radix_threshold<FM_THREADS, 1>(keys, m, (uint32_t)P, sm, T, need);
+  // ties at T: rank among equal keys by token id across all lists
+  for (int i = threadIdx.x; i < m; i += FM_THREADS)
+    fl[i] = (ids[i] >= 0 && !all && keys[i] == T) ? 1 : 0;
+  __syncthreads();
+  list_prefix(fl, n, L, pre_eq);
+  __syncthreads();
+  uint8_t *take = fl + m;
+  for (int i = threadIdx.x; i < m; i += FM_THREADS) {
+    const int j = i / L, a = i % L;
+    bool s = ids[i] >= 0 && (all || keys[i] > T);
+    if (!s && fl[i]) {
+      int rank = pre_eq[j * (L + 1) + a];
+      for (int o = 0; o < n; ++o)
+        if (o != j) rank += pre_eq[o * (L + 1) + lower_bound_ids(ids + o * L, s_valid[o], ids[i])];
+      s = rank < (int)need;
+    }
+    take[i] = s ? 1 : 0;
+  }
+  __syncthreads();
+  list_prefix(take, n, L, pre_sel);
+  __syncthreads();
+  for (int i = threadIdx.x; i < m; i += FM_THREADS) {
+    if (!take[i]) continue;
+    const int j = i / L, a = i % L;
+    int pos = pre_sel[j * (L + 1) + a];
+    for (int o = 0; o < n; ++o)
+      if (o != j) pos += pre_sel[o * (L + 1) + lower_bound_ids(ids + o * L, s_valid[o], ids[i])];
+    sel[(int64_t)b * L + pos] = ids[i];
+    if (j == st.shard_rank) sel_local[(int64_t)b * L + pre_sel[j * (L + 1) + a]] = ids[i];
+  }
+  if (threadIdx.x == 0) {
+    w.selcnt[b] = pre_sel[st.shard_rank * (L + 1) + L];
+    if (b == 0) {
+      st.state[KIV_ST_SEL] = P;
+      st.state[KIV_ST_SEL_LOCAL] = pre_sel[st.shard_rank * (L + 1) + L];
+    }
+  }
+}
+
+template <typename T, int LPR, int VPL, int RCH>
+static kiv_status launch_fs(const kiv_store *st, const kiv_query *q, const Workspace &w,
+                            cudaStream_t s) {
+  const int D = st->head_dim, S = st->page_size;
+  int tr = 1;
+  while (tr * 2 <= S && (int64_t)tr * 2 * D * (int)sizeof(T) <= FS_TILE_BYTES) tr *= 2;
+  const size_t qbytes = (size_t)q->num_query_heads * q->query_len * D * sizeof(float);
+  const int stage_q = qbytes <= 64 * 1024 ? 1 : 0;
+  const size_t smem = (size_t)FS_STAGES * tr * D * sizeof(T) + (size_t)((tr + 3) & ~3) * sizeof(float) +
+                      (stage_q ? qbytes : 0);
+  auto kern = fine_scores_kernel<T, LPR, VPL, RCH>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  int per_sm = 1;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, FS_THREADS, smem);
+  per_sm = std::max(per_sm, 1);
+  const int64_t units_cap = (int64_t)st->batch * (w.u_cap + 1) * ceil_div(S, tr);
+  const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(units_cap, (int64_t)sm_count() * per_sm));
+  kern<<<(unsigned)grid, FS_THREADS, smem, s>>>(*st, *q, w, tr, stage_q);
+  return cuda_status(cudaGetLastError(), "fine_scores");
+}
+
+template <typename T>
+static kiv_status dispatch_fs(const kiv_store *st, const kiv_query *q, const Workspace &w,
+                              cudaStream_t s) {
+  const int nv = st->head_dim / Elem<T>::V;
+  const int rows_kv = (q->num_query_heads / st->num_kv_heads) * q->query_len;
+  const bool small = rows_kv <= 4;
+#define KIV_FS(LPR, VPL) \
+  return small ? launch_fs<T, LPR, VPL, 4>(st, q, w, s) : launch_fs<T, LPR, VPL, 8>(st, q, w, s)
+  if (nv <= 2) KIV_FS(2, 1);
+  if (nv <= 4) KIV_FS(4, 1);
+  if (nv <= 8) KIV_FS(8, 1);
+  if (nv <= 16) KIV_FS(16, 1);
+  if (nv <= 32) KIV_FS(32, 1);
+  if (nv <= 64) KIV_FS(32, 2);
+#undef KIV_FS
+  return KIV_ERR_UNSUPPORTED;
+}
+
+kiv_status launch_fine_score(const kiv_store *st, const kiv_query *q, const Workspace &w, cudaStream_t s) {
+  switch (st->dtype) {
+    case KIV_DTYPE_F32: return dispatch_fs<float>(st, q, w, s);
+    case KIV_DTYPE_BF16: return dispatch_fs<__nv_bfloat16>(st, q, w, s);
+    case KIV_DTYPE_F16: return dispatch_fs<__half>(st, q, w, s);
+  }
+  return KIV_ERR_UNSUPPORTED;
+}
+
+kiv_status launch_fine(const kiv_store *st, const kiv_query *q, const Workspace &w, int32_t *sel,
+                       float *sel_scores, cudaStream_t s) {
+  const kiv_status rc = launch_fine_score(st, q, w, s);
+  if (rc != KIV_OK) return rc;
+  return launch_fine_topk(st, q, w, sel, sel_scores, s);
+}
+
+kiv_status launch_fine_topk(const kiv_store *st, const kiv_query *q, const Workspace &w, int32_t *sel,
+                            float *sel_scores, cudaStream_t s) {
+  // select: one cluster of SEL_CLUSTER CTAs per batch row
+  const int64_t chunk = ceil_div(w.c_cap, SEL_CLUSTER);
+  const int64_t limit = (200 * 1024 - (int64_t)sizeof(SelectSmem<SL_THREADS>)) / 4;
+  const int chunk_cap = (int)std::min<int64_t>(chunk, limit);
+  const size_t smem = (size_t)chunk_cap * sizeof(uint32_t);
+  auto kern = fine_select_kernel<SEL_CLUSTER>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(st->batch * SEL_CLUSTER));
+  cfg.blockDim = dim3(SL_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = SEL_CLUSTER;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, *st, *q, w, sel, sel_scores, chunk_cap);
+  return cuda_status(e, "fine_select");
+}
+
+kiv_status launch_fine_merge(const kiv_store *st, const kiv_query *q, const Workspace &w,
+                             const float *ls, const int32_t *lt, int32_t n, int32_t *sel,
+                             int32_t *sel_local, cudaStream_t s) {
+  const int64_t m = (int64_t)n * q->top_p;
+  const size_t smem = (size_t)m * 8 + (size_t)n * (q->top_p + 1) * 8 + (size_t)m * 2 + 16;
+  if (smem > 200 * 1024 || n > 64) {
+    set_error("fine_merge: %d lists of %d entries exceed the shared-memory merge", n, q->top_p);
+    return KIV_ERR_CAPACITY;
+  }
+  cudaFuncSetAttribute(fine_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  fine_merge_kernel<<<(unsigned)st->batch, FM_THREADS, smem, s>>>(*st, *q, w, ls, lt, n, sel, sel_local);
+  return cuda_status(cudaGetLastError(), "fine_merge");
+}
+
+}  // namespace kiv

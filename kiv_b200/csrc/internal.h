@@ -1,0 +1,82 @@
+// Host-side internals shared by the KIV translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/kiv_b200.h"
+
+namespace kiv {
+
+// kernel-private counters inside the device state block
+enum : int {
+  CTR_EVICT = 16,
+  CTR_COARSE = 17,
+  CTR_MERGE = 18,
+  CTR_FINE = 19,
+  CTR_SEL = 20,
+};
+
+constexpr int ATT_TILE = 32;     // keys per attention tile
+constexpr int ROW_CHUNK = 8;     // query rows per register chunk
+constexpr int SEL_CLUSTER = 8;   // CTAs per cluster in the fine top-P select
+
+// Scratch carved out of the caller's workspace for one store / query shape.
+struct Workspace {
+  float *scores;       // [R, np_cap]        coarse scores
+  uint8_t *flags;      // [np_cap]           page marks for the union
+  int32_t *uni;        // [u_cap]            union pages (global ids, ascending)
+  uint32_t *agg;       // [B, c_cap]         fine keys (monotone u32 of the max score)
+  int32_t *selcnt;     // [B]                selected tokens of this shard per batch row
+  float *part;         // [R, split_cap, D+2] attention split partials
+  int64_t R, K, np_cap, u_cap, c_cap, split_cap;
+  size_t bytes;
+};
+
+Workspace workspace_layout(const kiv_store *st, const kiv_query *q, void *base);
+
+int sm_count();
+void set_error(const char *fmt, ...);
+kiv_status cuda_status(cudaError_t e, const char *where);
+
+// launchers (one per kernel family); all stream-ordered, no host sync
+kiv_status launch_append_evict(const kiv_store *st, const void *k_new, const void *v_new,
+                               int64_t sb, int64_t sh, int64_t stt, int32_t n_new, int64_t keep,
+                               int64_t n_evict_max, cudaStream_t s);
+kiv_status launch_coarse(const kiv_store *st, const kiv_query *q, const Workspace &w,
+                         float *row_scores, int32_t *row_pages, cudaStream_t s);
+kiv_status launch_coarse_merge(const kiv_store *st, const kiv_query *q, const Workspace &w,
+                               const float *ls, const int32_t *lp, int32_t n, cudaStream_t s);
+kiv_status launch_fine(const kiv_store *st, const kiv_query *q, const Workspace &w, int32_t *sel,
+                       float *sel_scores, cudaStream_t s);
+kiv_status launch_fine_score(const kiv_store *st, const kiv_query *q, const Workspace &w, cudaStream_t s);
+kiv_status launch_fine_topk(const kiv_store *st, const kiv_query *q, const Workspace &w, int32_t *sel,
+                            float *sel_scores, cudaStream_t s);
+kiv_status launch_fine_merge(const kiv_store *st, const kiv_query *q, const Workspace &w,
+                             const float *ls, const int32_t *lt, int32_t n, int32_t *sel,
+                             int32_t *sel_local, cudaStream_t s);
+kiv_status launch_gather(const kiv_store *st, const int32_t *sel, int32_t sel_stride, int32_t P,
+                         void *ok, void *ov, cudaStream_t s);
+kiv_status launch_attend(const kiv_store *st, const kiv_query *q, const kiv_mask *m,
+                         const Workspace &w, const int32_t *sel, int32_t sel_stride,
+                         int32_t hot_slice, int32_t hot_slices, void *out, float *partial_out,
+                         cudaStream_t s);
+kiv_status launch_attend_merge(const kiv_store *st, const kiv_query *q, const float *partials,
+                               int32_t n, void *out, cudaStream_t s);
+
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// floats per attention partial row: out[D], max, sum, 16-byte aligned
+__host__ __device__ inline int partial_stride(int D) { return (D + 2 + 3) & ~3; }
+inline int64_t align_up(int64_t a, int64_t b) { return ceil_div(a, b) * b; }
+
+inline int elem_bytes(int dtype) { return dtype == KIV_DTYPE_F32 ? 4 : 2; }
+
+// number of attention splits per (b, kvh, row chunk) for this shape
+inline int64_t attn_split_cap(const kiv_store *st, const kiv_query *q) {
+  const int64_t keys = (int64_t)q->top_p + st->hot_capacity;
+  return ceil_div(keys > 0 ? keys : 1, ATT_TILE);
+}
+
+}  // namespace kiv

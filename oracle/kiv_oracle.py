@@ -74,7 +74,13 @@ def topk_total_order(scores: np.ndarray, k: int) -> np.ndarray:
     """
     n = scores.shape[0]
     k = min(k, n)
-    order = np.lexsort((np.arange(n), -scores.astype(np.float64)))
+    s = scores.astype(np.float64, copy=False)
+    if k < n:
+        part = np.argpartition(-s, k - 1)[:k]
+        cand = np.nonzero(s >= s[part].min())[0]     # every key tied with the k-th
+    else:
+        cand = np.arange(n)
+    order = cand[np.lexsort((cand, -s[cand]))]
     return order[:k]
 
 
@@ -130,23 +136,51 @@ class OracleStore:
     groups: int
     page_size: int
     storage: str = "f32"
-    k: np.ndarray = field(init=False)
-    v: np.ndarray = field(init=False)
-    summaries: np.ndarray = field(init=False)
+    compute: type = np.float64          # score arithmetic (float64: parity; float32: timing)
     cached_step: int = field(default=-1, init=False)
     cached_union: np.ndarray | None = field(default=None, init=False)
     cached_batch: int = field(default=-1, init=False)
 
     def __post_init__(self):
-        shape = (self.batch, self.num_kv_heads, 0, self.head_dim)
-        self.k = np.zeros(shape, np.float32)
-        self.v = np.zeros(shape, np.float32)
-        self.summaries = np.zeros(shape, np.float32)
+        shape = (self.batch, self.num_kv_heads, 16, self.head_dim)
+        self._k = np.zeros(shape, np.float32)
+        self._v = np.zeros(shape, np.float32)
+        self._s = np.zeros(shape, np.float32)
+        self._n = 0
+
+    # token-indexed views (storage grows by doubling: appends are amortized O(1))
+    @property
+    def k(self) -> np.ndarray:
+        return self._k[:, :, :self._n]
+
+    @property
+    def v(self) -> np.ndarray:
+        return self._v[:, :, :self._n]
+
+    @property
+    def summaries(self) -> np.ndarray:
+        return self._s[:, :, :self.num_pages]
+
+    def _grow(self, need: int) -> None:
+        cap = self._k.shape[2]
+        if need <= cap:
+            return
+        cap = max(need, 2 * cap)
+        for name in ("_k", "_v"):
+            old = getattr(self, name)
+            new = np.zeros(old.shape[:2] + (cap,) + old.shape[3:], np.float32)
+            new[:, :, :self._n] = old[:, :, :self._n]
+            setattr(self, name, new)
+        pages = cap // self.page_size + 1
+        if pages > self._s.shape[2]:
+            new = np.zeros(self._s.shape[:2] + (pages,) + self._s.shape[3:], np.float32)
+            new[:, :, :self.num_pages] = self._s[:, :, :self.num_pages]
+            self._s = new
 
     # -- sizes (kiv/cold_store.py:111-120) --
     @property
     def cold_length(self) -> int:
-        return self.k.shape[2]
+        return self._n
 
     @property
     def num_pages(self) -> int:
@@ -165,23 +199,27 @@ class OracleStore:
         """kiv/cold_store.py:142-184: append rows; every page that fills gets a summary."""
         self.invalidate()
         before = self.num_pages
-        self.k = np.concatenate([self.k, to_storage(k_ev, self.storage)], axis=2)
-        self.v = np.concatenate([self.v, to_storage(v_ev, self.storage)], axis=2)
+        n = k_ev.shape[2]
+        self._grow(self._n + n)
+        self._k[:, :, self._n:self._n + n] = to_storage(k_ev, self.storage)
+        self._v[:, :, self._n:self._n + n] = to_storage(v_ev, self.storage)
+        self._n += n
         S = self.page_size
-        new = [page_summary(self.k[:, :, p * S:(p + 1) * S, :], self.storage)[:, :, None, :]
-               for p in range(before, self.num_pages)]
-        if new:
-            self.summaries = np.concatenate([self.summaries] + new, axis=2)
+        done = self.num_pages
+        if done > before:
+            B, H, D = self.batch, self.num_kv_heads, self.head_dim
+            pages = self._k[:, :, before * S:done * S].reshape(B, H, done - before, S, D)
+            self._s[:, :, before:done] = page_summary(pages, self.storage)
 
     # -- coarse stage (kiv/cold_store.py:203-230) --
     def coarse(self, query: np.ndarray, scaling: float, top_pages: int):
         B, Hq, Q, D = query.shape
         Np = self.num_pages
-        q = to_storage(query, self.storage).astype(np.float64)
-        summ = self.summaries.astype(np.float64)                       # [B, Hkv, Np, D]
+        q = to_storage(query, self.storage).astype(self.compute)
+        summ = self.summaries.astype(self.compute)                      # [B, Hkv, Np, D]
         G = Hq // self.num_kv_heads
         rows = _group_rows(q, self.num_kv_heads)                        # [B, Hkv, GQ, D]
-        sc = np.einsum("bhrd,bhpd->bhrp", rows, summ) * float(scaling)  # [B, Hkv, GQ, Np]
+        sc = np.matmul(rows, summ.transpose(0, 1, 3, 2)) * self.compute(scaling)  # [B, Hkv, GQ, Np]
         sc = sc.reshape(B, self.num_kv_heads, G, Q, Np).reshape(B, Hq, Q, Np)
         k = min(top_pages, Np)
         top = np.zeros((B, Hq, Q, k), np.int64)
@@ -202,11 +240,11 @@ class OracleStore:
     def fine(self, query: np.ndarray, scaling: float, cand_idx: np.ndarray, top_p: int):
         """kiv/cold_store.py:301, :332-347: fine scores, max over heads/positions, top-P."""
         B, Hq, Q, D = query.shape
-        q = to_storage(query, self.storage).astype(np.float64)
-        kc = self.k[:, :, cand_idx, :].astype(np.float64)                # [B, Hkv, C, D]
+        q = to_storage(query, self.storage).astype(self.compute)
+        kc = self._k[:, :, cand_idx, :].astype(self.compute, copy=False)  # [B, Hkv, C, D]
         rows = _group_rows(q, self.num_kv_heads)
-        sc = np.einsum("bhrd,bhcd->bhrc", rows, kc) * float(scaling)     # [B, Hkv, GQ, C]
-        agg = sc.max(axis=(1, 2))                                       # [B, C]
+        sc = np.matmul(rows, kc.transpose(0, 1, 3, 2)) * self.compute(scaling)  # [B, Hkv, GQ, C]
+        agg = sc.max(axis=(1, 2)).astype(np.float64)                    # [B, C]
         P = min(top_p, self.cold_length, cand_idx.shape[0])
         sel = np.zeros((B, P), np.int64)
         for b in range(B):
@@ -217,8 +255,8 @@ class OracleStore:
     def gather(self, sel: np.ndarray):
         """kiv/cold_store.py:358-362: K and V rows of the selected tokens, per batch row."""
         B = sel.shape[0]
-        k = np.stack([self.k[b][:, sel[b], :] for b in range(B)])
-        v = np.stack([self.v[b][:, sel[b], :] for b in range(B)])
+        k = np.stack([self._k[b][:, sel[b], :] for b in range(B)])
+        v = np.stack([self._v[b][:, sel[b], :] for b in range(B)])
         return k, v
 
     def retrieve_top_kv(self, query: np.ndarray, scaling: float, top_pages: int,
@@ -280,7 +318,7 @@ def eager_attention(query, k_cold, v_cold, k_hot, v_hot, scaling, hot_mask=None,
     G = Hq // hkv
     K = np.repeat(K, G, axis=1)
     V = np.repeat(V, G, axis=1)
-    s = np.einsum("bhqd,bhkd->bhqk", q, K) * float(scaling)
+    s = np.matmul(q, K.transpose(0, 1, 3, 2)) * float(scaling)
     if softcap is not None:
         s = np.tanh(s / softcap) * softcap
     n_cold = 0 if k_cold is None else k_cold.shape[2]
@@ -289,7 +327,7 @@ def eager_attention(query, k_cold, v_cold, k_hot, v_hot, scaling, hot_mask=None,
     m = s.max(axis=-1, keepdims=True)
     p = np.exp(s - m)
     p /= p.sum(axis=-1, keepdims=True)
-    o = np.einsum("bhqk,bhkd->bhqd", p, V)
+    o = np.matmul(p, V)
     return o.transpose(0, 2, 1, 3)
 
 
