@@ -231,6 +231,22 @@ KIV_API kiv_status kiv_retrieve_attend(const kiv_store *st, const kiv_query *q, 
                                void *ws, size_t ws_bytes, int32_t reuse, int32_t *sel,
                                void *out, void *stream);
 
+/*
+ * kiv_retrieve_attend without a workspace argument: the scratch comes from a
+ * fixed device array inside the library (KIV_NOALLOC_SCRATCH_BYTES per GPU,
+ * held until the process exits), so the call allocates nothing.  For callers
+ * that may not allocate device memory while they serve (engines that own all
+ * memory through their own pool, plugin hosts without an allocator hook).
+ * Shapes needing more scratch are rejected with KIV_ERR_CAPACITY.  All calls
+ * on a device share the array: calls that overlap on the GPU race.  The first
+ * call on a device looks up the array's address; make it before any stream
+ * capture.  No counterpart in the reference (it has no C interface).
+ */
+#define KIV_NOALLOC_SCRATCH_BYTES (32u << 20)
+KIV_API kiv_status kiv_retrieve_attend_noalloc(const kiv_store *st, const kiv_query *q,
+                                               const kiv_mask *mask, int32_t *sel, void *out,
+                                               void *stream);
+
 /* Copy the store's device state words to host memory (synchronizes the stream). */
 KIV_API kiv_status kiv_read_state(const kiv_store *st, int64_t *host_words, void *stream);
 

@@ -74,6 +74,7 @@ SIGNATURES = {
     "kiv_attend_merge": (c_i32, [P(StoreDesc), P(QueryDesc), c_vp, c_i32, c_vp, c_vp]),
     "kiv_retrieve_attend": (c_i32, [P(StoreDesc), P(QueryDesc), P(MaskDesc), c_vp, c_sz, c_i32, c_vp,
                                     c_vp, c_vp]),
+    "kiv_retrieve_attend_noalloc": (c_i32, [P(StoreDesc), P(QueryDesc), P(MaskDesc), c_vp, c_vp, c_vp]),
     "kiv_read_state": (c_i32, [P(StoreDesc), P(c_i64), c_vp]),
 }
 
