@@ -56,6 +56,8 @@ WORKLOADS = {
     "c2": dict(layers=35, hq=8, hkv=1, d=256, cold=1048576, hot=2048, top_pages=64, top_p=1024),
     "c1": dict(layers=28, hq=28, hkv=4, d=128, cold=131072, hot=2048, top_pages=32, top_p=512),
     "tiny": dict(layers=3, hq=8, hkv=1, d=256, cold=65536, hot=2048, top_pages=64, top_p=1024),
+    # c2 per-layer shapes at full size, 3 layers (a few GB: small enough for ncu captures)
+    "c2s": dict(layers=3, hq=8, hkv=1, d=256, cold=1048576, hot=2048, top_pages=64, top_p=1024),
 }
 PAGE = 128
 SEGMENT = 512

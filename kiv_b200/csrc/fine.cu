@@ -126,6 +126,23 @@ fine_scores_kernel(kiv_store st, kiv_query q, Workspace w, int tr, int stage_q) 
   }
 
   int staged_b = -1;
+  // running stats of the batch row being processed (flushed when it changes)
+  int stat_b = -1;
+  uint32_t kmax = 0;
+  float ksum = 0.f;
+  auto flush_stats = [&]() {
+    if (stat_b < 0) return;
+    uint32_t mk = __reduce_max_sync(KIV_FULL_MASK, kmax);
+    float sm = ksum;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sm += __shfl_xor_sync(KIV_FULL_MASK, sm, o);
+    if (lane == 0 && mk != 0) {
+      atomicMax(reinterpret_cast<unsigned long long *>(&w.fstat[2 * stat_b]), (unsigned long long)mk);
+      atomicAdd(reinterpret_cast<double *>(&w.fstat[2 * stat_b + 1]), (double)sm);
+    }
+    kmax = 0;
+    ksum = 0.f;
+  };
   for (int64_t t = 0; t < my_tiles; ++t) {
     const Unit x = unit_of(t);
     const int kvh = (int)(t % H);
@@ -190,15 +207,27 @@ fine_scores_kernel(kiv_store st, kiv_query q, Workspace w, int tr, int stage_q) 
     __syncthreads();  // stage consumed, mx updated
     if (threadIdx.x == 0 && t + FS_STAGES < my_tiles) issue(t + FS_STAGES);
     if (kvh == H - 1) {
-      // unit complete: publish its keys, reset the running max
+      // unit complete: publish its keys (+ first-pass histogram, stats), reset the running max
+      if (x.b != stat_b) {
+        flush_stats();
+        stat_b = x.b;
+      }
       uint32_t *dst = w.agg + (int64_t)x.b * w.c_cap + x.u * S + (int64_t)x.rb * tr;
+      uint32_t *hb = w.fhist + (int64_t)x.b * SEL_BINS;
       for (int i = threadIdx.x; i < tr; i += FS_THREADS) {
-        if (i < x.rows) dst[i] = f2key(mx[i]);
+        if (i < x.rows) {
+          const uint32_t key = f2key(mx[i]);
+          dst[i] = key;
+          hist_add(hb, key >> 21);
+          kmax = key > kmax ? key : kmax;
+          ksum += mx[i];
+        }
         mx[i] = -INFINITY;
       }
       __syncthreads();
     }
   }
+  flush_stats();
   if (s_fail && threadIdx.x == 0)
     atomicOr(reinterpret_cast<unsigned long long *>(st.state + KIV_ST_ERROR), (unsigned long long)KIV_ERRBIT_WAIT_TIMEOUT);
 }
@@ -229,11 +258,11 @@ fine_select_kernel(kiv_store st, kiv_query q, Workspace w, int32_t *sel, float *
     keys = sk;
     __syncthreads();
   }
-  block_stats<SL_THREADS>(keys, n_local, st.state + KIV_ST_FINE_MAX, st.state + KIV_ST_FINE_SUM);
   const int64_t P = std::min<int64_t>(q.top_p, C);
   const bool all = P >= C;
   uint32_t T = 0, need = 0;
-  if (P > 0 && !all) radix_threshold<SL_THREADS, CL>(keys, n_local, (uint32_t)P, sm, T, need);
+  uint32_t *hb = w.fhist + (int64_t)b * SEL_BINS;
+  if (P > 0 && !all) radix_threshold<SL_THREADS, CL>(keys, n_local, (uint32_t)P, sm, T, need, hb);
   int32_t *out = sel + (int64_t)b * q.top_p;
   float *osc = scores ? scores + (int64_t)b * q.top_p : nullptr;
   if (P > 0) {
@@ -242,7 +271,18 @@ fine_select_kernel(kiv_store st, kiv_query q, Workspace w, int32_t *sel, float *
       if (osc) osc[pos] = key2f(keys[i]);
     });
   }
+  // every CTA of the cluster is past its reads of the shared histogram
+  cl_sync<CL>();
   if (r == 0) {
+    for (int i = threadIdx.x; i < SEL_BINS; i += SL_THREADS) hb[i] = 0;
+    if (threadIdx.x == 0) {
+      const unsigned long long mk = w.fstat[2 * b];
+      const unsigned long long sb = w.fstat[2 * b + 1];
+      if (mk) atomicMax(reinterpret_cast<unsigned long long *>(st.state + KIV_ST_FINE_MAX), mk);
+      atomicAdd(reinterpret_cast<double *>(st.state + KIV_ST_FINE_SUM), __longlong_as_double((long long)sb));
+      w.fstat[2 * b] = 0;
+      w.fstat[2 * b + 1] = 0;
+    }
     if (st.shard_count > 1) {
       for (int64_t j = P + threadIdx.x; j < q.top_p; j += SL_THREADS) {
         out[j] = -1;
@@ -408,6 +448,7 @@ static kiv_status dispatch_fs(const kiv_store *st, const kiv_query *q, const Wor
 }
 
 kiv_status launch_fine_score(const kiv_store *st, const kiv_query *q, const Workspace &w, cudaStream_t s) {
+  if (fine_tc_eligible(st, q)) return launch_fine_score_tc(st, q, w, s);
   switch (st->dtype) {
     case KIV_DTYPE_F32: return dispatch_fs<float>(st, q, w, s);
     case KIV_DTYPE_BF16: return dispatch_fs<__nv_bfloat16>(st, q, w, s);

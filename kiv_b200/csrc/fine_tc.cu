@@ -1,0 +1,296 @@
+// Kernel (c), tensor-core form: fine token scoring on tcgen05.
+//
+// Same result as fine_scores_kernel (fine.cu): for every candidate token of
+// the union pages (and the partial page), key = f2key(max over the G*Q query
+// rows of every KV head of scaling * <q, k>) -- restating kiv/cold_store.py:
+// 332-338.  Here one candidate page (128 tokens) of one KV head is one MMA
+// tile: M = 128 tokens, N = 16 or 32 query rows (zero-padded), K = head_dim.
+//
+//  warp 4 (one thread): TMA producer -- 2-D tensor-map loads (SWIZZLE_128B,
+//          boxes of 64 elements x 128 rows) of the K tile into a 3/4-stage
+//          shared-memory ring, completing on per-stage mbarriers;
+//  warp 5 (one thread): MMA issuer -- head_dim/16 tcgen05.mma per tile into
+//          one of two TMEM accumulators, tcgen05.commit to free the stage and
+//          to publish the accumulator;
+//  warps 0-3: epilogue -- tcgen05.ld of the accumulator (thread i = token i),
+//          max over the valid query rows, running max over KV heads, key
+//          store, and the first radix-select histogram + score stats of the
+//          batch row (so the select kernel skips its first pass).
+// The query rows are written once into shared memory in the same swizzled
+// K-major layout.  No multicast is used.  Used when the store is 16-bit,
+// page_size == 128, head_dim is a multiple of 64 (<= 256), batch == 1 and
+// G*Q <= 32; otherwise fine_scores_kernel runs.
+#include <algorithm>
+
+#include "internal.h"
+#include "select.cuh"
+#include "tc.cuh"
+
+namespace kiv {
+
+constexpr int TC_THREADS = 192;
+constexpr int TC_PAGE = 128;
+
+struct TcGeom {
+  int64_t U, np_global, partial, per_b;
+  bool part_owned;
+};
+
+template <bool BF16>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+fine_scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_query q, Workspace w,
+                      int ncols, int stages) {
+  using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+  griddep_wait();
+  extern __shared__ uint8_t tc_dyn[];
+  __shared__ uint64_t full[4], empty[4], acc_full[2], acc_empty[2];
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_fail;
+  __shared__ uint32_t s_wmax[4];
+  __shared__ float s_wsum[4];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int D = st.head_dim, H = st.num_kv_heads, S = st.page_size;
+  const int Hq = q.num_query_heads, Q = q.query_len, G = Hq / H;
+  const int rows_kv = G * Q;
+  const int nbox = D / 64;
+  const uint32_t tile_bytes = (uint32_t)TC_PAGE * D * sizeof(T);
+  const uint32_t qbox_bytes = (uint32_t)ncols * 128;
+
+  // 1024-byte aligned carve-up: [stages][tile] [H][nbox][qbox] [hist 2048]
+  const uint32_t base_addr = smem_u32(tc_dyn);
+  uint8_t *smem = tc_dyn + ((1024 - (base_addr & 1023)) & 1023);
+  uint8_t *stage_mem = smem;
+  uint8_t *qmem = stage_mem + (size_t)stages * tile_bytes;
+  uint32_t *hist = reinterpret_cast<uint32_t *>(qmem + (size_t)H * nbox * qbox_bytes);
+
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    st.state[KIV_ST_FINE_MAX] = 0;
+    st.state[KIV_ST_FINE_SUM] = 0;
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 4);
+    }
+    mbar_fence_init();
+    s_fail = 0;
+  }
+  if (warp == 0) {
+    tc::tmem_alloc(&s_tmem, (uint32_t)(2 * ncols < 32 ? 32 : 2 * ncols));
+    tc::tmem_relinquish();
+  }
+  if (threadIdx.x == 32 * 4) tc::prefetch_map(&kmap);
+  // query rows of batch row 0 -> swizzled K-major tiles [kvh][box][ncols x 128 B]
+  const T *qb = reinterpret_cast<const T *>(q.q);
+  for (int e = threadIdx.x; e < H * ncols * (D / 8); e += TC_THREADS) {
+    const int chunk = e % (D / 8);            // 16-byte chunk along D
+    const int n = (e / (D / 8)) % ncols;      // query row within the KV head
+    const int kvh = e / ((D / 8) * ncols);
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (n < rows_kv) {
+      const int h = kvh * G + n / Q, tq = n % Q;
+      v = ld16(qb + h * q.stride_h + tq * q.stride_t + chunk * 8);
+    }
+    const int box = chunk / 8, c = chunk % 8;
+    uint8_t *dst = qmem + ((size_t)kvh * nbox + box) * qbox_bytes + n * 128 + ((c ^ (n & 7)) * 16);
+    *reinterpret_cast<uint4 *>(dst) = v;
+  }
+  for (int i = threadIdx.x; i < SEL_BINS; i += TC_THREADS) hist[i] = 0;
+  tc::fence_proxy_async_smem();
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = s_tmem;
+
+  TcGeom f;
+  {
+    const int64_t cold = st_ld(st.state, KIV_ST_COLD_LEN);
+    f.U = st_ld(st.state, KIV_ST_UNION);
+    f.np_global = cold / S;
+    f.partial = cold % S;
+    f.part_owned = f.partial > 0 && (f.np_global % st.shard_count) == st.shard_rank;
+    f.per_b = f.U + (f.part_owned ? 1 : 0);
+  }
+  const int64_t units = f.per_b;  // batch 1: one unit per candidate page
+  const int64_t my_units = units > blockIdx.x ? (units - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+  const int64_t my_tiles = my_units * H;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      // ------------------------------------------------ TMA producer
+      for (int64_t t = 0; t < my_tiles; ++t) {
+        const int s = (int)(t % stages);
+        if (t >= stages && !mbar_wait_bounded(&empty[s], (uint32_t)((t / stages - 1) & 1))) {
+          s_fail = 1;
+          break;
+        }
+        const int64_t u = blockIdx.x + (t / H) * gridDim.x;
+        const int kvh = (int)(t % H);
+        const int64_t page = u < f.U ? (int64_t)w.uni[u] : f.np_global;
+        const int64_t lp = page / st.shard_count;
+        const int32_t y = (int32_t)((int64_t)kvh * st.cold_capacity + lp * S);
+        mbar_arrive_tx(&full[s], tile_bytes);
+        for (int j = 0; j < nbox; ++j)
+          tc::tma_load_2d(stage_mem + (size_t)s * tile_bytes + (size_t)j * TC_PAGE * 128, &kmap, 64 * j, y,
+                          &full[s]);
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      // ------------------------------------------------ MMA issuer
+      const uint32_t idesc = tc::idesc_f16(BF16, TC_PAGE, ncols);
+      for (int64_t t = 0; t < my_tiles; ++t) {
+        const int s = (int)(t % stages);
+        const int a = (int)(t & 1);
+        if (!mbar_wait_bounded(&full[s], (uint32_t)((t / stages) & 1))) { s_fail = 1; break; }
+        if (t >= 2 && !mbar_wait_bounded(&acc_empty[a], (uint32_t)((t / 2 - 1) & 1))) { s_fail = 1; break; }
+        tc::fence_after_sync();
+        const int kvh = (int)(t % H);
+        const uint32_t a0 = smem_u32(stage_mem + (size_t)s * tile_bytes);
+        const uint32_t b0 = smem_u32(qmem + (size_t)kvh * nbox * qbox_bytes);
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const int j = kk >> 2, sub = kk & 3;
+          const uint64_t ad = tc::sdesc_k128(a0 + j * (TC_PAGE * 128) + sub * 32);
+          const uint64_t bd = tc::sdesc_k128(b0 + j * qbox_bytes + sub * 32);
+          tc::mma_f16(tmem + (uint32_t)(a * ncols), ad, bd, idesc, kk > 0 ? 1u : 0u);
+        }
+        tc::commit(&empty[s]);
+        tc::commit(&acc_full[a]);
+      }
+    }
+  } else {
+    // -------------------------------------------------- epilogue, warps 0-3
+    const int tok = warp * 32 + lane;
+    float m = -INFINITY;
+    uint32_t kmax = 0;
+    float ksum = 0.f;
+    for (int64_t t = 0; t < my_tiles; ++t) {
+      const int a = (int)(t & 1);
+      if (!mbar_wait_bounded(&acc_full[a], (uint32_t)((t / 2) & 1))) { s_fail = 1; break; }
+      tc::fence_after_sync();
+      const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(a * ncols);
+      uint32_t r[16];
+      for (int c0 = 0; c0 < ncols; c0 += 16) {
+        tc::ld_32x16(taddr + c0, r);
+        tc::wait_ld();
+#pragma unroll
+        for (int c = 0; c < 16; ++c)
+          if (c0 + c < rows_kv) m = fmaxf(m, __uint_as_float(r[c]) * q.scaling);
+      }
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[a]);
+      if ((t % H) == H - 1) {
+        const int64_t u = blockIdx.x + (t / H) * gridDim.x;
+        const int n_tok = u < f.U ? TC_PAGE : (int)f.partial;
+        if (tok < n_tok) {
+          const uint32_t key = f2key(m);
+          w.agg[u * S + tok] = key;
+          hist_add(hist, key >> 21);
+          kmax = key > kmax ? key : kmax;
+          ksum += m;
+        }
+        m = -INFINITY;
+      }
+    }
+    // per-warp stats
+    kmax = __reduce_max_sync(KIV_FULL_MASK, kmax);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ksum += __shfl_xor_sync(KIV_FULL_MASK, ksum, o);
+    if (lane == 0) {
+      s_wmax[warp] = kmax;
+      s_wsum[warp] = ksum;
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  // publish the histogram and the stats of batch row 0 for the select kernel
+  for (int i = threadIdx.x; i < SEL_BINS; i += TC_THREADS)
+    if (hist[i]) atomicAdd(&w.fhist[i], hist[i]);
+  if (threadIdx.x == 0) {
+    uint32_t mk = 0;
+    double sm = 0.0;
+    for (int i = 0; i < 4; ++i) {
+      mk = s_wmax[i] > mk ? s_wmax[i] : mk;
+      sm += s_wsum[i];
+    }
+    if (my_tiles > 0) {
+      atomicMax(reinterpret_cast<unsigned long long *>(&w.fstat[0]), (unsigned long long)mk);
+      atomicAdd(reinterpret_cast<double *>(&w.fstat[1]), sm);
+    }
+    if (s_fail)
+      atomicOr(reinterpret_cast<unsigned long long *>(st.state + KIV_ST_ERROR),
+               (unsigned long long)KIV_ERRBIT_WAIT_TIMEOUT);
+  }
+  if (warp == 0) tc::tmem_dealloc(tmem, (uint32_t)(2 * ncols < 32 ? 32 : 2 * ncols));
+}
+
+// ------------------------------------------------------------------ host
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+static kiv_status encode_fn() {
+  if (g_encode) return KIV_OK;
+  void *fn = nullptr;
+  cudaDriverEntryPointQueryResult qr;
+  cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &qr);
+  if (e != cudaSuccess || qr != cudaDriverEntryPointSuccess || fn == nullptr) {
+    set_error("cuTensorMapEncodeTiled unavailable");
+    return KIV_ERR_CUDA;
+  }
+  g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  return KIV_OK;
+}
+
+bool fine_tc_eligible(const kiv_store *st, const kiv_query *q) {
+  const int rows_kv = (q->num_query_heads / st->num_kv_heads) * q->query_len;
+  const int ncols = rows_kv <= 16 ? 16 : 32;
+  const size_t qbytes = (size_t)st->num_kv_heads * ncols * st->head_dim * 2;
+  return (st->dtype == KIV_DTYPE_BF16 || st->dtype == KIV_DTYPE_F16) && st->page_size == TC_PAGE &&
+         st->head_dim % 64 == 0 && st->head_dim <= 256 && st->batch == 1 && rows_kv <= 32 &&
+         qbytes <= 32 * 1024 && (int64_t)st->num_kv_heads * st->cold_capacity < (1ll << 31) &&
+         getenv("KIV_DISABLE_TCGEN05") == nullptr;
+}
+
+kiv_status launch_fine_score_tc(const kiv_store *st, const kiv_query *q, const Workspace &w, cudaStream_t s) {
+  KIV_CHECK(encode_fn());
+  const int D = st->head_dim;
+  const int rows_kv = (q->num_query_heads / st->num_kv_heads) * q->query_len;
+  const int ncols = rows_kv <= 16 ? 16 : 32;
+  CUtensorMap map;
+  const cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)st->num_kv_heads * st->cold_capacity};
+  const cuuint64_t strides[1] = {(cuuint64_t)D * 2};
+  const cuuint32_t box[2] = {64, TC_PAGE};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = g_encode(&map, st->dtype == KIV_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                                : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                              2, st->cold_k, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return KIV_ERR_CUDA;
+  }
+  const size_t tile = (size_t)TC_PAGE * D * 2;
+  const size_t qbytes = (size_t)st->num_kv_heads * ncols * D * 2;
+  const size_t fixed = 1024 + qbytes + SEL_BINS * 4;
+  const int stages = (int)std::min<size_t>(4, (200 * 1024 - fixed) / tile);
+  if (stages < 2) return KIV_ERR_UNSUPPORTED;
+  const size_t smem = fixed + (size_t)stages * tile;
+  const int64_t units_cap = w.u_cap + 1;
+  const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(units_cap, sm_count()));
+  if (st->dtype == KIV_DTYPE_BF16) {
+    cudaFuncSetAttribute(fine_scores_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    fine_scores_tc_kernel<true><<<(unsigned)grid, TC_THREADS, smem, s>>>(map, *st, *q, w, ncols, stages);
+  } else {
+    cudaFuncSetAttribute(fine_scores_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    fine_scores_tc_kernel<false><<<(unsigned)grid, TC_THREADS, smem, s>>>(map, *st, *q, w, ncols, stages);
+  }
+  return cuda_status(cudaGetLastError(), "fine_scores_tc");
+}
+
+}  // namespace kiv

@@ -29,6 +29,8 @@ struct Workspace {
   int32_t *uni;        // [u_cap]            union pages (global ids, ascending)
   uint32_t *agg;       // [B, c_cap]         fine keys (monotone u32 of the max score)
   int32_t *selcnt;     // [B]                selected tokens of this shard per batch row
+  uint32_t *fhist;     // [B, 2048]          histogram of fine keys >> 21 (select pass 0), self-clearing
+  uint64_t *fstat;     // [B, 2]             largest fine key, sum of fine scores (double bits)
   float *part;         // [R, split_cap, D+2] attention split partials
   int64_t R, K, np_cap, u_cap, c_cap, split_cap;
   size_t bytes;
@@ -51,6 +53,8 @@ kiv_status launch_coarse_merge(const kiv_store *st, const kiv_query *q, const Wo
 kiv_status launch_fine(const kiv_store *st, const kiv_query *q, const Workspace &w, int32_t *sel,
                        float *sel_scores, cudaStream_t s);
 kiv_status launch_fine_score(const kiv_store *st, const kiv_query *q, const Workspace &w, cudaStream_t s);
+bool fine_tc_eligible(const kiv_store *st, const kiv_query *q);
+kiv_status launch_fine_score_tc(const kiv_store *st, const kiv_query *q, const Workspace &w, cudaStream_t s);
 kiv_status launch_fine_topk(const kiv_store *st, const kiv_query *q, const Workspace &w, int32_t *sel,
                             float *sel_scores, cudaStream_t s);
 kiv_status launch_fine_merge(const kiv_store *st, const kiv_query *q, const Workspace &w,
@@ -66,6 +70,12 @@ kiv_status launch_attend_merge(const kiv_store *st, const kiv_query *q, const fl
                                int32_t n, void *out, cudaStream_t s);
 
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+#define KIV_CHECK(x)                 \
+  do {                               \
+    const kiv_status _st = (x);      \
+    if (_st != KIV_OK) return _st;   \
+  } while (0)
 
 // floats per attention partial row: out[D], max, sum, 16-byte aligned
 __host__ __device__ inline int partial_stride(int D) { return (D + 2 + 3) & ~3; }

@@ -77,7 +77,7 @@ __device__ __forceinline__ void hist_add(uint32_t *h, uint32_t bin) {
 // needs a single cluster barrier.
 template <int BLOCK, int CL>
 __device__ void radix_threshold(const uint32_t *keys, int n_local, uint32_t k, SelectSmem<BLOCK> &sm,
-                                uint32_t &T, uint32_t &need_eq) {
+                                uint32_t &T, uint32_t &need_eq, const uint32_t *pre0 = nullptr) {
   constexpr int IPT = SEL_BINS / BLOCK;
   uint32_t prefix = 0, pmask = 0, remaining = k;
   const int shifts[3] = {21, 10, 0};
@@ -88,17 +88,23 @@ __device__ void radix_threshold(const uint32_t *keys, int n_local, uint32_t k, S
   cl_sync<CL>();
 #pragma unroll 1
   for (int pass = 0; pass < 3; ++pass) {
-    uint32_t *h = cl_map<CL>(sm.hist[pass], 0);
+    const uint32_t *h = cl_map<CL>(sm.hist[pass], 0);
     const int sh = shifts[pass];
-    for (int i = threadIdx.x; i < n_local; i += BLOCK) {
-      const uint32_t key = keys[i];
-      if ((key & pmask) == prefix) hist_add(h, (key >> sh) & (SEL_BINS - 1));
+    if (pass == 0 && pre0 != nullptr) {
+      h = pre0;   // the producer of the keys already built the first histogram
+    } else {
+      for (int i = threadIdx.x; i < n_local; i += BLOCK) {
+        const uint32_t key = keys[i];
+        if ((key & pmask) == prefix) hist_add(cl_map<CL>(sm.hist[pass], 0), (key >> sh) & (SEL_BINS - 1));
+      }
+      cl_sync<CL>();
     }
-    cl_sync<CL>();
     // totals, in descending bin order: item j of thread t is bin (SEL_BINS-1) - (t*IPT + j)
     uint32_t items[IPT];
 #pragma unroll
-    for (int j = 0; j < IPT; ++j) items[j] = h[SEL_BINS - 1 - (threadIdx.x * IPT + j)];
+    for (int j = 0; j < IPT; ++j)
+      items[j] = (pass == 0 && pre0 != nullptr) ? __ldcg(h + SEL_BINS - 1 - (threadIdx.x * IPT + j))
+                                                : h[SEL_BINS - 1 - (threadIdx.x * IPT + j)];
     uint32_t incl[IPT];
     cub::BlockScan<uint32_t, BLOCK>(sm.scan).InclusiveSum(items, incl);
 #pragma unroll
