@@ -18,7 +18,8 @@ namespace kiv {
 
 constexpr int CS_THREADS = 128;      // coarse scoring
 constexpr int CS_PAGES = 16;         // pages per work item (one bulk copy)
-constexpr int TK_THREADS = 256;      // per-row top-k
+constexpr int TK_THREADS = 1024;     // per-row top-k
+constexpr int CM_THREADS = 256;      // merge of gathered per-row lists
 
 // local finalized pages of this shard given the global finalized count
 __device__ __forceinline__ int64_t local_pages(int64_t np_global, int rank, int n) {
@@ -60,6 +61,8 @@ coarse_scores_kernel(kiv_store st, kiv_query q, Workspace w) {
   }
   __syncthreads();
 
+  uint32_t kmax = 0;
+  float ksum = 0.f;
   uint32_t phase = 0;
   for (int64_t it = blockIdx.x; it < items; it += gridDim.x, phase ^= 1) {
     const int64_t pb = it % nblk;
@@ -107,12 +110,24 @@ coarse_scores_kernel(kiv_store st, kiv_query q, Workspace w) {
           if (rr < rows_kv) {
             const int h = kvh * G + rr / Q, t = rr % Q;
             const int64_t R_idx = ((int64_t)b * q.num_query_heads + h) * Q + t;
-            w.scores[R_idx * w.np_cap + p0 + pi] = acc[i] * q.scaling;
+            const float sc = acc[i] * q.scaling;
+            w.scores[R_idx * w.np_cap + p0 + pi] = sc;
+            const uint32_t key = f2key(sc);
+            hist_add(w.chist + R_idx * SEL_BINS, key >> 21);
+            kmax = key > kmax ? key : kmax;
+            ksum += sc;
           }
         }
       }
     }
     __syncthreads();  // the tile is free for the next block
+  }
+  kmax = __reduce_max_sync(KIV_FULL_MASK, kmax);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ksum += __shfl_xor_sync(KIV_FULL_MASK, ksum, o);
+  if (lane == 0 && kmax != 0) {
+    atomicMax(reinterpret_cast<unsigned long long *>(&w.cstat[0]), (unsigned long long)kmax);
+    atomicAdd(reinterpret_cast<double *>(&w.cstat[1]), (double)ksum);
   }
   if (s_fail && threadIdx.x == 0)
     atomicOr(reinterpret_cast<unsigned long long *>(st.state + KIV_ST_ERROR), (unsigned long long)KIV_ERRBIT_WAIT_TIMEOUT);
@@ -136,11 +151,10 @@ coarse_topk_kernel(kiv_store st, kiv_query q, Workspace w, float *row_scores, in
     const float *src = w.scores + (int64_t)row * w.np_cap;
     for (int64_t i = threadIdx.x; i < np; i += TK_THREADS) keys[i] = f2key(src[i]);
     __syncthreads();
-    block_stats<TK_THREADS>(keys, (int)np, st.state + KIV_ST_COARSE_MAX, st.state + KIV_ST_COARSE_SUM);
     const uint32_t k = (uint32_t)(K < np ? (int64_t)K : np);
     uint32_t T = 0, need = 0;
     const bool all = (int64_t)k >= np;
-    if (!all) radix_threshold<TK_THREADS, 1>(keys, (int)np, k, sm, T, need);
+    if (!all) radix_threshold<TK_THREADS, 1>(keys, (int)np, k, sm, T, need, w.chist + (int64_t)row * SEL_BINS);
     const int rank = st.shard_rank, nsh = st.shard_count;
     if (nsh == 1) {
       ordered_emit<TK_THREADS, 1>(keys, (int)np, T, need, all, sm,
@@ -163,10 +177,20 @@ coarse_topk_kernel(kiv_store st, kiv_query q, Workspace w, float *row_scores, in
       row_pages[(int64_t)row * K + j] = -1;
     }
   }
-  if (st.shard_count == 1) {
-    if (last_block(reinterpret_cast<unsigned long long *>(st.state + CTR_COARSE), gridDim.x)) {
-      const int64_t u = compact_flags<TK_THREADS>(w.flags, np, w.uni, w.u_cap, 1, 0, sm.scan);
+  // the scorer's histogram of this row has been used: clear it for the next pass
+  __syncthreads();
+  for (int i = threadIdx.x; i < SEL_BINS; i += TK_THREADS) w.chist[(int64_t)row * SEL_BINS + i] = 0;
+  if (last_block(reinterpret_cast<unsigned long long *>(st.state + CTR_COARSE), gridDim.x)) {
+    if (st.shard_count == 1) {
+      const int64_t u = compact_flags<TK_THREADS>(w.flags, np, w.uni, w.u_cap, 1, 0, sm.scan32);
       if (threadIdx.x == 0) st.state[KIV_ST_UNION] = u;
+    }
+    if (threadIdx.x == 0) {
+      const unsigned long long mk = w.cstat[0], sb = w.cstat[1];
+      if (mk) atomicMax(reinterpret_cast<unsigned long long *>(st.state + KIV_ST_COARSE_MAX), mk);
+      atomicAdd(reinterpret_cast<double *>(st.state + KIV_ST_COARSE_SUM), __longlong_as_double((long long)sb));
+      w.cstat[0] = 0;
+      w.cstat[1] = 0;
     }
   }
 }
@@ -174,12 +198,12 @@ coarse_topk_kernel(kiv_store st, kiv_query q, Workspace w, float *row_scores, in
 // Merge gathered per-row lists [n][R][K] into the global per-row top-k and
 // keep the union pages this shard owns.  Ties at the threshold are broken by
 // the lowest page id.
-__global__ void __launch_bounds__(TK_THREADS)
+__global__ void __launch_bounds__(CM_THREADS)
 coarse_merge_kernel(kiv_store st, kiv_query q, Workspace w, const float *ls, const int32_t *lp,
                     int32_t n) {
   griddep_wait();
   extern __shared__ uint4 dyn_smem[];
-  __shared__ SelectSmem<TK_THREADS> sm;
+  __shared__ SelectSmem<CM_THREADS> sm;
   const int S = st.page_size;
   const int64_t np_global = st_ld(st.state, KIV_ST_COLD_LEN) / S;
   const int row = blockIdx.x;
@@ -188,7 +212,7 @@ coarse_merge_kernel(kiv_store st, kiv_query q, Workspace w, const float *ls, con
   const int m = n * K;
   uint32_t *keys = reinterpret_cast<uint32_t *>(dyn_smem);
   int32_t *ids = reinterpret_cast<int32_t *>(keys + m);
-  for (int i = threadIdx.x; i < m; i += TK_THREADS) {
+  for (int i = threadIdx.x; i < m; i += CM_THREADS) {
     const int src = i / K, j = i % K;
     const int64_t off = ((int64_t)src * R + row) * K + j;
     const int32_t pg = lp[off];
@@ -199,9 +223,9 @@ coarse_merge_kernel(kiv_store st, kiv_query q, Workspace w, const float *ls, con
   const uint32_t k = (uint32_t)(K < np_global ? (int64_t)K : np_global);
   if (k > 0) {
     uint32_t T = 0, need = 0;
-    radix_threshold<TK_THREADS, 1>(keys, m, k, sm, T, need);
+    radix_threshold<CM_THREADS, 1>(keys, m, k, sm, T, need);
     // entries == T: take the `need` lowest page ids
-    for (int i = threadIdx.x; i < m; i += TK_THREADS) {
+    for (int i = threadIdx.x; i < m; i += CM_THREADS) {
       bool take = keys[i] > T;
       if (!take && keys[i] == T && ids[i] >= 0) {
         uint32_t rank = 0;
@@ -215,8 +239,8 @@ coarse_merge_kernel(kiv_store st, kiv_query q, Workspace w, const float *ls, con
   }
   if (last_block(reinterpret_cast<unsigned long long *>(st.state + CTR_MERGE), gridDim.x)) {
     const int64_t np = local_pages(np_global, st.shard_rank, st.shard_count);
-    const int64_t u = compact_flags<TK_THREADS>(w.flags, np, w.uni, w.u_cap, st.shard_count,
-                                                st.shard_rank, sm.scan);
+    const int64_t u = compact_flags<CM_THREADS>(w.flags, np, w.uni, w.u_cap, st.shard_count,
+                                                st.shard_rank, sm.scan32);
     if (threadIdx.x == 0) st.state[KIV_ST_UNION] = u;
   }
 }
@@ -257,7 +281,9 @@ static kiv_status dispatch_cs(const kiv_store *st, const kiv_query *q, const Wor
 kiv_status launch_coarse(const kiv_store *st, const kiv_query *q, const Workspace &w,
                          float *row_scores, int32_t *row_pages, cudaStream_t s) {
   kiv_status rc;
-  switch (st->dtype) {
+  if (fine_tc_eligible(st, q)) {
+    rc = launch_coarse_score_tc(st, q, w, s);
+  } else switch (st->dtype) {
     case KIV_DTYPE_F32: rc = dispatch_cs<float>(st, q, w, s); break;
     case KIV_DTYPE_BF16: rc = dispatch_cs<__nv_bfloat16>(st, q, w, s); break;
     case KIV_DTYPE_F16: rc = dispatch_cs<__half>(st, q, w, s); break;
@@ -280,7 +306,7 @@ kiv_status launch_coarse_merge(const kiv_store *st, const kiv_query *q, const Wo
   const size_t smem = (size_t)n * q->top_pages * (sizeof(uint32_t) + sizeof(int32_t));
   if (smem > 200 * 1024) return KIV_ERR_CAPACITY;
   cudaFuncSetAttribute(coarse_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  coarse_merge_kernel<<<(unsigned)w.R, TK_THREADS, smem, s>>>(*st, *q, w, ls, lp, n);
+  coarse_merge_kernel<<<(unsigned)w.R, CM_THREADS, smem, s>>>(*st, *q, w, ls, lp, n);
   return cuda_status(cudaGetLastError(), "coarse_merge");
 }
 

@@ -23,7 +23,7 @@ namespace kiv {
 constexpr int FS_THREADS = 256;
 constexpr int FS_STAGES = 4;
 constexpr int FS_TILE_BYTES = 16384;
-constexpr int SL_THREADS = 512;
+constexpr int SL_THREADS = 1024;
 constexpr int FM_THREADS = 512;
 
 struct FineGeom {

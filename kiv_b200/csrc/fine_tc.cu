@@ -36,10 +36,13 @@ struct TcGeom {
   bool part_owned;
 };
 
-template <bool BF16>
+// COARSE == false: fine scoring over candidate pages (key per token, max over rows)
+// COARSE == true:  coarse scoring over page summaries (score per row and page,
+//                  plus each row's first radix histogram)
+template <bool BF16, bool COARSE>
 __global__ void __launch_bounds__(TC_THREADS, 1)
-fine_scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_query q, Workspace w,
-                      int ncols, int stages) {
+scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_query q, Workspace w,
+                 int ncols, int stages) {
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   griddep_wait();
   extern __shared__ uint8_t tc_dyn[];
@@ -64,8 +67,8 @@ fine_scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, ki
   uint32_t *hist = reinterpret_cast<uint32_t *>(qmem + (size_t)H * nbox * qbox_bytes);
 
   if (blockIdx.x == 0 && threadIdx.x == 0) {
-    st.state[KIV_ST_FINE_MAX] = 0;
-    st.state[KIV_ST_FINE_SUM] = 0;
+    st.state[COARSE ? KIV_ST_COARSE_MAX : KIV_ST_FINE_MAX] = 0;
+    st.state[COARSE ? KIV_ST_COARSE_SUM : KIV_ST_FINE_SUM] = 0;
   }
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
@@ -115,7 +118,11 @@ fine_scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, ki
     f.part_owned = f.partial > 0 && (f.np_global % st.shard_count) == st.shard_rank;
     f.per_b = f.U + (f.part_owned ? 1 : 0);
   }
-  const int64_t units = f.per_b;  // batch 1: one unit per candidate page
+  // batch 1.  FINE: one unit per candidate page (tiles = its KV heads);
+  // COARSE: one unit per block of 128 finalized local pages (tiles = KV heads)
+  const int64_t np_local = f.np_global > st.shard_rank
+                               ? (f.np_global - st.shard_rank + st.shard_count - 1) / st.shard_count : 0;
+  const int64_t units = COARSE ? (np_local + TC_PAGE - 1) / TC_PAGE : f.per_b;
   const int64_t my_units = units > blockIdx.x ? (units - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
   const int64_t my_tiles = my_units * H;
 
@@ -130,9 +137,14 @@ fine_scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, ki
         }
         const int64_t u = blockIdx.x + (t / H) * gridDim.x;
         const int kvh = (int)(t % H);
-        const int64_t page = u < f.U ? (int64_t)w.uni[u] : f.np_global;
-        const int64_t lp = page / st.shard_count;
-        const int32_t y = (int32_t)((int64_t)kvh * st.cold_capacity + lp * S);
+        int32_t y;
+        if (COARSE) {
+          y = (int32_t)((int64_t)kvh * w.np_cap + u * TC_PAGE);
+        } else {
+          const int64_t page = u < f.U ? (int64_t)w.uni[u] : f.np_global;
+          const int64_t lp = page / st.shard_count;
+          y = (int32_t)((int64_t)kvh * st.cold_capacity + lp * S);
+        }
         mbar_arrive_tx(&full[s], tile_bytes);
         for (int j = 0; j < nbox; ++j)
           tc::tma_load_2d(stage_mem + (size_t)s * tile_bytes + (size_t)j * TC_PAGE * 128, &kmap, 64 * j, y,
@@ -174,6 +186,36 @@ fine_scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, ki
       tc::fence_after_sync();
       const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(a * ncols);
       uint32_t r[16];
+      if (COARSE) {
+        // one score per (query row, page): thread tok holds page u*128 + tok
+        const int64_t u = blockIdx.x + (t / H) * gridDim.x;
+        const int kvh = (int)(t % H);
+        const int64_t p = u * TC_PAGE + tok;
+        for (int c0 = 0; c0 < ncols; c0 += 16) {
+          tc::ld_32x16(taddr + c0, r);
+          tc::wait_ld();
+          if (p < np_local) {
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+              const int rr = c0 + c;
+              if (rr < rows_kv) {
+                const float sc = __uint_as_float(r[c]) * q.scaling;
+                const int h = kvh * G + rr / Q, tq = rr % Q;
+                const int64_t R_idx = (int64_t)h * Q + tq;
+                w.scores[R_idx * w.np_cap + p] = sc;
+                const uint32_t key = f2key(sc);
+                hist_add(w.chist + R_idx * SEL_BINS, key >> 21);
+                kmax = key > kmax ? key : kmax;
+                ksum += sc;
+              }
+            }
+          }
+        }
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[a]);
+        continue;
+      }
       for (int c0 = 0; c0 < ncols; c0 += 16) {
         tc::ld_32x16(taddr + c0, r);
         tc::wait_ld();
@@ -210,8 +252,10 @@ fine_scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, ki
   __syncthreads();
   tc::fence_after_sync();
   // publish the histogram and the stats of batch row 0 for the select kernel
-  for (int i = threadIdx.x; i < SEL_BINS; i += TC_THREADS)
-    if (hist[i]) atomicAdd(&w.fhist[i], hist[i]);
+  if (!COARSE) {
+    for (int i = threadIdx.x; i < SEL_BINS; i += TC_THREADS)
+      if (hist[i]) atomicAdd(&w.fhist[i], hist[i]);
+  }
   if (threadIdx.x == 0) {
     uint32_t mk = 0;
     double sm = 0.0;
@@ -220,8 +264,13 @@ fine_scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, ki
       sm += s_wsum[i];
     }
     if (my_tiles > 0) {
-      atomicMax(reinterpret_cast<unsigned long long *>(&w.fstat[0]), (unsigned long long)mk);
-      atomicAdd(reinterpret_cast<double *>(&w.fstat[1]), sm);
+      if (COARSE) {
+        atomicMax(reinterpret_cast<unsigned long long *>(&w.cstat[0]), (unsigned long long)mk);
+        atomicAdd(reinterpret_cast<double *>(&w.cstat[1]), sm);
+      } else {
+        atomicMax(reinterpret_cast<unsigned long long *>(&w.fstat[0]), (unsigned long long)mk);
+        atomicAdd(reinterpret_cast<double *>(&w.fstat[1]), sm);
+      }
     }
     if (s_fail)
       atomicOr(reinterpret_cast<unsigned long long *>(st.state + KIV_ST_ERROR),
@@ -256,21 +305,24 @@ bool fine_tc_eligible(const kiv_store *st, const kiv_query *q) {
          getenv("KIV_DISABLE_TCGEN05") == nullptr;
 }
 
-kiv_status launch_fine_score_tc(const kiv_store *st, const kiv_query *q, const Workspace &w, cudaStream_t s) {
+// tensor-core scoring: coarse (summaries) or fine (candidate pages)
+static kiv_status launch_scores_tc(const kiv_store *st, const kiv_query *q, const Workspace &w, cudaStream_t s,
+                                   bool coarse) {
   KIV_CHECK(encode_fn());
   const int D = st->head_dim;
   const int rows_kv = (q->num_query_heads / st->num_kv_heads) * q->query_len;
   const int ncols = rows_kv <= 16 ? 16 : 32;
   CUtensorMap map;
-  const cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)st->num_kv_heads * st->cold_capacity};
+  const int64_t rows = coarse ? (int64_t)st->num_kv_heads * w.np_cap : (int64_t)st->num_kv_heads * st->cold_capacity;
+  const cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)D * 2};
   const cuuint32_t box[2] = {64, TC_PAGE};
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = g_encode(&map, st->dtype == KIV_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                                 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                              2, st->cold_k, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                              2, coarse ? st->summaries : st->cold_k, dims, strides, box, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_error("cuTensorMapEncodeTiled failed (%d)", (int)r);
     return KIV_ERR_CUDA;
@@ -281,16 +333,28 @@ kiv_status launch_fine_score_tc(const kiv_store *st, const kiv_query *q, const W
   const int stages = (int)std::min<size_t>(4, (200 * 1024 - fixed) / tile);
   if (stages < 2) return KIV_ERR_UNSUPPORTED;
   const size_t smem = fixed + (size_t)stages * tile;
-  const int64_t units_cap = w.u_cap + 1;
+  const int64_t units_cap = coarse ? ceil_div(w.np_cap, TC_PAGE) : w.u_cap + 1;
   const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(units_cap, sm_count()));
-  if (st->dtype == KIV_DTYPE_BF16) {
-    cudaFuncSetAttribute(fine_scores_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    fine_scores_tc_kernel<true><<<(unsigned)grid, TC_THREADS, smem, s>>>(map, *st, *q, w, ncols, stages);
-  } else {
-    cudaFuncSetAttribute(fine_scores_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    fine_scores_tc_kernel<false><<<(unsigned)grid, TC_THREADS, smem, s>>>(map, *st, *q, w, ncols, stages);
-  }
-  return cuda_status(cudaGetLastError(), "fine_scores_tc");
+#define KIV_TC_LAUNCH(BF, CO)                                                                          \
+  do {                                                                                                 \
+    cudaFuncSetAttribute(scores_tc_kernel<BF, CO>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+    scores_tc_kernel<BF, CO><<<(unsigned)grid, TC_THREADS, smem, s>>>(map, *st, *q, w, ncols, stages);    \
+  } while (0)
+  const bool bf = st->dtype == KIV_DTYPE_BF16;
+  if (bf && coarse) KIV_TC_LAUNCH(true, true);
+  else if (bf) KIV_TC_LAUNCH(true, false);
+  else if (coarse) KIV_TC_LAUNCH(false, true);
+  else KIV_TC_LAUNCH(false, false);
+#undef KIV_TC_LAUNCH
+  return cuda_status(cudaGetLastError(), coarse ? "coarse_scores_tc" : "fine_scores_tc");
+}
+
+kiv_status launch_fine_score_tc(const kiv_store *st, const kiv_query *q, const Workspace &w, cudaStream_t s) {
+  return launch_scores_tc(st, q, w, s, false);
+}
+
+kiv_status launch_coarse_score_tc(const kiv_store *st, const kiv_query *q, const Workspace &w, cudaStream_t s) {
+  return launch_scores_tc(st, q, w, s, true);
 }
 
 }  // namespace kiv

@@ -31,6 +31,8 @@ struct Workspace {
   int32_t *selcnt;     // [B]                selected tokens of this shard per batch row
   uint32_t *fhist;     // [B, 2048]          histogram of fine keys >> 21 (select pass 0), self-clearing
   uint64_t *fstat;     // [B, 2]             largest fine key, sum of fine scores (double bits)
+  uint32_t *chist;     // [R, 2048]          histogram of coarse keys >> 21 per query row, self-clearing
+  uint64_t *cstat;     // [2]                largest coarse key, sum of coarse scores (double bits)
   float *part;         // [R, split_cap, D+2] attention split partials
   int64_t R, K, np_cap, u_cap, c_cap, split_cap;
   size_t bytes;
@@ -55,6 +57,7 @@ kiv_status launch_fine(const kiv_store *st, const kiv_query *q, const Workspace 
 kiv_status launch_fine_score(const kiv_store *st, const kiv_query *q, const Workspace &w, cudaStream_t s);
 bool fine_tc_eligible(const kiv_store *st, const kiv_query *q);
 kiv_status launch_fine_score_tc(const kiv_store *st, const kiv_query *q, const Workspace &w, cudaStream_t s);
+kiv_status launch_coarse_score_tc(const kiv_store *st, const kiv_query *q, const Workspace &w, cudaStream_t s);
 kiv_status launch_fine_topk(const kiv_store *st, const kiv_query *q, const Workspace &w, int32_t *sel,
                             float *sel_scores, cudaStream_t s);
 kiv_status launch_fine_merge(const kiv_store *st, const kiv_query *q, const Workspace &w,

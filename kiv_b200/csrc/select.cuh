@@ -24,13 +24,19 @@ namespace cg = cooperative_groups;
 
 constexpr int SEL_BINS = 2048;
 
+constexpr int SEL_MAX_CL = 16;
+
 template <int BLOCK>
 struct SelectSmem {
-  uint32_t hist[3][SEL_BINS];   // rotating; with a cluster only rank 0's are used
-  uint32_t cnt[2];          // this CTA's (gt, eq) counts
-  uint32_t bin;             // chosen bin of the current pass
-  uint32_t above;           // keys strictly above the chosen bin
-  typename cub::BlockScan<uint32_t, BLOCK>::TempStorage scan;
+  uint32_t hist[2][SEL_BINS];   // local histograms, double-buffered across passes
+  uint64_t cnt;                 // this CTA's packed (gt << 32 | eq) counts
+  uint64_t rank_cnt[SEL_MAX_CL];
+  uint32_t bin;                 // chosen bin of the current pass
+  uint32_t above;               // keys strictly above the chosen bin
+  union {
+    typename cub::BlockScan<uint32_t, BLOCK>::TempStorage scan32;
+    typename cub::BlockScan<unsigned long long, BLOCK>::TempStorage scan64;
+  };
 };
 
 template <int CL>
@@ -60,59 +66,73 @@ __device__ __forceinline__ int cl_rank() {
   }
 }
 
-// warp-aggregated shared-memory histogram increment (h may be another
-// cluster CTA's shared memory)
+// warp-aggregated histogram increment (shared or global memory).  Lanes are
+// grouped by target address, so lanes may update different histograms.
 __device__ __forceinline__ void hist_add(uint32_t *h, uint32_t bin) {
   const unsigned act = __activemask();
-  const unsigned peers = __match_any_sync(act, bin);
+  const unsigned peers = __match_any_sync(act, reinterpret_cast<unsigned long long>(h + bin));
   const int leader = __ffs(peers) - 1;
   if ((int)(threadIdx.x & 31) == leader) atomicAdd(&h[bin], (uint32_t)__popc(peers));
 }
 
 // Find the threshold key T of the k largest keys among all CTAs of the
-// cluster (k >= 1 and k <= total keys).  Every CTA returns the same T and
-// need_eq.  `keys` may point to shared or global memory.  With a cluster,
-// every CTA adds its counts into rank 0's histogram (shared::cluster
-// atomics, warp-aggregated); the three histograms rotate so that each pass
-// needs a single cluster barrier.
+// cluster (1 <= k <= total keys); every CTA returns the same T and need_eq.
+// `keys` may point to shared or global memory.  pre0, when given, is the
+// histogram of (key >> 21) over all keys of the selection (global memory),
+// built by the kernel that produced the keys; it replaces the first pass.
+// Later passes count only keys matching the known prefix -- a small set --
+// into this CTA's histogram; every CTA then reads the histograms of all
+// cluster ranks (one cluster barrier per pass).
 template <int BLOCK, int CL>
 __device__ void radix_threshold(const uint32_t *keys, int n_local, uint32_t k, SelectSmem<BLOCK> &sm,
                                 uint32_t &T, uint32_t &need_eq, const uint32_t *pre0 = nullptr) {
-  constexpr int IPT = SEL_BINS / BLOCK;
+  static_assert(SEL_BINS % BLOCK == 0 || BLOCK % SEL_BINS == 0, "block size");
+  constexpr int IPT = SEL_BINS >= BLOCK ? SEL_BINS / BLOCK : 1;
   uint32_t prefix = 0, pmask = 0, remaining = k;
   const int shifts[3] = {21, 10, 0};
-  const bool leader = cl_rank<CL>() == 0;
-  if (leader || CL == 1) {
-    for (int i = threadIdx.x; i < 3 * SEL_BINS; i += BLOCK) (&sm.hist[0][0])[i] = 0;
-  }
-  cl_sync<CL>();
 #pragma unroll 1
   for (int pass = 0; pass < 3; ++pass) {
-    const uint32_t *h = cl_map<CL>(sm.hist[pass], 0);
     const int sh = shifts[pass];
-    if (pass == 0 && pre0 != nullptr) {
-      h = pre0;   // the producer of the keys already built the first histogram
-    } else {
+    const bool from_pre = pass == 0 && pre0 != nullptr;
+    uint32_t *h = sm.hist[pass & 1];
+    if (!from_pre) {
+      for (int i = threadIdx.x; i < SEL_BINS; i += BLOCK) h[i] = 0;
+      __syncthreads();
       for (int i = threadIdx.x; i < n_local; i += BLOCK) {
         const uint32_t key = keys[i];
-        if ((key & pmask) == prefix) hist_add(cl_map<CL>(sm.hist[pass], 0), (key >> sh) & (SEL_BINS - 1));
+        if ((key & pmask) == prefix) {
+          const uint32_t bin = (key >> sh) & (SEL_BINS - 1);
+          if (pass == 0) hist_add(h, bin);      // every key: aggregate within the warp
+          else atomicAdd(&h[bin], 1u);           // few keys, spread bins
+        }
       }
       cl_sync<CL>();
     }
-    // totals, in descending bin order: item j of thread t is bin (SEL_BINS-1) - (t*IPT + j)
+    // totals in descending bin order: item j of thread t is bin (SEL_BINS-1) - (t*IPT + j)
     uint32_t items[IPT];
 #pragma unroll
-    for (int j = 0; j < IPT; ++j)
-      items[j] = (pass == 0 && pre0 != nullptr) ? __ldcg(h + SEL_BINS - 1 - (threadIdx.x * IPT + j))
-                                                : h[SEL_BINS - 1 - (threadIdx.x * IPT + j)];
+    for (int j = 0; j < IPT; ++j) {
+      const int idx = threadIdx.x * IPT + j;
+      uint32_t t = 0;
+      if (idx < SEL_BINS) {
+        const int bin = SEL_BINS - 1 - idx;
+        if (from_pre) {
+          t = __ldcg(pre0 + bin);
+        } else {
+#pragma unroll
+          for (int r = 0; r < CL; ++r) t += cl_map<CL>(h, r)[bin];
+        }
+      }
+      items[j] = t;
+    }
     uint32_t incl[IPT];
-    cub::BlockScan<uint32_t, BLOCK>(sm.scan).InclusiveSum(items, incl);
+    cub::BlockScan<uint32_t, BLOCK>(sm.scan32).InclusiveSum(items, incl);
 #pragma unroll
     for (int j = 0; j < IPT; ++j) {
-      const int bin = SEL_BINS - 1 - (threadIdx.x * IPT + j);
-      const uint32_t above = incl[j] - items[j];   // keys in bins > bin
-      if (above < remaining && incl[j] >= remaining) {
-        sm.bin = (uint32_t)bin;
+      const int idx = threadIdx.x * IPT + j;
+      const uint32_t above = incl[j] - items[j];   // keys in bins above this one
+      if (idx < SEL_BINS && above < remaining && incl[j] >= remaining) {
+        sm.bin = (uint32_t)(SEL_BINS - 1 - idx);
         sm.above = above;
       }
     }
@@ -128,13 +148,15 @@ __device__ void radix_threshold(const uint32_t *keys, int n_local, uint32_t k, S
 }
 
 // Emit the selected keys (key > T, plus the first need_eq keys == T in
-// cluster index order) in ascending index order.  `emit(local_index, out_pos)`
+// cluster index order) in ascending index order.  emit(local_index, out_pos)
 // is called once per selected key; out_pos counts over the whole cluster.
-// With take_all, every key is selected.
+// With take_all, every key is selected.  Each thread owns a contiguous
+// segment; one 64-bit block scan gives both counts before the thread, and the
+// CTAs exchange their totals in one cluster round trip.
 template <int BLOCK, int CL, typename Emit>
 __device__ void ordered_emit(const uint32_t *keys, int n_local, uint32_t T, uint32_t need_eq,
                              bool take_all, SelectSmem<BLOCK> &sm, Emit emit) {
-  using Scan = cub::BlockScan<uint32_t, BLOCK>;
+  using Scan = cub::BlockScan<unsigned long long, BLOCK>;
   const int seg = (n_local + BLOCK - 1) / BLOCK;
   const int lo = min(n_local, (int)threadIdx.x * seg);
   const int hi = min(n_local, lo + seg);
@@ -144,44 +166,24 @@ __device__ void ordered_emit(const uint32_t *keys, int n_local, uint32_t T, uint
     gt += (take_all || key > T) ? 1u : 0u;
     eq += (!take_all && key == T) ? 1u : 0u;
   }
-  uint32_t eq_before_thread, gt_before_thread, cta_gt, cta_eq;
-  Scan(sm.scan).ExclusiveSum(eq, eq_before_thread, cta_eq);
-  __syncthreads();
-  Scan(sm.scan).ExclusiveSum(gt, gt_before_thread, cta_gt);
-  if (threadIdx.x == 0) {
-    sm.cnt[0] = cta_gt;
-    sm.cnt[1] = cta_eq;
-  }
+  unsigned long long before, total;
+  Scan(sm.scan64).ExclusiveSum(((unsigned long long)gt << 32) | eq, before, total);
+  if (threadIdx.x == 0) sm.cnt = total;
   cl_sync<CL>();
-  // ranks before mine in the cluster
   const int me = cl_rank<CL>();
+  if ((int)threadIdx.x < CL) sm.rank_cnt[threadIdx.x] = *cl_map<CL>(&sm.cnt, (int)threadIdx.x);
+  __syncthreads();
   uint32_t eq_before_cta = 0, out_before_cta = 0;
   for (int r = 0; r < me; ++r) {
-    const uint32_t *c = cl_map<CL>(sm.cnt, r);
-    const uint32_t g = c[0], e = c[1];
-    const uint32_t take = (need_eq > eq_before_cta) ? min(e, need_eq - eq_before_cta) : 0u;
+    const uint32_t g = (uint32_t)(sm.rank_cnt[r] >> 32), e = (uint32_t)sm.rank_cnt[r];
+    const uint32_t take = need_eq > eq_before_cta ? min(e, need_eq - eq_before_cta) : 0u;
     out_before_cta += g + take;
     eq_before_cta += e;
   }
-  // selected count of this thread's segment
-  uint32_t eq_rank = eq_before_cta + eq_before_thread;
-  uint32_t mine = 0;
-  {
-    uint32_t er = eq_rank;
-    for (int i = lo; i < hi; ++i) {
-      const uint32_t key = keys[i];
-      if (take_all || key > T) {
-        ++mine;
-      } else if (key == T) {
-        if (er < need_eq) ++mine;
-        ++er;
-      }
-    }
-  }
-  uint32_t out_before_thread;
-  __syncthreads();
-  Scan(sm.scan).ExclusiveSum(mine, out_before_thread);
-  uint32_t pos = out_before_cta + out_before_thread;
+  const uint32_t gt_before = (uint32_t)(before >> 32), eq_before = (uint32_t)before;
+  const uint32_t room = need_eq > eq_before_cta ? need_eq - eq_before_cta : 0u;
+  uint32_t pos = out_before_cta + gt_before + min(eq_before, room);
+  uint32_t eq_rank = eq_before_cta + eq_before;
   for (int i = lo; i < hi; ++i) {
     const uint32_t key = keys[i];
     bool s = false;
