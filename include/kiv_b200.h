@@ -64,6 +64,7 @@ typedef int32_t kiv_status;
 #define KIV_ST_COARSE_SUM 9  /* double: sum of all coarse scores of the last pass */
 #define KIV_ST_FINE_MAX 10   /* key of the largest fine (max over heads) score */
 #define KIV_ST_FINE_SUM 11   /* double: sum of the fine scores of all candidates */
+#define KIV_ST_UNION_PENDING 12  /* 1: the page marks hold a new union the fine pass must read */
 /* words 16..31 are kernel-private counters */
 
 /* Error bits a kernel sets in state[KIV_ST_ERROR] instead of writing out of bounds. */
@@ -116,7 +117,7 @@ KIV_API size_t kiv_workspace_bytes(const kiv_store *st, const kiv_query *q);
 
 /* Byte offsets of the workspace sub-buffers, for inspection by the host:
  * out[0] scores (R x np_cap float, coarse scores of the last pass),
- * out[1] page flags, out[2] union pages (int32, KIV_ST_UNION valid entries),
+ * out[1] page marks (bitmap), out[2] union pages (int32, KIV_ST_UNION valid entries),
  * out[3] fine keys (B x c_cap uint32, order-preserving keys of the max
  * scores), out[4] per-row selected counts (int32 [B]), out[5] attention
  * partials; out[6..9] = R, np_cap, u_cap, c_cap. */

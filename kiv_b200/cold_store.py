@@ -364,13 +364,6 @@ class ColdKVStore:
                                               ws.numel(), None, None, s), "coarse_select")
             else:
                 self._sharded_coarse(desc, qd, ws, B * Hq * Q, top_pages, s)
-            if self.num_pages > 0:
-                uni = ws[lay[2]:lay[2] + 4 * lay[8]].view(torch.int32)
-                self._telemetry.record_coarse(state=self._state, union=uni, num_pages=self.num_pages,
-                                              cold_length=self._cold_len,
-                                              n_scores=B * Hq * Q * self._local_pages(self.num_pages))
-            else:
-                self._telemetry.record_coarse_skipped(cold_length=self._cold_len)
             marker = self._buffer("marker", (B, 0), torch.int8)
             self._cached_candidate_k = marker
             self._cached_candidate_v = marker
@@ -394,6 +387,15 @@ class ColdKVStore:
             sel_local = sel
         else:
             sel_local = self._sharded_fine(desc, qd, ws, B, top_p, sel, s)
+        if not reuse:
+            # the fine scorer materializes the page union the coarse pass marked
+            if self.num_pages > 0:
+                uni = ws[lay[2]:lay[2] + 4 * lay[8]].view(torch.int32)
+                self._telemetry.record_coarse(state=self._state, union=uni, num_pages=self.num_pages,
+                                              cold_length=self._cold_len,
+                                              n_scores=B * Hq * Q * self._local_pages(self.num_pages))
+            else:
+                self._telemetry.record_coarse_skipped(cold_length=self._cold_len)
         return sel, sel_local, ws, qd
 
     def _record_fine(self, sel: torch.Tensor, P: int | None, top_p: int) -> None:

@@ -48,7 +48,7 @@ Workspace workspace_layout(const kiv_store *st, const kiv_query *q, void *base) 
     return r;
   };
   w.scores = reinterpret_cast<float *>(take(w.R * w.np_cap * 4));
-  w.flags = reinterpret_cast<uint8_t *>(take(w.np_cap));
+  w.pbits = reinterpret_cast<uint32_t *>(take(ceil_div(w.np_cap, 32) * 4));
   w.uni = reinterpret_cast<int32_t *>(take(w.u_cap * 4));
   w.agg = reinterpret_cast<uint32_t *>(take((int64_t)st->batch * w.c_cap * 4));
   w.selcnt = reinterpret_cast<int32_t *>(take((int64_t)st->batch * 4));
@@ -164,7 +164,7 @@ kiv_status kiv_workspace_layout(const kiv_store *st, const kiv_query *q, int64_t
   const Workspace w = workspace_layout(st, q, reinterpret_cast<void *>(0x100));
   const auto off = [](const void *p) { return (int64_t)(reinterpret_cast<uintptr_t>(p) - 0x100); };
   out[0] = off(w.scores);
-  out[1] = off(w.flags);
+  out[1] = off(w.pbits);
   out[2] = off(w.uni);
   out[3] = off(w.agg);
   out[4] = off(w.selcnt);

@@ -43,7 +43,6 @@ __device__ __forceinline__ float *sc_out_slot(float *ored, int pairs, int ksub, 
 template <typename T, int LPR, int VPL, int RCH>
 __global__ void __launch_bounds__(AT_THREADS)
 attend_split_kernel(AttnArgs<T> a) {
-  griddep_wait();
   extern __shared__ __align__(128) uint8_t at_smem[];
   __shared__ uint64_t bars[AT_STAGES];
   __shared__ float s_m[RCH], s_l[RCH], s_alpha[RCH];
@@ -68,10 +67,46 @@ attend_split_kernel(AttnArgs<T> a) {
   const int bh = rest / nchunks;
   const int b = bh / H, kvh = bh % H;
 
+  // ---- prologue: inputs written before the retrieval's first kernel (the
+  // hot window state, the query); with programmatic dependent launch it
+  // overlaps the selection kernel's tail
   const int64_t hot_len = st_ld(st.state, KIV_ST_HOT_LEN);
   const int64_t hot_start = st_ld(st.state, KIV_ST_HOT_START);
   const int64_t hot_lo = hot_len * a.hot_slice / a.hot_slices;
   const int64_t hot_hi = hot_len * (a.hot_slice + 1) / a.hot_slices;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < AT_STAGES; ++s) mbar_init(&bars[s], 1);
+    mbar_fence_init();
+    s_fail = 0;
+  }
+  if (threadIdx.x < RCH) {
+    s_m[threadIdx.x] = -INFINITY;
+    s_l[threadIdx.x] = 0.f;
+  }
+  // query rows of this chunk (fp32 registers)
+  const T *qb = reinterpret_cast<const T *>(q.q);
+  int row_h[RCH], row_t[RCH];
+  RowDot<T, LPR, VPL, RCH> dot;
+  {
+    const T *qrows[RCH];
+#pragma unroll
+    for (int r = 0; r < RCH; ++r) {
+      const int rr = ch * RCH + r;
+      if (rr < rows_kv) {
+        row_h[r] = kvh * G + rr / Q;
+        row_t[r] = rr % Q;
+        qrows[r] = qb + b * q.stride_b + row_h[r] * q.stride_h + row_t[r] * q.stride_t;
+      } else {
+        row_h[r] = -1;
+        row_t[r] = 0;
+        qrows[r] = nullptr;
+      }
+    }
+    dot.load_query(qrows, g, nv, 1.0f);
+  }
+  __syncthreads();
+  // ---- the selection (previous kernel) is needed from here on
+  griddep_wait();
   const int64_t ncold = a.w.selcnt[b];
   const int64_t nkeys = ncold + (hot_hi - hot_lo);
   int64_t kps = (nkeys + a.n_split - 1) / a.n_split;
@@ -121,41 +156,8 @@ attend_split_kernel(AttnArgs<T> a) {
       bulk_g2s(vt + ((size_t)stage * ATT_TILE + lane) * D, pv, row_bytes, &bars[stage]);
     }
   };
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < AT_STAGES; ++s) mbar_init(&bars[s], 1);
-    mbar_fence_init();
-    s_fail = 0;
-  }
-  if (threadIdx.x < RCH) {
-    s_m[threadIdx.x] = -INFINITY;
-    s_l[threadIdx.x] = 0.f;
-  }
-  __syncthreads();
   if (warp == 0) {
     for (int t = 0; t < (ntile < AT_STAGES ? ntile : AT_STAGES); ++t) issue(t);
-  }
-
-  // query rows of this chunk (scaled by `scaling` in fp32 registers)
-  const T *qb = reinterpret_cast<const T *>(q.q);
-  int row_h[RCH], row_t[RCH];
-  RowDot<T, LPR, VPL, RCH> dot;
-  {
-    const T *qrows[RCH];
-#pragma unroll
-    for (int r = 0; r < RCH; ++r) {
-      const int rr = ch * RCH + r;
-      if (rr < rows_kv) {
-        row_h[r] = kvh * G + rr / Q;
-        row_t[r] = rr % Q;
-        qrows[r] = qb + b * q.stride_b + row_h[r] * q.stride_h + row_t[r] * q.stride_t;
-      } else {
-        row_h[r] = -1;
-        row_t[r] = 0;
-        qrows[r] = nullptr;
-      }
-    }
-    dot.load_query(qrows, g, nv, 1.0f);
   }
 
   // P.V mapping: thread -> (vector dv, row r, key subset ks)
@@ -398,7 +400,8 @@ static void launch_combine(const float *part, int64_t row_stride, int64_t pstrid
   const size_t smem = (size_t)(((n + 3) & ~3) + (CB_THREADS / 32) * D) * sizeof(float);
   auto kern = combine_kernel<T>;
   if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  kern<<<(unsigned)rows, CB_THREADS, smem, s>>>(part, row_stride, pstride, n, D, Hq, Q, final_out, merged);
+  launch_pdl(kern, dim3((unsigned)rows), dim3(CB_THREADS), smem, s, 1, part, row_stride, pstride, n, D, Hq, Q,
+             final_out, merged);
 }
 
 template <typename T>
@@ -440,8 +443,7 @@ static kiv_status launch_at(const AttnArgs<T> &a, cudaStream_t s) {
   const int64_t nchunks = ceil_div(rows_kv, RCH);
   const int64_t grid = (int64_t)a.st.batch * H * nchunks * a.n_split;
   if (grid > 0x7fffffff) return KIV_ERR_ARG;
-  kern<<<(unsigned)grid, AT_THREADS, smem, s>>>(a);
-  return cuda_status(cudaGetLastError(), "attend_split");
+  return cuda_status(launch_pdl(kern, dim3((unsigned)grid), dim3(AT_THREADS), smem, s, 1, a), "attend_split");
 }
 
 template <typename T>
@@ -482,10 +484,11 @@ static kiv_status attend_t(const kiv_store *st, const kiv_query *q, const kiv_ma
   const int rows_kv = (q->num_query_heads / H) * q->query_len;
   const int64_t nchunks = ceil_div(rows_kv, rows_kv <= 4 ? 4 : 8);
   const int64_t base = (int64_t)st->batch * H * nchunks;
-  // splits of >= 64 keys (two tiles) each, about one CTA per SM in total
+  // one tile of keys per split where the SMs allow it (at most about one CTA
+  // per SM in total): each CTA then waits for a single round of row copies
   const int64_t keys_hint = std::max<int64_t>(1, (int64_t)q->top_p + expected_hot);
   a.n_split = (int)std::max<int64_t>(
-      1, std::min<int64_t>({w.split_cap, ceil_div(keys_hint, 2 * ATT_TILE), ceil_div(sm_count(), base)}));
+      1, std::min<int64_t>({w.split_cap, ceil_div(keys_hint, ATT_TILE), ceil_div(sm_count(), base)}));
   kiv_status rc = dispatch_at<T>(a, s);
   if (rc != KIV_OK) return rc;
   const int64_t rows = w.R;
@@ -542,14 +545,16 @@ kiv_status launch_gather(const kiv_store *st, const int32_t *sel, int32_t sel_st
   const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(ceil_div(total, 256), (int64_t)sm_count() * 8));
   switch (st->dtype) {
     case KIV_DTYPE_F32:
-      gather_kernel<float><<<(unsigned)grid, 256, 0, s>>>(*st, sel, sel_stride, P, (float *)ok, (float *)ov);
+      launch_pdl(gather_kernel<float>, dim3((unsigned)grid), dim3(256), 0, s, 1, *st, sel, sel_stride, P,
+                 (float *)ok, (float *)ov);
       break;
     case KIV_DTYPE_BF16:
-      gather_kernel<__nv_bfloat16><<<(unsigned)grid, 256, 0, s>>>(*st, sel, sel_stride, P,
+      launch_pdl(gather_kernel<__nv_bfloat16>, dim3((unsigned)grid), dim3(256), 0, s, 1, *st, sel, sel_stride, P,
                                                                   (__nv_bfloat16 *)ok, (__nv_bfloat16 *)ov);
       break;
     case KIV_DTYPE_F16:
-      gather_kernel<__half><<<(unsigned)grid, 256, 0, s>>>(*st, sel, sel_stride, P, (__half *)ok, (__half *)ov);
+      launch_pdl(gather_kernel<__half>, dim3((unsigned)grid), dim3(256), 0, s, 1, *st, sel, sel_stride, P,
+                 (__half *)ok, (__half *)ov);
       break;
     default:
       return KIV_ERR_UNSUPPORTED;

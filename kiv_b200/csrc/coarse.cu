@@ -18,8 +18,11 @@ namespace kiv {
 
 constexpr int CS_THREADS = 128;      // coarse scoring
 constexpr int CS_PAGES = 16;         // pages per work item (one bulk copy)
-constexpr int TK_THREADS = 1024;     // per-row top-k
+constexpr int TK_THREADS = 512;      // per-row top-k
+constexpr int TK_BND = 1024;         // boundary-bin capacity of the candidate select
+constexpr int TK_SCAP = 16384;       // scores of a row staged in shared memory
 constexpr int CM_THREADS = 256;      // merge of gathered per-row lists
+constexpr int UN_THREADS = 1024;     // page union from the page marks
 
 // local finalized pages of this shard given the global finalized count
 __device__ __forceinline__ int64_t local_pages(int64_t np_global, int rank, int n) {
@@ -49,6 +52,7 @@ coarse_scores_kernel(kiv_store st, kiv_query q, Workspace w) {
   const int nchunks = (rows_kv + RCH - 1) / RCH;
   const int64_t np_global = st_ld(st.state, KIV_ST_COLD_LEN) / S;
   const int64_t np = local_pages(np_global, st.shard_rank, st.shard_count);
+  clear_stale_marks(st, w, np);
   const int64_t nblk = (np + CS_PAGES - 1) / CS_PAGES;
   const int64_t items = (int64_t)st.batch * H * nchunks * nblk;
   const T *qb = reinterpret_cast<const T *>(q.q);
@@ -133,66 +137,135 @@ coarse_scores_kernel(kiv_store st, kiv_query q, Workspace w) {
     atomicOr(reinterpret_cast<unsigned long long *>(st.state + KIV_ST_ERROR), (unsigned long long)KIV_ERRBIT_WAIT_TIMEOUT);
 }
 
-// Per-row top-k.  shard_count == 1: mark pages and let the last block build
-// the union.  shard_count > 1: write the row's local list (score, page id).
+// Per-row top-k.  The scorer left each row's first-pass histogram (bins of
+// key >> 21) in w.chist; only pages in bins at or above the threshold bin are
+// compacted and resolved (select_candidates).  shard_count == 1: mark the
+// selected pages in w.pbits (the fine pass builds the sorted union from
+// them).  shard_count > 1: write the row's local list (score, page id) in
+// page order for the all-gather.
 __global__ void __launch_bounds__(TK_THREADS)
-coarse_topk_kernel(kiv_store st, kiv_query q, Workspace w, float *row_scores, int32_t *row_pages) {
-  griddep_wait();
+coarse_topk_kernel(kiv_store st, kiv_query q, Workspace w, float *row_scores, int32_t *row_pages, int cap,
+                   int scap) {
   extern __shared__ uint4 dyn_smem[];
-  __shared__ SelectSmem<TK_THREADS> sm;
+  __shared__ __align__(16) CandSmem<TK_THREADS> cs;
+  __shared__ SelectSmem<TK_THREADS> rs;
+  __shared__ uint64_t bar;
+  __shared__ int s_fail;
+  uint32_t *ckey = reinterpret_cast<uint32_t *>(dyn_smem);
+  int32_t *cidx = reinterpret_cast<int32_t *>(ckey + cap);
+  uint32_t *bkey = reinterpret_cast<uint32_t *>(cidx + cap);
+  int32_t *bidx = reinterpret_cast<int32_t *>(bkey + TK_BND);
+  int32_t *sel_ci = bidx + TK_BND;                 // [top_pages, padded to 4] chosen candidates
+  float *sscore = reinterpret_cast<float *>(sel_ci + ((q.top_pages + 3) & ~3));   // [scap] staged scores
+  uint8_t *flag = reinterpret_cast<uint8_t *>(sscore + scap);
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    mbar_fence_init();
+    s_fail = 0;
+  }
+  __syncthreads();
+  griddep_wait();
   const int S = st.page_size;
   const int64_t np_global = st_ld(st.state, KIV_ST_COLD_LEN) / S;
   const int64_t np = local_pages(np_global, st.shard_rank, st.shard_count);
   const int row = blockIdx.x;
   const int K = q.top_pages;
-  if (np > 0) {
-    // stage this row's keys in shared memory (converted from float bits)
-    uint32_t *keys = reinterpret_cast<uint32_t *>(dyn_smem);
-    const float *src = w.scores + (int64_t)row * w.np_cap;
-    for (int64_t i = threadIdx.x; i < np; i += TK_THREADS) keys[i] = f2key(src[i]);
-    __syncthreads();
-    const uint32_t k = (uint32_t)(K < np ? (int64_t)K : np);
-    uint32_t T = 0, need = 0;
-    const bool all = (int64_t)k >= np;
-    if (!all) radix_threshold<TK_THREADS, 1>(keys, (int)np, k, sm, T, need, w.chist + (int64_t)row * SEL_BINS);
-    const int rank = st.shard_rank, nsh = st.shard_count;
+  const int rank = st.shard_rank, nsh = st.shard_count;
+  const uint32_t *pre = w.chist + (int64_t)row * SEL_BINS;
+  float *src = w.scores + (int64_t)row * w.np_cap;
+  float *ls = row_scores ? row_scores + (int64_t)row * K : nullptr;
+  int32_t *lpg = row_pages ? row_pages + (int64_t)row * K : nullptr;
+  auto emit_page = [&](int64_t lp, uint32_t pos, uint32_t key) {
     if (nsh == 1) {
-      ordered_emit<TK_THREADS, 1>(keys, (int)np, T, need, all, sm,
-                                  [&](int i, uint32_t) { w.flags[i] = 1; });
-    } else {
-      float *ls = row_scores + (int64_t)row * K;
-      int32_t *lpg = row_pages + (int64_t)row * K;
-      ordered_emit<TK_THREADS, 1>(keys, (int)np, T, need, all, sm, [&](int i, uint32_t pos) {
-        ls[pos] = key2f(keys[i]);
-        lpg[pos] = (int32_t)((int64_t)i * nsh + rank);
-      });
-      for (int j = (int)k + threadIdx.x; j < K; j += TK_THREADS) {
-        ls[j] = 0.f;
-        lpg[j] = -1;
-      }
+      atomicOr(&w.pbits[lp >> 5], 1u << (lp & 31));
+    } else if (pos < (uint32_t)K) {
+      ls[pos] = key2f(key);
+      lpg[pos] = (int32_t)(lp * nsh + rank);
     }
-  } else if (st.shard_count > 1) {
-    for (int j = threadIdx.x; j < K; j += TK_THREADS) {
-      row_scores[(int64_t)row * K + j] = 0.f;
-      row_pages[(int64_t)row * K + j] = -1;
+  };
+  const uint32_t k = (uint32_t)(K < np ? (int64_t)K : np);
+  // inputs -> shared memory in one round trip: the row's histogram and scores
+  const bool staged = np > 0 && np <= scap && (reinterpret_cast<uintptr_t>(src) & 15) == 0;
+  if (threadIdx.x == 0 && np > 0) {
+    const uint32_t sb = staged ? (uint32_t)((np * 4 + 15) & ~15ll) : 0u;
+    mbar_arrive_tx(&bar, SEL_BINS * 4 + sb);
+    bulk_g2s(cs.hist, pre, SEL_BINS * 4, &bar);
+    if (sb) bulk_g2s(sscore, src, sb, &bar);
+  }
+  if (np > 0 && !mbar_wait_bounded(&bar, 0)) s_fail = 1;
+  auto score_at = [&](int64_t i) { return staged ? sscore[i] : __ldcg(src + i); };
+  if (np > 0 && (int64_t)k >= np) {
+    for (int64_t i = threadIdx.x; i < np; i += TK_THREADS) emit_page(i, (uint32_t)i, f2key(score_at(i)));
+  } else if (np > 0) {
+    find_bin<TK_THREADS>(k, cs, [&](int b) { return cs.hist[b]; });
+    const uint32_t b0 = cs.bin, need0 = k - cs.above;
+    __syncthreads();
+    const int n = ordered_compact<TK_THREADS>(
+        (int)np, [&](int i) { return f2key(score_at(i)); },
+        [&](uint32_t key) { return (key >> 21) >= b0; }, ckey, cidx, 0, cap, cs);
+    if (n <= cap) {
+      select_candidates<TK_THREADS>(ckey, n, b0, need0, bkey, bidx, flag, TK_BND, cs, rs,
+                                    [&](int ci, uint32_t pos) {
+                                      if (pos < k) sel_ci[pos] = ci;
+                                    });
+      __syncthreads();
+      for (int p = threadIdx.x; p < (int)k; p += TK_THREADS) {
+        const int ci = sel_ci[p];
+        emit_page(cidx[ci], (uint32_t)p, ckey[ci]);
+      }
+    } else {
+      // too many candidates for shared memory: exact radix select over the
+      // row in global memory (keys written in place of the scores)
+      uint32_t *gk = reinterpret_cast<uint32_t *>(src);
+      for (int64_t i = threadIdx.x; i < np; i += TK_THREADS) gk[i] = f2key(src[i]);
+      __syncthreads();
+      uint32_t T = 0, need = 0;
+      radix_threshold<TK_THREADS, 1>(gk, (int)np, k, rs, T, need, pre);
+      ordered_emit<TK_THREADS, 1>(gk, (int)np, T, need, false, rs,
+                                  [&](int i, uint32_t pos) { emit_page(i, pos, gk[i]); });
     }
   }
-  // the scorer's histogram of this row has been used: clear it for the next pass
+  if (nsh > 1) {
+    for (int j = (int)k + threadIdx.x; j < K; j += TK_THREADS) {
+      ls[j] = 0.f;
+      lpg[j] = -1;
+    }
+  }
+  // this row's first-pass histogram has been used: clear it for the next pass
   __syncthreads();
   for (int i = threadIdx.x; i < SEL_BINS; i += TK_THREADS) w.chist[(int64_t)row * SEL_BINS + i] = 0;
-  if (last_block(reinterpret_cast<unsigned long long *>(st.state + CTR_COARSE), gridDim.x)) {
-    if (st.shard_count == 1) {
-      const int64_t u = compact_flags<TK_THREADS>(w.flags, np, w.uni, w.u_cap, 1, 0, sm.scan32);
-      if (threadIdx.x == 0) st.state[KIV_ST_UNION] = u;
-    }
-    if (threadIdx.x == 0) {
-      const unsigned long long mk = w.cstat[0], sb = w.cstat[1];
-      if (mk) atomicMax(reinterpret_cast<unsigned long long *>(st.state + KIV_ST_COARSE_MAX), mk);
-      atomicAdd(reinterpret_cast<double *>(st.state + KIV_ST_COARSE_SUM), __longlong_as_double((long long)sb));
-      w.cstat[0] = 0;
-      w.cstat[1] = 0;
-    }
+  if (row == 0 && threadIdx.x == 0) {
+    if (nsh == 1) st.state[KIV_ST_UNION_PENDING] = 1;
+    const unsigned long long mk = w.cstat[0], sb = w.cstat[1];
+    if (mk) atomicMax(reinterpret_cast<unsigned long long *>(st.state + KIV_ST_COARSE_MAX), mk);
+    atomicAdd(reinterpret_cast<double *>(st.state + KIV_ST_COARSE_SUM), __longlong_as_double((long long)sb));
+    w.cstat[0] = 0;
+    w.cstat[1] = 0;
   }
+  if (s_fail && threadIdx.x == 0)
+    atomicOr(reinterpret_cast<unsigned long long *>(st.state + KIV_ST_ERROR), (unsigned long long)KIV_ERRBIT_WAIT_TIMEOUT);
+}
+
+// Sorted page union from the marks the coarse pass set (single CTA): used
+// ahead of the scorers that do not build it themselves.  Clears the marks and
+// the pending word; a no-op when no coarse pass is pending (reused union).
+__global__ void __launch_bounds__(UN_THREADS) union_kernel(kiv_store st, Workspace w) {
+  griddep_wait();
+  __shared__ int wsum[UN_THREADS / 32];
+  if (st_ld(st.state, KIV_ST_UNION_PENDING) == 0) return;
+  const int64_t np_global = st_ld(st.state, KIV_ST_COLD_LEN) / st.page_size;
+  const int64_t np = local_pages(np_global, st.shard_rank, st.shard_count);
+  const int u = union_from_bits<UN_THREADS, false>(w.pbits, np, w.uni, (int)w.u_cap, st.shard_rank,
+                                                   st.shard_count, wsum);
+  for (int64_t i = threadIdx.x; i < (np + 31) / 32; i += UN_THREADS) w.pbits[i] = 0;
+  if (threadIdx.x == 0) {
+    st.state[KIV_ST_UNION] = u;
+    st.state[KIV_ST_UNION_PENDING] = 0;
+  }
+}
+
+kiv_status launch_union(const kiv_store *st, const Workspace &w, cudaStream_t s) {
+  return cuda_status(launch_pdl(union_kernel, dim3(1), dim3(UN_THREADS), 0, s, 1, *st, w), "union");
 }
 
 // Merge gathered per-row lists [n][R][K] into the global per-row top-k and
@@ -234,15 +307,13 @@ coarse_merge_kernel(kiv_store st, kiv_query q, Workspace w, const float *ls, con
         take = rank < need;
       }
       if (take && ids[i] >= 0 && (ids[i] % st.shard_count) == st.shard_rank)
-        w.flags[ids[i] / st.shard_count] = 1;
+      {
+        const int32_t lp = ids[i] / st.shard_count;
+        atomicOr(&w.pbits[lp >> 5], 1u << (lp & 31));
+      }
     }
   }
-  if (last_block(reinterpret_cast<unsigned long long *>(st.state + CTR_MERGE), gridDim.x)) {
-    const int64_t np = local_pages(np_global, st.shard_rank, st.shard_count);
-    const int64_t u = compact_flags<CM_THREADS>(w.flags, np, w.uni, w.u_cap, st.shard_count,
-                                                st.shard_rank, sm.scan32);
-    if (threadIdx.x == 0) st.state[KIV_ST_UNION] = u;
-  }
+  if (row == 0 && threadIdx.x == 0) st.state[KIV_ST_UNION_PENDING] = 1;
 }
 
 template <typename T, int LPR, int VPL, int RCH>
@@ -253,7 +324,8 @@ static void launch_cs(const kiv_store *st, const kiv_query *q, const Workspace &
   const int64_t items = (int64_t)st->batch * H * nchunks * ceil_div(w.np_cap, CS_PAGES);
   const int64_t grid = std::min<int64_t>(std::max<int64_t>(items, 1), (int64_t)sm_count() * 8);
   const size_t smem = (size_t)CS_PAGES * st->head_dim * sizeof(T);
-  coarse_scores_kernel<T, LPR, VPL, RCH><<<(unsigned)grid, CS_THREADS, smem, s>>>(*st, *q, w);
+  launch_pdl(coarse_scores_kernel<T, LPR, VPL, RCH>, dim3((unsigned)grid), dim3(CS_THREADS), smem, s, 1, *st, *q,
+             w);
 }
 
 template <typename T>
@@ -290,14 +362,22 @@ kiv_status launch_coarse(const kiv_store *st, const kiv_query *q, const Workspac
     default: rc = KIV_ERR_UNSUPPORTED;
   }
   if (rc != KIV_OK) return rc;
-  const size_t smem = (size_t)w.np_cap * sizeof(uint32_t);
-  if (smem > 200 * 1024) {
-    set_error("coarse: %lld pages per shard exceed the shared-memory select (max %d)",
-              (long long)w.np_cap, 200 * 1024 / 4);
+  if (q->top_pages > 8192) {
+    set_error("coarse: top_pages %d exceeds the shared-memory select (max 8192)", q->top_pages);
     return KIV_ERR_CAPACITY;
   }
+  // candidate buffer (key + index + flag per page), the boundary scratch, the
+  // chosen list and the staged scores of the row
+  const int64_t np_pad = align_up(w.np_cap, 16);
+  const int scap = (int)std::min<int64_t>(np_pad, TK_SCAP);
+  const int64_t fixed = 8 * TK_BND + 4 * align_up(q->top_pages, 4) + 4 * (int64_t)scap;
+  const int64_t room = (176 * 1024 - fixed) / 9;
+  const int cap = std::max(16, (int)std::min<int64_t>(np_pad, room & ~15ll));
+  const size_t smem = (size_t)cap * 9 + (size_t)fixed;
   cudaFuncSetAttribute(coarse_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  coarse_topk_kernel<<<(unsigned)w.R, TK_THREADS, smem, s>>>(*st, *q, w, row_scores, row_pages);
+  const cudaError_t e = launch_pdl(coarse_topk_kernel, dim3((unsigned)w.R), dim3(TK_THREADS), smem, s, 1, *st, *q,
+                                   w, row_scores, row_pages, cap, scap);
+  if (e != cudaSuccess) return cuda_status(e, "coarse_topk");
   return cuda_status(cudaGetLastError(), "coarse");
 }
 
@@ -306,7 +386,9 @@ kiv_status launch_coarse_merge(const kiv_store *st, const kiv_query *q, const Wo
   const size_t smem = (size_t)n * q->top_pages * (sizeof(uint32_t) + sizeof(int32_t));
   if (smem > 200 * 1024) return KIV_ERR_CAPACITY;
   cudaFuncSetAttribute(coarse_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  coarse_merge_kernel<<<(unsigned)w.R, CM_THREADS, smem, s>>>(*st, *q, w, ls, lp, n);
+  const cudaError_t e = launch_pdl(coarse_merge_kernel, dim3((unsigned)w.R), dim3(CM_THREADS), smem, s, 1, *st,
+                                   *q, w, ls, lp, n);
+  if (e != cudaSuccess) return cuda_status(e, "coarse_merge");
   return cuda_status(cudaGetLastError(), "coarse_merge");
 }
 

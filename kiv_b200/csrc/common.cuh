@@ -243,9 +243,11 @@ __device__ __forceinline__ bool last_block(unsigned long long *ctr, unsigned lon
   return s_last != 0;
 }
 
-// programmatic dependent launch: wait for the preceding kernel's results.
+// programmatic dependent launch: wait for the preceding kernel's results,
+// then let the next kernel in the stream start its prologue.
 __device__ __forceinline__ void griddep_wait() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 __device__ __forceinline__ void griddep_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");

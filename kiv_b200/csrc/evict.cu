@@ -146,16 +146,16 @@ kiv_status launch_append_evict(const kiv_store *st, const void *k_new, const voi
   }
   switch (st->dtype) {
     case KIV_DTYPE_F32:
-      append_evict_kernel<float><<<(unsigned)blocks, EV_THREADS, 0, s>>>(
+      launch_pdl(append_evict_kernel<float>, dim3((unsigned)blocks), dim3(EV_THREADS), 0, s, 1,
           *st, (const float *)k_new, (const float *)v_new, sb, sh, stt, n_new, keep, n_evict_max, (int)ppb, (int)apb);
       break;
     case KIV_DTYPE_BF16:
-      append_evict_kernel<__nv_bfloat16><<<(unsigned)blocks, EV_THREADS, 0, s>>>(
+      launch_pdl(append_evict_kernel<__nv_bfloat16>, dim3((unsigned)blocks), dim3(EV_THREADS), 0, s, 1,
           *st, (const __nv_bfloat16 *)k_new, (const __nv_bfloat16 *)v_new, sb, sh, stt, n_new, keep,
           n_evict_max, (int)ppb, (int)apb);
       break;
     case KIV_DTYPE_F16:
-      append_evict_kernel<__half><<<(unsigned)blocks, EV_THREADS, 0, s>>>(
+      launch_pdl(append_evict_kernel<__half>, dim3((unsigned)blocks), dim3(EV_THREADS), 0, s, 1,
           *st, (const __half *)k_new, (const __half *)v_new, sb, sh, stt, n_new, keep, n_evict_max,
           (int)ppb, (int)apb);
       break;

@@ -23,7 +23,11 @@ namespace kiv {
 constexpr int FS_THREADS = 256;
 constexpr int FS_STAGES = 4;
 constexpr int FS_TILE_BYTES = 16384;
-constexpr int SL_THREADS = 1024;
+constexpr int SL_THREADS = 512;
+constexpr int SL_BND = 1024;      // boundary-bin capacity of the candidate select
+constexpr int SL_CAP = 4096;      // candidates resolved in rank 0's shared memory
+constexpr int SL_UCAP = 4096;     // union pages staged in shared memory
+constexpr int SL_KCAP = 16384;    // keys per CTA staged in shared memory
 constexpr int FM_THREADS = 512;
 
 struct FineGeom {
@@ -233,60 +237,162 @@ fine_scores_kernel(kiv_store st, kiv_query q, Workspace w, int tr, int stage_q) 
 }
 
 // One cluster of CL CTAs per batch row: exact top-P over the C candidates.
+// The scorer left the row's first-pass histogram (key >> 21) in w.fhist, so
+// the threshold bin b0 is known up front.  Right after the dependency wait
+// one bulk copy per input brings the histogram, this CTA's index range of
+// keys and (rank 0) the union pages into shared memory, so the kernel pays
+// one memory round trip for its inputs.  Each CTA compacts its keys in bins
+// >= b0 (index order), the CTAs exchange their counts, push their candidates
+// into rank 0's shared memory, and rank 0 resolves the top P among them
+// (select_candidates).  When the candidates do not fit, the cluster runs the
+// full radix select over the keys instead.
 // shard_count == 1: sel[b, :P] = selected token ids (ascending).
 // shard_count > 1: sel / scores hold this shard's local list (tail -1).
 template <int CL>
 __global__ void __launch_bounds__(SL_THREADS)
-fine_select_kernel(kiv_store st, kiv_query q, Workspace w, int32_t *sel, float *scores,
-                   int chunk_cap) {
-  griddep_wait();
+fine_select_kernel(kiv_store st, kiv_query q, Workspace w, int32_t *sel, float *scores, int cap, int ucap,
+                   int kcap) {
   extern __shared__ uint4 sl_dyn[];
+  __shared__ __align__(16) CandSmem<SL_THREADS> cs;
   __shared__ SelectSmem<SL_THREADS> sm;
+  __shared__ int s_cnt;
+  __shared__ int s_fail;
+  __shared__ uint64_t bar;
+  uint32_t *ckey = reinterpret_cast<uint32_t *>(sl_dyn);
+  int32_t *cidx = reinterpret_cast<int32_t *>(ckey + cap);
+  uint32_t *bkey = reinterpret_cast<uint32_t *>(cidx + cap);
+  int32_t *bidx = reinterpret_cast<int32_t *>(bkey + SL_BND);
+  int32_t *sel_ci = bidx + SL_BND;                        // [cap] chosen candidates
+  int32_t *suni = sel_ci + cap;                            // [ucap] union pages (staged)
+  uint32_t *skey = reinterpret_cast<uint32_t *>(suni + ucap);   // [kcap] this CTA's keys (staged)
+  uint8_t *flag = reinterpret_cast<uint8_t *>(skey + kcap);
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    mbar_fence_init();
+    s_fail = 0;
+  }
+  __syncthreads();
+  griddep_wait();
   const int b = blockIdx.x / CL;
   const int r = cl_rank<CL>();
   const int S = st.page_size;
   const FineGeom f = fine_geom(st);
   const int64_t C = f.U * S + (f.part_owned ? f.partial : 0);
-  const int64_t chunk = (C + CL - 1) / CL;
+  const int64_t chunk = ((C + CL - 1) / CL + 15) / 16 * 16;
   const int64_t lo = std::min<int64_t>(C, r * chunk);
   const int n_local = (int)(std::min<int64_t>(C, lo + chunk) - lo);
   const uint32_t *src = w.agg + (int64_t)b * w.c_cap + lo;
-  const uint32_t *keys = src;
-  if (chunk <= chunk_cap) {
-    uint32_t *sk = reinterpret_cast<uint32_t *>(sl_dyn);
-    for (int i = threadIdx.x; i < n_local; i += SL_THREADS) sk[i] = src[i];
-    keys = sk;
-    __syncthreads();
-  }
   const int64_t P = std::min<int64_t>(q.top_p, C);
   const bool all = P >= C;
-  uint32_t T = 0, need = 0;
   uint32_t *hb = w.fhist + (int64_t)b * SEL_BINS;
-  if (P > 0 && !all) radix_threshold<SL_THREADS, CL>(keys, n_local, (uint32_t)P, sm, T, need, hb);
   int32_t *out = sel + (int64_t)b * q.top_p;
   float *osc = scores ? scores + (int64_t)b * q.top_p : nullptr;
-  if (P > 0) {
-    ordered_emit<SL_THREADS, CL>(keys, n_local, T, need, all, sm, [&](int i, uint32_t pos) {
-      out[pos] = cand_token(w, f, S, lo + i);
-      if (osc) osc[pos] = key2f(keys[i]);
-    });
+  // ---- inputs -> shared memory (one round trip)
+  const bool kstaged = n_local > 0 && n_local <= kcap && (reinterpret_cast<uintptr_t>(src) & 15) == 0;
+  const bool ustaged = r == 0 && f.U > 0 && f.U <= ucap;
+  if (threadIdx.x == 0) {
+    const uint32_t kb = kstaged ? (uint32_t)((n_local * 4 + 15) & ~15) : 0u;
+    const uint32_t ub = ustaged ? (uint32_t)((f.U * 4 + 15) & ~15) : 0u;
+    mbar_arrive_tx(&bar, SEL_BINS * 4 + kb + ub);
+    bulk_g2s(cs.hist, hb, SEL_BINS * 4, &bar);
+    if (kb) bulk_g2s(skey, src, kb, &bar);
+    if (ub) bulk_g2s(suni, w.uni, ub, &bar);
   }
-  // every CTA of the cluster is past its reads of the shared histogram
-  cl_sync<CL>();
+  // cleanup inputs, loaded while the copies fly
+  unsigned long long st_mk = 0, st_sb = 0;
+  int64_t pending = 0;
+  if (r == 0 && threadIdx.x == 0) {
+    st_mk = w.fstat[2 * b];
+    st_sb = w.fstat[2 * b + 1];
+    pending = st_ld(st.state, KIV_ST_UNION_PENDING);
+  }
+  if (!mbar_wait_bounded(&bar, 0)) s_fail = 1;
+  const uint32_t *keys = kstaged ? skey : src;
+  auto key_at = [&](int i) { return kstaged ? skey[i] : __ldcg(src + i); };
+  auto emit_global = [&](int i, uint32_t pos) {   // i: index within this CTA's range
+    if (pos < P) {
+      out[pos] = cand_token(w, f, S, lo + i);
+      if (osc) osc[pos] = key2f(key_at(i));
+    }
+  };
+  if (P > 0 && !all) {
+    find_bin<SL_THREADS>((uint32_t)P, cs, [&](int bin) { return cs.hist[bin]; });
+    const uint32_t b0 = cs.bin, need0 = (uint32_t)P - cs.above;
+    __syncthreads();
+    const int n_r = ordered_compact<SL_THREADS>(
+        n_local, key_at, [&](uint32_t key) { return (key >> 21) >= b0; }, ckey, cidx, 0, cap, cs);
+    if (threadIdx.x == 0) s_cnt = n_r;
+    cl_sync<CL>();
+    int total = 0, off = 0;
+#pragma unroll 1
+    for (int o = 0; o < CL; ++o) {
+      const int c = *cl_map<CL>(&s_cnt, o);
+      off += o < r ? c : 0;
+      total += c;
+    }
+    if (total <= cap) {
+      if (r > 0) {
+        uint32_t *rk = cl_map<CL>(ckey, 0);
+        int32_t *ri = cl_map<CL>(cidx, 0);
+        for (int i = threadIdx.x; i < n_r; i += SL_THREADS) {
+          rk[off + i] = ckey[i];
+          ri[off + i] = (int32_t)lo + cidx[i];
+        }
+      }
+      cl_sync<CL>();
+      if (r == 0) {
+        select_candidates<SL_THREADS>(ckey, total, b0, need0, bkey, bidx, flag, SL_BND, cs, sm,
+                                      [&](int ci, uint32_t pos) {
+                                        if (pos < P) sel_ci[pos] = ci;
+                                      });
+        __syncthreads();
+        const int64_t uS = f.U * S;
+        for (int p = threadIdx.x; p < (int)P; p += SL_THREADS) {
+          const int ci = sel_ci[p];
+          const int64_t c = cidx[ci];
+          int32_t tok;
+          if (c < uS) tok = (int32_t)((int64_t)(ustaged ? suni[c / S] : __ldcg(w.uni + c / S)) * S + c % S);
+          else tok = (int32_t)(f.np_global * S + (c - uS));
+          out[p] = tok;
+          if (osc) osc[p] = key2f(ckey[ci]);
+        }
+      }
+    } else {
+      uint32_t T = 0, need = 0;
+      radix_threshold<SL_THREADS, CL>(keys, n_local, (uint32_t)P, sm, T, need, hb);
+      ordered_emit<SL_THREADS, CL>(keys, n_local, T, need, false, sm, emit_global);
+    }
+  } else if (P > 0) {
+    ordered_emit<SL_THREADS, CL>(keys, n_local, 0u, 0u, true, sm, emit_global);
+  }
+  // every CTA has read the histogram (first cluster barrier, or P == 0)
   if (r == 0) {
+    __syncthreads();
     for (int i = threadIdx.x; i < SEL_BINS; i += SL_THREADS) hb[i] = 0;
     if (threadIdx.x == 0) {
-      const unsigned long long mk = w.fstat[2 * b];
-      const unsigned long long sb = w.fstat[2 * b + 1];
-      if (mk) atomicMax(reinterpret_cast<unsigned long long *>(st.state + KIV_ST_FINE_MAX), mk);
-      atomicAdd(reinterpret_cast<double *>(st.state + KIV_ST_FINE_SUM), __longlong_as_double((long long)sb));
+      if (st_mk) atomicMax(reinterpret_cast<unsigned long long *>(st.state + KIV_ST_FINE_MAX), st_mk);
+      atomicAdd(reinterpret_cast<double *>(st.state + KIV_ST_FINE_SUM), __longlong_as_double((long long)st_sb));
       w.fstat[2 * b] = 0;
       w.fstat[2 * b + 1] = 0;
+      if (s_fail)
+        atomicOr(reinterpret_cast<unsigned long long *>(st.state + KIV_ST_ERROR),
+                 (unsigned long long)KIV_ERRBIT_WAIT_TIMEOUT);
     }
     if (st.shard_count > 1) {
       for (int64_t j = P + threadIdx.x; j < q.top_p; j += SL_THREADS) {
         out[j] = -1;
         if (osc) osc[j] = 0.f;
+      }
+    }
+    if (b == 0) {
+      // the scorer built the union from the coarse pass's page marks: consume them
+      if (threadIdx.x == 0) s_cnt = (int)pending;
+      __syncthreads();
+      if (s_cnt) {
+        const int64_t np = f.np_global > st.shard_rank
+                               ? (f.np_global - st.shard_rank + st.shard_count - 1) / st.shard_count : 0;
+        for (int64_t i = threadIdx.x; i < (np + 31) / 32; i += SL_THREADS) w.pbits[i] = 0;
+        if (threadIdx.x == 0) st.state[KIV_ST_UNION_PENDING] = 0;
       }
     }
     if (threadIdx.x == 0) {
@@ -425,8 +531,8 @@ static kiv_status launch_fs(const kiv_store *st, const kiv_query *q, const Works
   per_sm = std::max(per_sm, 1);
   const int64_t units_cap = (int64_t)st->batch * (w.u_cap + 1) * ceil_div(S, tr);
   const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(units_cap, (int64_t)sm_count() * per_sm));
-  kern<<<(unsigned)grid, FS_THREADS, smem, s>>>(*st, *q, w, tr, stage_q);
-  return cuda_status(cudaGetLastError(), "fine_scores");
+  return cuda_status(launch_pdl(kern, dim3((unsigned)grid), dim3(FS_THREADS), smem, s, 1, *st, *q, w, tr, stage_q),
+                     "fine_scores");
 }
 
 template <typename T>
@@ -449,6 +555,7 @@ static kiv_status dispatch_fs(const kiv_store *st, const kiv_query *q, const Wor
 
 kiv_status launch_fine_score(const kiv_store *st, const kiv_query *q, const Workspace &w, cudaStream_t s) {
   if (fine_tc_eligible(st, q)) return launch_fine_score_tc(st, q, w, s);
+  KIV_CHECK(launch_union(st, w, s));
   switch (st->dtype) {
     case KIV_DTYPE_F32: return dispatch_fs<float>(st, q, w, s);
     case KIV_DTYPE_BF16: return dispatch_fs<__nv_bfloat16>(st, q, w, s);
@@ -467,25 +574,14 @@ kiv_status launch_fine(const kiv_store *st, const kiv_query *q, const Workspace 
 kiv_status launch_fine_topk(const kiv_store *st, const kiv_query *q, const Workspace &w, int32_t *sel,
                             float *sel_scores, cudaStream_t s) {
   // select: one cluster of SEL_CLUSTER CTAs per batch row
-  const int64_t chunk = ceil_div(w.c_cap, SEL_CLUSTER);
-  const int64_t limit = (200 * 1024 - (int64_t)sizeof(SelectSmem<SL_THREADS>)) / 4;
-  const int chunk_cap = (int)std::min<int64_t>(chunk, limit);
-  const size_t smem = (size_t)chunk_cap * sizeof(uint32_t);
+  const int cap = (int)std::max<int64_t>(16, std::min<int64_t>(SL_CAP, align_up(w.c_cap, 16)));
+  const int ucap = (int)std::min<int64_t>(SL_UCAP, align_up(w.u_cap, 4));
+  const int kcap = (int)std::min<int64_t>(SL_KCAP, align_up(ceil_div(w.c_cap, SEL_CLUSTER), 16) + 16);
+  const size_t smem = (size_t)cap * 13 + (size_t)SL_BND * 8 + (size_t)ucap * 4 + (size_t)kcap * 4;
   auto kern = fine_select_kernel<SEL_CLUSTER>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(st->batch * SEL_CLUSTER));
-  cfg.blockDim = dim3(SL_THREADS);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = SEL_CLUSTER;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, *st, *q, w, sel, sel_scores, chunk_cap);
+  const cudaError_t e = launch_pdl(kern, dim3((unsigned)(st->batch * SEL_CLUSTER)), dim3(SL_THREADS), smem, s,
+                                   SEL_CLUSTER, *st, *q, w, sel, sel_scores, cap, ucap, kcap);
   return cuda_status(e, "fine_select");
 }
 
@@ -499,7 +595,9 @@ kiv_status launch_fine_merge(const kiv_store *st, const kiv_query *q, const Work
     return KIV_ERR_CAPACITY;
   }
   cudaFuncSetAttribute(fine_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  fine_merge_kernel<<<(unsigned)st->batch, FM_THREADS, smem, s>>>(*st, *q, w, ls, lt, n, sel, sel_local);
+  const cudaError_t e = launch_pdl(fine_merge_kernel, dim3((unsigned)st->batch), dim3(FM_THREADS), smem, s, 1, *st,
+                                   *q, w, ls, lt, n, sel, sel_local);
+  if (e != cudaSuccess) return cuda_status(e, "fine_merge");
   return cuda_status(cudaGetLastError(), "fine_merge");
 }
 

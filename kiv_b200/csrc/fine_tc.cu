@@ -30,6 +30,7 @@ namespace kiv {
 
 constexpr int TC_THREADS = 192;
 constexpr int TC_PAGE = 128;
+constexpr int64_t TC_UNION_INLINE = 8192;   // largest union built inside the fine scorer
 
 struct TcGeom {
   int64_t U, np_global, partial, per_b;
@@ -42,15 +43,15 @@ struct TcGeom {
 template <bool BF16, bool COARSE>
 __global__ void __launch_bounds__(TC_THREADS, 1)
 scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_query q, Workspace w,
-                 int ncols, int stages) {
+                 int ncols, int stages, int union_inline) {
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-  griddep_wait();
   extern __shared__ uint8_t tc_dyn[];
-  __shared__ uint64_t full[4], empty[4], acc_full[2], acc_empty[2];
+  __shared__ uint64_t full[4], empty[4], acc_full[2], acc_empty[2], ubar;
   __shared__ uint32_t s_tmem;
   __shared__ int s_fail;
   __shared__ uint32_t s_wmax[4];
   __shared__ float s_wsum[4];
+  __shared__ int s_psum[TC_THREADS / 32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int D = st.head_dim, H = st.num_kv_heads, S = st.page_size;
   const int Hq = q.num_query_heads, Q = q.query_len, G = Hq / H;
@@ -59,17 +60,17 @@ scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_que
   const uint32_t tile_bytes = (uint32_t)TC_PAGE * D * sizeof(T);
   const uint32_t qbox_bytes = (uint32_t)ncols * 128;
 
-  // 1024-byte aligned carve-up: [stages][tile] [H][nbox][qbox] [hist 2048]
+  // 1024-byte aligned carve-up: [stages][tile] [H][nbox][qbox] [hist 2048] [union list]
   const uint32_t base_addr = smem_u32(tc_dyn);
   uint8_t *smem = tc_dyn + ((1024 - (base_addr & 1023)) & 1023);
   uint8_t *stage_mem = smem;
   uint8_t *qmem = stage_mem + (size_t)stages * tile_bytes;
   uint32_t *hist = reinterpret_cast<uint32_t *>(qmem + (size_t)H * nbox * qbox_bytes);
+  int32_t *ulist = reinterpret_cast<int32_t *>(hist + SEL_BINS);
 
-  if (blockIdx.x == 0 && threadIdx.x == 0) {
-    st.state[COARSE ? KIV_ST_COARSE_MAX : KIV_ST_FINE_MAX] = 0;
-    st.state[COARSE ? KIV_ST_COARSE_SUM : KIV_ST_FINE_SUM] = 0;
-  }
+  // ---- prologue: independent of the previous kernel in the stream (with
+  // programmatic dependent launch it overlaps that kernel's tail).  The
+  // query was written before the layer-step's first kernel.
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
       mbar_init(&full[s], 1);
@@ -79,6 +80,7 @@ scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_que
       mbar_init(&acc_full[a], 1);
       mbar_init(&acc_empty[a], 4);
     }
+    mbar_init(&ubar, 1);
     mbar_fence_init();
     s_fail = 0;
   }
@@ -108,20 +110,57 @@ scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_que
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = s_tmem;
+  // ---- the previous kernel's results (state, union) are needed from here on
+  griddep_wait();
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    st.state[COARSE ? KIV_ST_COARSE_MAX : KIV_ST_FINE_MAX] = 0;
+    st.state[COARSE ? KIV_ST_COARSE_SUM : KIV_ST_FINE_SUM] = 0;
+  }
 
   TcGeom f;
-  {
-    const int64_t cold = st_ld(st.state, KIV_ST_COLD_LEN);
-    f.U = st_ld(st.state, KIV_ST_UNION);
-    f.np_global = cold / S;
-    f.partial = cold % S;
-    f.part_owned = f.partial > 0 && (f.np_global % st.shard_count) == st.shard_rank;
-    f.per_b = f.U + (f.part_owned ? 1 : 0);
-  }
-  // batch 1.  FINE: one unit per candidate page (tiles = its KV heads);
-  // COARSE: one unit per block of 128 finalized local pages (tiles = KV heads)
+  const int32_t *pages = w.uni;
+  const int64_t cold = st_ld(st.state, KIV_ST_COLD_LEN);
+  f.np_global = cold / S;
+  f.partial = cold % S;
+  f.part_owned = f.partial > 0 && (f.np_global % st.shard_count) == st.shard_rank;
   const int64_t np_local = f.np_global > st.shard_rank
                                ? (f.np_global - st.shard_rank + st.shard_count - 1) / st.shard_count : 0;
+  if (COARSE) {
+    clear_stale_marks(st, w, np_local);
+    f.U = 0;
+  } else if (union_inline && st_ld(st.state, KIV_ST_UNION_PENDING) != 0) {
+    // a new coarse pass marked its pages: every CTA builds the sorted union
+    // from the page marks; CTA 0 also publishes it (the select kernel and the
+    // reuse path read it from the workspace)
+    // the page marks come in with one bulk copy into the (still unused) stage ring
+    const uint32_t fbytes = (uint32_t)((((np_local + 31) / 32) * 4 + 15) & ~15ll);
+    const bool bulk = np_local > 0 && (int64_t)fbytes <= (int64_t)stages * tile_bytes && fbytes < (1u << 20);
+    if (bulk) {
+      if (threadIdx.x == 0) {
+        mbar_arrive_tx(&ubar, fbytes);
+        bulk_g2s(stage_mem, w.pbits, fbytes, &ubar);
+      }
+      if (!mbar_wait_bounded(&ubar, 0)) s_fail = 1;
+      f.U = union_from_bits<TC_THREADS, true>(reinterpret_cast<const uint32_t *>(stage_mem), np_local, ulist,
+                                              (int)w.u_cap, st.shard_rank, st.shard_count, s_psum);
+      // the stage ring is written by TMA next: order these generic reads first
+      tc::fence_proxy_async_smem();
+      __syncthreads();
+    } else {
+      f.U = union_from_bits<TC_THREADS, false>(w.pbits, np_local, ulist, (int)w.u_cap, st.shard_rank,
+                                               st.shard_count, s_psum);
+    }
+    if (blockIdx.x == 0) {
+      for (int i = threadIdx.x; i < f.U; i += TC_THREADS) w.uni[i] = ulist[i];
+      if (threadIdx.x == 0) st.state[KIV_ST_UNION] = f.U;
+    }
+    pages = ulist;
+  } else {
+    f.U = st_ld(st.state, KIV_ST_UNION);
+  }
+  f.per_b = f.U + (f.part_owned ? 1 : 0);
+  // batch 1.  FINE: one unit per candidate page (tiles = its KV heads);
+  // COARSE: one unit per block of 128 finalized local pages (tiles = KV heads)
   const int64_t units = COARSE ? (np_local + TC_PAGE - 1) / TC_PAGE : f.per_b;
   const int64_t my_units = units > blockIdx.x ? (units - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
   const int64_t my_tiles = my_units * H;
@@ -141,7 +180,7 @@ scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_que
         if (COARSE) {
           y = (int32_t)((int64_t)kvh * w.np_cap + u * TC_PAGE);
         } else {
-          const int64_t page = u < f.U ? (int64_t)w.uni[u] : f.np_global;
+          const int64_t page = u < f.U ? (int64_t)pages[u] : f.np_global;
           const int64_t lp = page / st.shard_count;
           y = (int32_t)((int64_t)kvh * st.cold_capacity + lp * S);
         }
@@ -329,7 +368,10 @@ static kiv_status launch_scores_tc(const kiv_store *st, const kiv_query *q, cons
   }
   const size_t tile = (size_t)TC_PAGE * D * 2;
   const size_t qbytes = (size_t)st->num_kv_heads * ncols * D * 2;
-  const size_t fixed = 1024 + qbytes + SEL_BINS * 4;
+  // fine pass: the union list is built in shared memory unless it is large
+  const int union_inline = !coarse && w.u_cap <= TC_UNION_INLINE ? 1 : 0;
+  if (!coarse && !union_inline) KIV_CHECK(launch_union(st, w, s));
+  const size_t fixed = 1024 + qbytes + SEL_BINS * 4 + (union_inline ? (size_t)w.u_cap * 4 : 0);
   const int stages = (int)std::min<size_t>(4, (200 * 1024 - fixed) / tile);
   if (stages < 2) return KIV_ERR_UNSUPPORTED;
   const size_t smem = fixed + (size_t)stages * tile;
@@ -338,15 +380,17 @@ static kiv_status launch_scores_tc(const kiv_store *st, const kiv_query *q, cons
 #define KIV_TC_LAUNCH(BF, CO)                                                                          \
   do {                                                                                                 \
     cudaFuncSetAttribute(scores_tc_kernel<BF, CO>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
-    scores_tc_kernel<BF, CO><<<(unsigned)grid, TC_THREADS, smem, s>>>(map, *st, *q, w, ncols, stages);    \
+    e = launch_pdl(scores_tc_kernel<BF, CO>, dim3((unsigned)grid), dim3(TC_THREADS), smem, s, 1, map, *st, *q, w, \
+                   ncols, stages, union_inline);                                                        \
   } while (0)
   const bool bf = st->dtype == KIV_DTYPE_BF16;
+  cudaError_t e = cudaSuccess;
   if (bf && coarse) KIV_TC_LAUNCH(true, true);
   else if (bf) KIV_TC_LAUNCH(true, false);
   else if (coarse) KIV_TC_LAUNCH(false, true);
   else KIV_TC_LAUNCH(false, false);
 #undef KIV_TC_LAUNCH
-  return cuda_status(cudaGetLastError(), coarse ? "coarse_scores_tc" : "fine_scores_tc");
+  return cuda_status(e, coarse ? "coarse_scores_tc" : "fine_scores_tc");
 }
 
 kiv_status launch_fine_score_tc(const kiv_store *st, const kiv_query *q, const Workspace &w, cudaStream_t s) {

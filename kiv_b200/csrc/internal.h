@@ -4,6 +4,9 @@
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
+#include <stdlib.h>
+
+#include <utility>
 
 #include "../../include/kiv_b200.h"
 
@@ -25,7 +28,7 @@ constexpr int SEL_CLUSTER = 8;   // CTAs per cluster in the fine top-P select
 // Scratch carved out of the caller's workspace for one store / query shape.
 struct Workspace {
   float *scores;       // [R, np_cap]        coarse scores
-  uint8_t *flags;      // [np_cap]           page marks for the union
+  uint32_t *pbits;     // [np_cap / 32]      page marks of the union (one bit per local page)
   int32_t *uni;        // [u_cap]            union pages (global ids, ascending)
   uint32_t *agg;       // [B, c_cap]         fine keys (monotone u32 of the max score)
   int32_t *selcnt;     // [B]                selected tokens of this shard per batch row
@@ -55,6 +58,7 @@ kiv_status launch_coarse_merge(const kiv_store *st, const kiv_query *q, const Wo
 kiv_status launch_fine(const kiv_store *st, const kiv_query *q, const Workspace &w, int32_t *sel,
                        float *sel_scores, cudaStream_t s);
 kiv_status launch_fine_score(const kiv_store *st, const kiv_query *q, const Workspace &w, cudaStream_t s);
+kiv_status launch_union(const kiv_store *st, const Workspace &w, cudaStream_t s);
 bool fine_tc_eligible(const kiv_store *st, const kiv_query *q);
 kiv_status launch_fine_score_tc(const kiv_store *st, const kiv_query *q, const Workspace &w, cudaStream_t s);
 kiv_status launch_coarse_score_tc(const kiv_store *st, const kiv_query *q, const Workspace &w, cudaStream_t s);
@@ -74,6 +78,40 @@ kiv_status launch_attend_merge(const kiv_store *st, const kiv_query *q, const fl
 
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// Programmatic dependent launch: a kernel may start (and run its prologue)
+// while the previous kernel in the stream finishes; every kernel calls
+// griddepcontrol.wait before reading the previous kernel's results and
+// releases its dependents right after that wait.  KIV_DISABLE_PDL=1 turns it off.
+inline bool pdl_enabled() {
+  static const bool on = getenv("KIV_DISABLE_PDL") == nullptr;
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              int cluster_x, Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[n].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  ++n;
+  if (cluster_x > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster_x;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 #define KIV_CHECK(x)                 \
   do {                               \
     const kiv_status _st = (x);      \
@@ -82,6 +120,17 @@ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 // floats per attention partial row: out[D], max, sum, 16-byte aligned
 __host__ __device__ inline int partial_stride(int D) { return (D + 2 + 3) & ~3; }
+
+#ifdef __CUDACC__
+// A coarse pass whose page marks were never consumed by a fine pass left them
+// set: clear them (grid-stride) before this coarse pass marks its own.
+__device__ __forceinline__ void clear_stale_marks(const kiv_store &st, const Workspace &w, int64_t np_local) {
+  if (*reinterpret_cast<volatile const int64_t *>(st.state + KIV_ST_UNION_PENDING) == 0) return;
+  const int64_t nw = (np_local + 31) / 32;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nw; i += (int64_t)gridDim.x * blockDim.x)
+    w.pbits[i] = 0;
+}
+#endif
 inline int64_t align_up(int64_t a, int64_t b) { return ceil_div(a, b) * b; }
 
 inline int elem_bytes(int dtype) { return dtype == KIV_DTYPE_F32 ? 4 : 2; }
