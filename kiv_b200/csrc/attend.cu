@@ -22,6 +22,7 @@ namespace kiv {
 constexpr int AT_THREADS = 256;
 constexpr int AT_STAGES = 2;
 constexpr int CB_THREADS = 256;
+constexpr int CB_COLS = 64;        // output columns per combine CTA
 
 template <typename T>
 struct AttnArgs {
@@ -104,16 +105,15 @@ attend_split_kernel(AttnArgs<T> a) {
     }
     dot.load_query(qrows, g, nv, 1.0f);
   }
-  __syncthreads();
-  // ---- the selection (previous kernel) is needed from here on
-  griddep_wait();
-  const int64_t ncold = a.w.selcnt[b];
-  const int64_t nkeys = ncold + (hot_hi - hot_lo);
-  int64_t kps = (nkeys + a.n_split - 1) / a.n_split;
+  // Key order of the split: the hot window rows first, then the selected
+  // cold rows.  The split size is fixed by the cold list capacity
+  // (sel_stride bounds the selected count), so a split made only of hot rows
+  // is known before the selection finishes and never waits for it.
+  const int64_t hot_count = hot_hi - hot_lo;
+  int64_t kps = (a.sel_stride + hot_count + a.n_split - 1) / a.n_split;
   kps = (kps + 7) / 8 * 8;
-  const int64_t k_lo = std::min<int64_t>(nkeys, split * kps);
-  const int64_t k_hi = std::min<int64_t>(nkeys, k_lo + kps);
-  const int ntile = (int)((k_hi - k_lo + ATT_TILE - 1) / ATT_TILE);
+  const int64_t k_lo = split * kps;
+  const bool hot_only = k_lo + kps <= hot_count;
 
   T *kt = reinterpret_cast<T *>(at_smem);                 // [STAGES][TILE][D]
   T *vt = kt + (size_t)AT_STAGES * ATT_TILE * D;          // [STAGES][TILE][D]
@@ -128,37 +128,73 @@ attend_split_kernel(AttnArgs<T> a) {
   const int64_t bhk = (int64_t)b * H + kvh;
   const uint32_t row_bytes = (uint32_t)D * sizeof(T);
 
-  auto key_rows = [&](int64_t k, const T *&pk, const T *&pv) {
-    if (k < ncold) {
-      const int64_t tok = selb[k];
+  // tok_hint: the cold key's token when already loaded, else -1
+  auto key_rows = [&](int64_t k, const T *&pk, const T *&pv, int32_t tok_hint) {
+    if (k < hot_count) {
+      const int64_t slot = (hot_start + hot_lo + k) % st.hot_capacity;
+      pk = hot_k + (bhk * st.hot_capacity + slot) * D;
+      pv = hot_v + (bhk * st.hot_capacity + slot) * D;
+    } else {
+      const int64_t tok = tok_hint >= 0 ? tok_hint : selb[k - hot_count];
       const int64_t p = tok / S;
       const int64_t slot = (p / st.shard_count) * S + tok % S;
       pk = cold_k + (bhk * st.cold_capacity + slot) * D;
       pv = cold_v + (bhk * st.cold_capacity + slot) * D;
-    } else {
-      const int64_t j = hot_lo + (k - ncold);
-      const int64_t slot = (hot_start + j) % st.hot_capacity;
-      pk = hot_k + (bhk * st.hot_capacity + slot) * D;
-      pv = hot_v + (bhk * st.hot_capacity + slot) * D;
     }
   };
-  // warp 0 issues one tile: lane i copies key row i (K and V)
-  auto issue = [&](int t) {
+  // warp 0 copies the rows of tile t with key index in [lo, hi): lane i takes
+  // key k0 + i (K and V).  `arrive`: this is the tile's last part (completes
+  // the barrier phase); otherwise only the expected bytes are added.
+  auto issue_part = [&](int t, int64_t lo, int64_t hi, bool arrive, int32_t tok_hint) {
     const int stage = t % AT_STAGES;
     const int64_t k0 = k_lo + (int64_t)t * ATT_TILE;
-    const int n = (int)std::min<int64_t>(ATT_TILE, k_hi - k0);
-    if (lane == 0) mbar_arrive_tx(&bars[stage], 2u * n * row_bytes);
+    const int64_t a0 = std::max<int64_t>(k0, lo), a1 = std::min<int64_t>(k0 + ATT_TILE, hi);
+    const uint32_t bytes = a1 > a0 ? 2u * (uint32_t)(a1 - a0) * row_bytes : 0u;
+    if (lane == 0) {
+      if (arrive) mbar_arrive_tx(&bars[stage], bytes);
+      else if (bytes) mbar_expect_tx(&bars[stage], bytes);
+    }
     __syncwarp();
-    if (lane < n) {
+    const int64_t k = k0 + lane;
+    if (k >= a0 && k < a1) {
       const T *pk, *pv;
-      key_rows(k0 + lane, pk, pv);
+      key_rows(k, pk, pv, tok_hint);
       bulk_g2s(kt + ((size_t)stage * ATT_TILE + lane) * D, pk, row_bytes, &bars[stage]);
       bulk_g2s(vt + ((size_t)stage * ATT_TILE + lane) * D, pv, row_bytes, &bars[stage]);
     }
   };
-  if (warp == 0) {
-    for (int t = 0; t < (ntile < AT_STAGES ? ntile : AT_STAGES); ++t) issue(t);
+  const int early_tiles = (int)std::min<int64_t>(AT_STAGES, (std::min<int64_t>(kps, hot_count - k_lo) +
+                                                             ATT_TILE - 1) / ATT_TILE);
+  __syncthreads();   // barriers initialized
+  // hot rows of the first tiles: independent of the selection
+  if (warp == 0)
+    for (int t = 0; t < early_tiles; ++t)
+      issue_part(t, k_lo, std::min<int64_t>(hot_count, k_lo + kps), hot_only, -1);
+  int64_t ncold = 0;
+  int32_t tok0 = -1, tok1 = -1;
+  static_assert(AT_STAGES == 2, "two preloaded tiles");
+  if (!hot_only) {
+    // ---- the selection (previous kernel) is needed from here on.  The
+    // selected count and the tokens of the first two tiles load together
+    // (entries past the count are ignored).
+    griddep_wait();
+    if (warp == 0) {
+      const int64_t c0 = k_lo + lane - hot_count, c1 = c0 + ATT_TILE;
+      const int64_t lim = std::min<int64_t>((int64_t)a.sel_stride, k_lo + kps - hot_count);
+      if (c0 >= 0 && c0 < lim) tok0 = selb[c0];
+      if (c1 >= 0 && c1 < lim) tok1 = selb[c1];
+    }
+    ncold = a.w.selcnt[b];
   }
+  const int64_t nkeys = hot_count + ncold;
+  const int64_t k_hi = std::min<int64_t>(nkeys, k_lo + kps);
+  const int ntile = k_hi > k_lo ? (int)((k_hi - k_lo + ATT_TILE - 1) / ATT_TILE) : 0;
+  if (warp == 0 && !hot_only) {
+    // cold rows of the first tiles (and the arrival that completes them)
+    if (ntile > 0) issue_part(0, hot_count, k_hi, true, tok0);
+    if (ntile > 1) issue_part(1, hot_count, k_hi, true, tok1);
+  }
+  auto issue = [&](int t) { issue_part(t, k_lo, k_hi, true, -1); };
 
   // P.V mapping: thread -> (vector dv, row r, key subset ks)
   const int nvp = nv;  // vectors per row
@@ -197,8 +233,8 @@ attend_split_kernel(AttnArgs<T> a) {
             s = acc[i] * q.scaling;
             if (q.softcap > 0.f) s = q.softcap * tanhf(s / q.softcap);
             const int64_t k = k0 + kk;
-            if (k >= ncold) {
-              const int64_t j = hot_lo + (k - ncold);
+            if (k < hot_count) {
+              const int64_t j = hot_lo + k;
               if (a.mask.causal && j > hot_len - Q + row_t[r]) s = -INFINITY;
               if (a.mask.add != nullptr)
                 s += a.mask.add[b * a.mask.stride_b + row_h[r] * a.mask.stride_h +
@@ -261,6 +297,27 @@ attend_split_kernel(AttnArgs<T> a) {
       atomicOr(reinterpret_cast<unsigned long long *>(st.state + KIV_ST_ERROR), 8ull);
     return;
   }
+  const int Dp = partial_stride(D);
+  if (ksub == 1) {
+    // one thread per (row, vector): write the partial straight from registers
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int idx = threadIdx.x + i * AT_THREADS;
+      if (idx >= pairs) continue;
+      const int dv = idx % nvp, r = idx / nvp;
+      if (row_h[r] < 0) continue;
+      const int64_t R_idx = ((int64_t)b * q.num_query_heads + row_h[r]) * Q + row_t[r];
+      float *dst = a.w.part + (R_idx * a.w.split_cap + split) * Dp;
+#pragma unroll
+      for (int e = 0; e < V; e += 4)
+        *reinterpret_cast<float4 *>(dst + dv * V + e) = make_float4(o[i][e], o[i][e + 1], o[i][e + 2], o[i][e + 3]);
+      if (dv == 0) {
+        dst[D] = s_m[r];
+        dst[D + 1] = s_l[r];
+      }
+    }
+    return;
+  }
   // reduce over key subsets in a fixed order (deterministic) and write the
   // partial (out, max, sum)
 #pragma unroll
@@ -283,7 +340,6 @@ attend_split_kernel(AttnArgs<T> a) {
     for (int e = 0; e < V; ++e) sc_out_slot(ored, pairs, ksub, V)[(size_t)r * D + dv * V + e] = acc[e];
   }
   __syncthreads();
-  const int Dp = partial_stride(D);
   for (int r = 0; r < RCH; ++r) {
     if (row_h[r] < 0) continue;
     const int64_t R_idx = ((int64_t)b * q.num_query_heads + row_h[r]) * Q + row_t[r];
@@ -297,111 +353,447 @@ attend_split_kernel(AttnArgs<T> a) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-core decode attention for 16-bit stores with at most 16 query rows
+// per KV head (the G*Q rows of a decode step).  Same splits, key order and
+// partial format as attend_split_kernel; per 32-key tile S = Q K^T and
+// O = P V run on warp-level MMAs (m16n8k16, fp32 accumulate): the query rows
+// form a single 16-row tile, a quarter of the smallest tcgen05 tile, and
+// this kernel is on the latency path of every decode step.  K and V rows are
+// staged by per-row bulk copies into rows padded by 16 bytes, so the
+// ldmatrix reads of 8 rows hit 8 distinct bank groups.  P is rounded to the
+// store dtype before the P V product (as flash attention does).
+// ---------------------------------------------------------------------------
+constexpr int AM_THREADS = 128;    // 4 warps: 8 keys each for S, D/4 columns each for O
+constexpr int AM_ROWS = 16;        // query rows per tile
+constexpr int AM_PPITCH = 80;      // bytes per row of the P tile (32 keys + pad)
+
+template <typename T> struct MmaOp;
+template <> struct MmaOp<__nv_bfloat16> {
+  __device__ __forceinline__ static void mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+  __device__ __forceinline__ static uint32_t pack2(float x, float y) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(x, y);
+    return *reinterpret_cast<uint32_t *>(&h);
+  }
+};
+template <> struct MmaOp<__half> {
+  __device__ __forceinline__ static void mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+  __device__ __forceinline__ static uint32_t pack2(float x, float y) {
+    __half2 h = __floats2half2_rn(x, y);
+    return *reinterpret_cast<uint32_t *>(&h);
+  }
+};
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void *p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void *p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+
+template <typename T>
+__global__ void __launch_bounds__(AM_THREADS)
+attend_mma_kernel(AttnArgs<T> a) {
+  extern __shared__ __align__(128) uint8_t am_smem[];
+  __shared__ uint64_t bars[AT_STAGES];
+  __shared__ float s_red[4][AM_ROWS], s_sum[4][AM_ROWS];
+  __shared__ float s_m[AM_ROWS], s_l[AM_ROWS], s_mnew[AM_ROWS];
+  __shared__ int s_fail;
+  using Op = MmaOp<T>;
+  const kiv_store &st = a.st;
+  const kiv_query &q = a.q;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 2, t4 = lane & 3;
+  const int D = st.head_dim, H = st.num_kv_heads, S = st.page_size;
+  const int G = q.num_query_heads / H, Q = q.query_len;
+  const int rows_kv = G * Q;
+  const int pitch = D * (int)sizeof(T) + 16;   // bytes per staged row
+  const int split = blockIdx.x % a.n_split;
+  const int bh = blockIdx.x / a.n_split;
+  const int b = bh / H, kvh = bh % H;
+
+  uint8_t *qs = am_smem;                                         // [16][pitch]
+  uint8_t *ks = qs + AM_ROWS * pitch;                            // [STAGES][TILE][pitch]
+  uint8_t *vs = ks + AT_STAGES * ATT_TILE * pitch;               // [STAGES][TILE][pitch]
+  uint8_t *ps = vs + AT_STAGES * ATT_TILE * pitch;               // [16][AM_PPITCH]
+
+  // ---- prologue: inputs written before the retrieval's first kernel
+  const int64_t hot_len = st_ld(st.state, KIV_ST_HOT_LEN);
+  const int64_t hot_start = st_ld(st.state, KIV_ST_HOT_START);
+  const int64_t hot_lo = hot_len * a.hot_slice / a.hot_slices;
+  const int64_t hot_hi = hot_len * (a.hot_slice + 1) / a.hot_slices;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < AT_STAGES; ++s) mbar_init(&bars[s], 1);
+    mbar_fence_init();
+    s_fail = 0;
+  }
+  if (threadIdx.x < AM_ROWS) {
+    s_m[threadIdx.x] = -INFINITY;
+    s_l[threadIdx.x] = 0.f;
+  }
+  {
+    const T *qb = reinterpret_cast<const T *>(q.q);
+    const int nc = D / 8;                                         // 16-byte chunks per row
+    for (int e = threadIdx.x; e < AM_ROWS * nc; e += AM_THREADS) {
+      const int rr = e / nc, c = e % nc;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (rr < rows_kv) {
+        const int h = kvh * G + rr / Q, tq = rr % Q;
+        v = ld16(qb + b * q.stride_b + h * q.stride_h + tq * q.stride_t + c * 8);
+      }
+      *reinterpret_cast<uint4 *>(qs + rr * pitch + c * 16) = v;
+    }
+  }
+  const int64_t hot_count = hot_hi - hot_lo;
+  int64_t kps = (a.sel_stride + hot_count + a.n_split - 1) / a.n_split;
+  kps = (kps + 7) / 8 * 8;
+  const int64_t k_lo = split * kps;
+  const bool hot_only = k_lo + kps <= hot_count;
+
+  const T *cold_k = reinterpret_cast<const T *>(st.cold_k);
+  const T *cold_v = reinterpret_cast<const T *>(st.cold_v);
+  const T *hot_k = reinterpret_cast<const T *>(st.hot_k);
+  const T *hot_v = reinterpret_cast<const T *>(st.hot_v);
+  const int32_t *selb = a.sel + (int64_t)b * a.sel_stride;
+  const int64_t bhk = (int64_t)b * H + kvh;
+  const uint32_t row_bytes = (uint32_t)D * sizeof(T);
+  auto key_rows = [&](int64_t k, const T *&pk, const T *&pv, int32_t tok_hint) {
+    if (k < hot_count) {
+      const int64_t slot = (hot_start + hot_lo + k) % st.hot_capacity;
+      pk = hot_k + (bhk * st.hot_capacity + slot) * D;
+      pv = hot_v + (bhk * st.hot_capacity + slot) * D;
+    } else {
+      const int64_t tok = tok_hint >= 0 ? tok_hint : selb[k - hot_count];
+      const int64_t p = tok / S;
+      const int64_t slot = (p / st.shard_count) * S + tok % S;
+      pk = cold_k + (bhk * st.cold_capacity + slot) * D;
+      pv = cold_v + (bhk * st.cold_capacity + slot) * D;
+    }
+  };
+  auto issue_part = [&](int t, int64_t lo, int64_t hi, bool arrive, int32_t tok_hint) {
+    const int stage = t % AT_STAGES;
+    const int64_t k0 = k_lo + (int64_t)t * ATT_TILE;
+    const int64_t a0 = std::max<int64_t>(k0, lo), a1 = std::min<int64_t>(k0 + ATT_TILE, hi);
+    const uint32_t bytes = a1 > a0 ? 2u * (uint32_t)(a1 - a0) * row_bytes : 0u;
+    if (lane == 0) {
+      if (arrive) mbar_arrive_tx(&bars[stage], bytes);
+      else if (bytes) mbar_expect_tx(&bars[stage], bytes);
+    }
+    __syncwarp();
+    const int64_t k = k0 + lane;
+    if (k >= a0 && k < a1) {
+      const T *pk, *pv;
+      key_rows(k, pk, pv, tok_hint);
+      bulk_g2s(ks + ((size_t)stage * ATT_TILE + lane) * pitch, pk, row_bytes, &bars[stage]);
+      bulk_g2s(vs + ((size_t)stage * ATT_TILE + lane) * pitch, pv, row_bytes, &bars[stage]);
+    }
+  };
+  const int early_tiles = (int)std::min<int64_t>(AT_STAGES, (std::min<int64_t>(kps, hot_count - k_lo) +
+                                                             ATT_TILE - 1) / ATT_TILE);
+  __syncthreads();   // barriers, statistics and query tile ready
+  if (warp == 0)
+    for (int t = 0; t < early_tiles; ++t)
+      issue_part(t, k_lo, std::min<int64_t>(hot_count, k_lo + kps), hot_only, -1);
+  int64_t ncold = 0;
+  int32_t tok0 = -1, tok1 = -1;
+  if (!hot_only) {
+    // ---- the selection (previous kernel) is needed from here on
+    griddep_wait();
+    if (warp == 0) {
+      const int64_t c0 = k_lo + lane - hot_count, c1 = c0 + ATT_TILE;
+      const int64_t lim = std::min<int64_t>((int64_t)a.sel_stride, k_lo + kps - hot_count);
+      if (c0 >= 0 && c0 < lim) tok0 = selb[c0];
+      if (c1 >= 0 && c1 < lim) tok1 = selb[c1];
+    }
+    ncold = a.w.selcnt[b];
+  }
+  const int64_t nkeys = hot_count + ncold;
+  const int64_t k_hi = std::min<int64_t>(nkeys, k_lo + kps);
+  const int ntile = k_hi > k_lo ? (int)((k_hi - k_lo + ATT_TILE - 1) / ATT_TILE) : 0;
+  if (warp == 0 && !hot_only) {
+    if (ntile > 0) issue_part(0, hot_count, k_hi, true, tok0);
+    if (ntile > 1) issue_part(1, hot_count, k_hi, true, tok1);
+  }
+
+  const int ntw = D / 32;           // 8-column output tiles per warp
+  const int dbase = warp * (D / 4);
+  float o[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+
+  for (int t = 0; t < ntile; ++t) {
+    const int stage = t % AT_STAGES;
+    if (!mbar_wait_bounded(&bars[stage], (uint32_t)((t / AT_STAGES) & 1))) s_fail = 1;
+    const int64_t k0 = k_lo + (int64_t)t * ATT_TILE;
+    const int n = (int)std::min<int64_t>(ATT_TILE, k_hi - k0);
+    uint8_t *kst = ks + (size_t)stage * ATT_TILE * pitch;
+    uint8_t *vst = vs + (size_t)stage * ATT_TILE * pitch;
+    if (n < ATT_TILE) {
+      // rows past the tile's keys hold stale data: zero V there (P is 0 there)
+      for (int e = threadIdx.x; e < (ATT_TILE - n) * (D / 8); e += AM_THREADS)
+        *reinterpret_cast<uint4 *>(vst + (n + e / (D / 8)) * pitch + (e % (D / 8)) * 16) = make_uint4(0, 0, 0, 0);
+    }
+    __syncthreads();
+    if (s_fail) break;
+    // ---- S = Q K^T for keys [8 warp, 8 warp + 8)
+    float sacc[4] = {0.f, 0.f, 0.f, 0.f};
+    {
+      const uint8_t *qrow = qs + (lane & 15) * pitch + 16 * (lane >> 4);
+      const uint8_t *krow = kst + (8 * warp + (lane & 7)) * pitch + 16 * (lane >> 3);
+#pragma unroll 2
+      for (int d0 = 0; d0 < D; d0 += 32) {
+        uint32_t qa[4], qb2[4], kb[4];
+        ldsm_x4(qa, qrow + d0 * 2);
+        ldsm_x4(qb2, qrow + d0 * 2 + 32);
+        ldsm_x4(kb, krow + d0 * 2);
+        Op::mma(sacc, qa, kb[0], kb[1]);
+        Op::mma(sacc, qb2, kb[2], kb[3]);
+      }
+    }
+    float sv[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int row = g + 8 * (i >> 1);
+      const int kk = 8 * warp + 2 * t4 + (i & 1);
+      float sc = -INFINITY;
+      if (kk < n && row < rows_kv) {
+        sc = sacc[i] * q.scaling;
+        if (q.softcap > 0.f) sc = q.softcap * tanhf(sc / q.softcap);
+        const int64_t k = k0 + kk;
+        if (k < hot_count) {
+          const int64_t j = hot_lo + k;
+          const int h = kvh * G + row / Q, tq = row % Q;
+          if (a.mask.causal && j > hot_len - Q + tq) sc = -INFINITY;
+          if (a.mask.add != nullptr)
+            sc += a.mask.add[b * a.mask.stride_b + h * a.mask.stride_h + tq * a.mask.stride_t + j];
+        }
+      }
+      sv[i] = sc;
+    }
+    // ---- online softmax over the tile (rows g and g + 8 of this thread)
+    float m0 = fmaxf(sv[0], sv[1]), m1 = fmaxf(sv[2], sv[3]);
+#pragma unroll
+    for (int off = 1; off < 4; off <<= 1) {
+      m0 = fmaxf(m0, __shfl_xor_sync(KIV_FULL_MASK, m0, off));
+      m1 = fmaxf(m1, __shfl_xor_sync(KIV_FULL_MASK, m1, off));
+    }
+    if (t4 == 0) {
+      s_red[warp][g] = m0;
+      s_red[warp][g + 8] = m1;
+    }
+    __syncthreads();
+    float mn[2], al[2];
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int row = g + 8 * hh;
+      float mt = s_red[0][row];
+#pragma unroll
+      for (int w2 = 1; w2 < 4; ++w2) mt = fmaxf(mt, s_red[w2][row]);
+      const float mo = s_m[row];
+      mn[hh] = fmaxf(mo, mt);
+      al[hh] = (mn[hh] == -INFINITY || mo == -INFINITY) ? (mn[hh] == -INFINITY ? 1.f : 0.f) : __expf(mo - mn[hh]);
+    }
+    float pv[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float m = mn[i >> 1];
+      pv[i] = (sv[i] == -INFINITY || m == -INFINITY) ? 0.f : __expf(sv[i] - m);
+    }
+    *reinterpret_cast<uint32_t *>(ps + g * AM_PPITCH + (8 * warp + 2 * t4) * 2) = Op::pack2(pv[0], pv[1]);
+    *reinterpret_cast<uint32_t *>(ps + (g + 8) * AM_PPITCH + (8 * warp + 2 * t4) * 2) = Op::pack2(pv[2], pv[3]);
+    float l0 = pv[0] + pv[1], l1 = pv[2] + pv[3];
+#pragma unroll
+    for (int off = 1; off < 4; off <<= 1) {
+      l0 += __shfl_xor_sync(KIV_FULL_MASK, l0, off);
+      l1 += __shfl_xor_sync(KIV_FULL_MASK, l1, off);
+    }
+    if (t4 == 0) {
+      s_sum[warp][g] = l0;
+      s_sum[warp][g + 8] = l1;
+      if (warp == 0) {
+        s_mnew[g] = mn[0];
+        s_mnew[g + 8] = mn[1];
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      o[i][0] *= al[0];
+      o[i][1] *= al[0];
+      o[i][2] *= al[1];
+      o[i][3] *= al[1];
+    }
+    __syncthreads();
+    if (threadIdx.x < AM_ROWS) {
+      const int row = threadIdx.x;
+      const float mo = s_m[row], mnr = s_mnew[row];
+      const float alr = (mnr == -INFINITY || mo == -INFINITY) ? (mnr == -INFINITY ? 1.f : 0.f) : __expf(mo - mnr);
+      s_l[row] = s_l[row] * alr + s_sum[0][row] + s_sum[1][row] + s_sum[2][row] + s_sum[3][row];
+      s_m[row] = mnr;
+    }
+    // ---- O += P V for columns [dbase, dbase + D/4)
+#pragma unroll
+    for (int kk0 = 0; kk0 < ATT_TILE; kk0 += 16) {
+      uint32_t pa[4];
+      ldsm_x4(pa, ps + (lane & 15) * AM_PPITCH + (kk0 + 8 * (lane >> 4)) * 2);
+      const uint8_t *vrow = vst + (kk0 + (lane & 15)) * pitch + (dbase + 8 * (lane >> 4)) * 2;
+#pragma unroll
+      for (int nt = 0; nt < 8; nt += 2) {
+        if (nt < ntw) {
+          uint32_t vb[4];
+          ldsm_x4_t(vb, vrow + nt * 16);
+          Op::mma(o[nt], pa, vb[0], vb[1]);
+          Op::mma(o[nt + 1], pa, vb[2], vb[3]);
+        }
+      }
+    }
+    __syncthreads();
+    if (warp == 0 && t + AT_STAGES < ntile) issue_part(t + AT_STAGES, k_lo, k_hi, true, -1);
+  }
+  if (s_fail) {
+    if (threadIdx.x == 0)
+      atomicOr(reinterpret_cast<unsigned long long *>(st.state + KIV_ST_ERROR), 8ull);
+    return;
+  }
+  // ---- partial (out, max, sum) of every query row
+  const int Dp = partial_stride(D);
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    const int row = g + 8 * hh;
+    if (row >= rows_kv) continue;
+    const int h = kvh * G + row / Q, tq = row % Q;
+    const int64_t R_idx = ((int64_t)b * q.num_query_heads + h) * Q + tq;
+    float *dst = a.w.part + (R_idx * a.w.split_cap + split) * Dp;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt)
+      if (nt < ntw)
+        *reinterpret_cast<float2 *>(dst + dbase + nt * 8 + 2 * t4) = make_float2(o[nt][2 * hh], o[nt][2 * hh + 1]);
+    if (warp == 0 && t4 == 0) {
+      dst[D] = s_m[row];
+      dst[D + 1] = s_l[row];
+    }
+  }
+}
+
+template <typename T>
+static bool attend_mma_eligible(const kiv_store *st, const kiv_query *q) {
+  const int rows_kv = (q->num_query_heads / st->num_kv_heads) * q->query_len;
+  return sizeof(T) == 2 && rows_kv <= AM_ROWS && st->head_dim % 64 == 0 && st->head_dim <= 256 &&
+         getenv("KIV_DISABLE_MMA_ATTN") == nullptr;
+}
+
+template <typename T>
+static kiv_status launch_am(const AttnArgs<T> &a, cudaStream_t s) {
+  const int pitch = a.st.head_dim * (int)sizeof(T) + 16;
+  const size_t smem = (size_t)(AM_ROWS + 2 * AT_STAGES * ATT_TILE) * pitch + (size_t)AM_ROWS * AM_PPITCH;
+  auto kern = attend_mma_kernel<T>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const int64_t grid = (int64_t)a.st.batch * a.st.num_kv_heads * a.n_split;
+  if (grid > 0x7fffffff) return KIV_ERR_ARG;
+  return cuda_status(launch_pdl(kern, dim3((unsigned)grid), dim3(AM_THREADS), smem, s, 1, a), "attend_mma");
+}
+
 // Merge n partials per row.  Partial i of row r is at
 // part + r*row_stride + i*pstride*PSTRIDE(D): (out[D], max, sum, pad, pad).
-// One CTA per row: threads over partials for the max and the sum, then warps
-// over partials and lanes over float4 columns for the output, reduced across
-// warps in shared memory.  final_out != nullptr: write out/sum in the store
-// dtype at [B, Q, Hq, D]; otherwise write the merged (out, max, sum).
+// One CTA per (row, CB_COLS-column chunk); thread (c4, grp) folds partials
+// grp, grp + NG, ... into a running (max, sum, out) -- every load is
+// independent of the others, so the partials stream in one round trip --
+// and the NG groups are merged in a fixed order (deterministic).
+// final_out != nullptr: write out/sum in the store dtype at [B, Q, Hq, D];
+// otherwise write the merged (out, max, sum).
 template <typename T>
 __global__ void __launch_bounds__(CB_THREADS)
 combine_kernel(const float *part, int64_t row_stride, int64_t pstride, int n, int D, int Hq, int Q,
                T *final_out, float *merged) {
   griddep_wait();
-  extern __shared__ float cb_smem[];
-  float *wgt = cb_smem;                       // [n] exp(m_i - M)
-  float *red = cb_smem + ((n + 3) & ~3);      // [CB_THREADS/32][D]
-  __shared__ float s_red[CB_THREADS / 32];
-  __shared__ float s_M, s_L;
-  const int64_t row = blockIdx.x;  // (b*Hq + h)*Q + t
+  constexpr int C4 = CB_COLS / 4;              // float4 columns per chunk
+  constexpr int NG = CB_THREADS / C4;          // partial groups
+  __shared__ float4 s_acc[NG][C4];
+  __shared__ float s_m[NG][C4], s_l[NG][C4];
+  const int nch = (D + CB_COLS - 1) / CB_COLS;
+  const int64_t row = blockIdx.x / nch;        // (b*Hq + h)*Q + t
+  const int chunk = blockIdx.x % nch;
   const float *p = part + row * row_stride;
   const int Dp = partial_stride(D);
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  constexpr int NW = CB_THREADS / 32;
-  float m = -INFINITY;
-  for (int i = threadIdx.x; i < n; i += CB_THREADS) m = fmaxf(m, p[(int64_t)i * pstride * Dp + D]);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(KIV_FULL_MASK, m, o));
-  if (lane == 0) s_red[warp] = m;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float M = -INFINITY;
-    for (int w = 0; w < NW; ++w) M = fmaxf(M, s_red[w]);
-    s_M = M;
-  }
-  __syncthreads();
-  const float M = s_M;
-  float l = 0.f;
-  for (int i = threadIdx.x; i < n; i += CB_THREADS) {
+  const int c4 = threadIdx.x % C4, grp = threadIdx.x / C4;
+  const int col = chunk * CB_COLS + c4 * 4;
+  const int colc = col < D ? col : 0;          // in-bounds column for the loads
+  float m = -INFINITY, l = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+  for (int i = grp; i < n; i += NG) {
     const float *pi = p + (int64_t)i * pstride * Dp;
-    const float mi = pi[D];
-    const float wi = (mi == -INFINITY) ? 0.f : __expf(mi - M);
-    wgt[i] = wi;
-    l += pi[D + 1] * wi;
+    const float4 v = *reinterpret_cast<const float4 *>(pi + colc);
+    const float mi = pi[D], li = pi[D + 1];
+    if (mi == -INFINITY) continue;             // empty partial
+    const float mn = fmaxf(m, mi);
+    const float a = __expf(m - mn), bi = __expf(mi - mn);   // m == -inf: a = 0
+    acc.x = acc.x * a + v.x * bi;
+    acc.y = acc.y * a + v.y * bi;
+    acc.z = acc.z * a + v.z * bi;
+    acc.w = acc.w * a + v.w * bi;
+    l = l * a + li * bi;
+    m = mn;
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(KIV_FULL_MASK, l, o);
+  s_acc[grp][c4] = acc;
+  s_m[grp][c4] = m;
+  s_l[grp][c4] = l;
   __syncthreads();
-  if (lane == 0) s_red[warp] = l;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float L = 0.f;
-    for (int w = 0; w < NW; ++w) L += s_red[w];
-    s_L = L;
-  }
-  // weighted sum of the partial outputs: warp w takes partials w, w+NW, ...
-  const int nd4 = D / 4;
-  for (int c0 = 0; c0 < nd4; c0 += 32 * 2) {
-    float4 acc[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
-    for (int i = warp; i < n; i += NW) {
-      const float wi = wgt[i];
-      const float4 *pi = reinterpret_cast<const float4 *>(p + (int64_t)i * pstride * Dp);
+  if (grp != 0) return;
+  float M = -INFINITY;
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int c = c0 + lane + 32 * j;
-        if (c < nd4 && wi != 0.f) {
-          const float4 v = pi[c];
-          acc[j].x = fmaf(wi, v.x, acc[j].x);
-          acc[j].y = fmaf(wi, v.y, acc[j].y);
-          acc[j].z = fmaf(wi, v.z, acc[j].z);
-          acc[j].w = fmaf(wi, v.w, acc[j].w);
-        }
-      }
-    }
+  for (int gi = 0; gi < NG; ++gi) M = fmaxf(M, s_m[gi][c4]);
+  float L = 0.f;
+  float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const int c = c0 + lane + 32 * j;
-      if (c < nd4) reinterpret_cast<float4 *>(red + warp * D)[c] = acc[j];
-    }
+  for (int gi = 0; gi < NG; ++gi) {
+    const float mg = s_m[gi][c4];
+    const float w = mg == -INFINITY ? 0.f : __expf(mg - M);
+    const float4 u = s_acc[gi][c4];
+    t.x += u.x * w;
+    t.y += u.y * w;
+    t.z += u.z * w;
+    t.w += u.w * w;
+    L += s_l[gi][c4] * w;
   }
-  __syncthreads();
-  const float L = s_L;
-  for (int d = threadIdx.x; d < D; d += CB_THREADS) {
-    float acc = 0.f;
-#pragma unroll
-    for (int w = 0; w < NW; ++w) acc += red[w * D + d];
-    if (final_out) {
-      const int64_t t = row % Q, bh = row / Q;
-      const int64_t h = bh % Hq, b = bh / Hq;
-      final_out[((b * Q + t) * Hq + h) * D + d] = Elem<T>::from_f(L > 0.f ? acc / L : 0.f);
-    } else {
-      merged[row * Dp + d] = acc;
+  if (col >= D) return;
+  if (final_out) {
+    const int64_t tq = row % Q, bh = row / Q;
+    const int64_t h = bh % Hq, b = bh / Hq;
+    T *dst = final_out + ((b * Q + tq) * Hq + h) * D + col;
+    dst[0] = Elem<T>::from_f(L > 0.f ? t.x / L : 0.f);
+    dst[1] = Elem<T>::from_f(L > 0.f ? t.y / L : 0.f);
+    dst[2] = Elem<T>::from_f(L > 0.f ? t.z / L : 0.f);
+    dst[3] = Elem<T>::from_f(L > 0.f ? t.w / L : 0.f);
+  } else {
+    *reinterpret_cast<float4 *>(merged + row * Dp + col) = t;
+    if (chunk == 0 && c4 == 0) {
+      merged[row * Dp + D] = M;
+      merged[row * Dp + D + 1] = L;
     }
-  }
-  if (!final_out && threadIdx.x == 0) {
-    merged[row * Dp + D] = M;
-    merged[row * Dp + D + 1] = L;
   }
 }
 
 template <typename T>
 static void launch_combine(const float *part, int64_t row_stride, int64_t pstride, int n, int D, int Hq,
                            int Q, int64_t rows, T *final_out, float *merged, cudaStream_t s) {
-  const size_t smem = (size_t)(((n + 3) & ~3) + (CB_THREADS / 32) * D) * sizeof(float);
-  auto kern = combine_kernel<T>;
-  if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  launch_pdl(kern, dim3((unsigned)rows), dim3(CB_THREADS), smem, s, 1, part, row_stride, pstride, n, D, Hq, Q,
-             final_out, merged);
+  const int64_t nch = ceil_div(D, CB_COLS);
+  launch_pdl(combine_kernel<T>, dim3((unsigned)(rows * nch)), dim3(CB_THREADS), 0, s, 1, part, row_stride, pstride,
+             n, D, Hq, Q, final_out, merged);
 }
 
 template <typename T>
@@ -489,7 +881,12 @@ static kiv_status attend_t(const kiv_store *st, const kiv_query *q, const kiv_ma
   const int64_t keys_hint = std::max<int64_t>(1, (int64_t)q->top_p + expected_hot);
   a.n_split = (int)std::max<int64_t>(
       1, std::min<int64_t>({w.split_cap, ceil_div(keys_hint, ATT_TILE), ceil_div(sm_count(), base)}));
-  kiv_status rc = dispatch_at<T>(a, s);
+  kiv_status rc;
+  if constexpr (sizeof(T) == 2) {
+    rc = attend_mma_eligible<T>(st, q) ? launch_am<T>(a, s) : dispatch_at<T>(a, s);
+  } else {
+    rc = dispatch_at<T>(a, s);
+  }
   if (rc != KIV_OK) return rc;
   const int64_t rows = w.R;
   const int64_t rs = w.split_cap * partial_stride(st->head_dim);

@@ -1,5 +1,6 @@
-"""bf16 parity of the CUDA path (tcgen05 fine scoring and the CUDA-core path)
-against the oracle run on the same bf16-valued inputs in float64 math.
+"""bf16 parity of the CUDA path (tcgen05 scoring with the tensor-core attention,
+and the CUDA-core scoring and attention) against the oracle run on the same
+bf16-valued inputs in float64 math.
 
 Shapes are the c1 (Qwen2.5-7B: Hq 28 / Hkv 4 / D 128) and c2 (Gemma-style MQA:
 Hq 8 / Hkv 1 / D 256) decode shapes with a reduced cold length.  Index sets
@@ -31,8 +32,10 @@ SHAPES = {
 def test_bf16_decode_parity(shape, path, monkeypatch):
     if path == "cuda_cores":
         monkeypatch.setenv("KIV_DISABLE_TCGEN05", "1")
+        monkeypatch.setenv("KIV_DISABLE_MMA_ATTN", "1")
     else:
         monkeypatch.delenv("KIV_DISABLE_TCGEN05", raising=False)
+        monkeypatch.delenv("KIV_DISABLE_MMA_ATTN", raising=False)
     spec, knobs = SHAPES[shape]
     prob = make_problem(spec, seed=1, dtype=torch.bfloat16)
     f32 = lambda t: t.float().numpy()
