@@ -496,6 +496,8 @@ class ColdKVStore:
                 self._comm.all_gather(gathered, part)
                 nat.check(L.kiv_attend_merge(ctypes.byref(desc), ctypes.byref(qd), gathered.data_ptr(),
                                              self._shard_count, out.data_ptr(), s), "attend_merge")
+                if self._profile is not None:
+                    self._profile.record("attend_end")
         return out
 
     def _zero_selcounts(self, ws: torch.Tensor, qd: nat.QueryDesc) -> None:
@@ -523,8 +525,17 @@ class ColdKVStore:
         L = nat.lib()
         lt = self._buffer("fl_t", (B, top_p), torch.int32)
         ls = self._buffer("fl_s", (B, top_p), torch.float32)
-        nat.check(L.kiv_fine_select(ctypes.byref(desc), ctypes.byref(qd), ws.data_ptr(), ws.numel(),
-                                    lt.data_ptr(), ls.data_ptr(), s), "fine_select")
+        prof = self._profile
+        if prof is not None:
+            prof.record("fine_score_begin")
+        nat.check(L.kiv_fine_score(ctypes.byref(desc), ctypes.byref(qd), ws.data_ptr(), ws.numel(), s),
+                  "fine_score")
+        if prof is not None:
+            prof.record("fine_score_end")
+        nat.check(L.kiv_fine_topk(ctypes.byref(desc), ctypes.byref(qd), ws.data_ptr(), ws.numel(),
+                                  lt.data_ptr(), ls.data_ptr(), s), "fine_topk")
+        if prof is not None:
+            prof.record("fine_topk_end")
         n = self._shard_count
         all_t = self._buffer("fl_t_all", (n, B, top_p), torch.int32)
         all_s = self._buffer("fl_s_all", (n, B, top_p), torch.float32)

@@ -258,7 +258,7 @@ __device__ __forceinline__ void griddep_launch_dependents() {
 namespace kiv {
 
 // ---------------------------------------------------------------------------
-// 1-D bulk copies (cp.async.bulk, TMA engine, no tensor map, no multicast)
+// 1-D bulk copies (cp.async.bulk, TMA engine, no tensor map, one destination CTA)
 // completing on an mbarrier.  Waits are bounded: after ~2^31 cycles the wait
 // gives up and reports failure so the kernel can set an error bit and leave.
 // ---------------------------------------------------------------------------

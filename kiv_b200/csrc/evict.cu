@@ -44,8 +44,12 @@ append_evict_kernel(kiv_store st, const T *__restrict__ k_new, const T *__restri
   const int64_t hot_after = direct ? hot_len : hot_len + n_new - n_ev;
   bool ok = direct || (hot_len + n_new <= hcap) || (hcap == 0 && hot_len == 0 && n_ev == n_new);
   ok = ok && (direct || hot_after <= (hcap > 0 ? hcap : 0));
+  // the highest page this shard owns among those the evicted rows reach must
+  // fit its local slots
   const int64_t last_page = (cold_len + n_ev + S - 1) / S - 1;  // global page of the last evicted row
-  if (n_ev > 0 && (last_page / st.shard_count + 1) * (int64_t)S > st.cold_capacity) ok = false;
+  if (n_ev > 0 && last_page >= st.shard_rank &&
+      ((last_page - st.shard_rank) / st.shard_count + 1) * (int64_t)S > st.cold_capacity)
+    ok = false;
   // the grid covers ceil(n_evict_max / S) + 1 pages per (b, h)
   if (n_ev > n_evict_max) ok = false;
 

@@ -17,7 +17,7 @@
 //          store, and the first radix-select histogram + score stats of the
 //          batch row (so the select kernel skips its first pass).
 // The query rows are written once into shared memory in the same swizzled
-// K-major layout.  No multicast is used.  Used when the store is 16-bit,
+// K-major layout.  Every load targets only this CTA.  Used when the store is 16-bit,
 // page_size == 128, head_dim is a multiple of 64 (<= 256), batch == 1 and
 // G*Q <= 32; otherwise fine_scores_kernel runs.
 #include <algorithm>

@@ -1,5 +1,5 @@
 // sm_100a tensor-core and TMA helpers: tcgen05 (TMEM alloc, MMA, commit, ld)
-// and 2-D tensor-map bulk loads (no multicast).  Descriptor bit layouts follow
+// and 2-D tensor-map bulk loads into this CTA only.  Descriptor bit layouts follow
 // the PTX ISA for tcgen05 shared-memory matrix descriptors and the kind::f16
 // instruction descriptor.
 #pragma once
@@ -92,7 +92,7 @@ __device__ __forceinline__ void ld_32x16(uint32_t taddr, uint32_t (&r)[16]) {
 __device__ __forceinline__ void wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // ------------------------------------------------------------------ TMA
-// 2-D tiled bulk load (no multicast): box at element coordinates (x, y);
+// 2-D tiled bulk load into this CTA: box at element coordinates (x, y);
 // x * element size must be a multiple of 16 bytes.
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int32_t x, int32_t y,
                                             uint64_t *bar) {

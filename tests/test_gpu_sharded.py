@@ -1,0 +1,125 @@
+"""Page-sharded decode on 2 GPUs (NCCL) against the same step on one GPU.
+
+Two ranks (one process per GPU) build the same cache with the cold pages
+sharded ``p % 2`` and run one decode layer-step through the public surface
+(retrieve_indices, attend).  Rank 0 also runs the step unsharded on its GPU.
+The global selections must be identical (both sides use the same kernels and
+the sharded merge breaks ties like the single-GPU select: score descending,
+id ascending) and the attention outputs must agree within 1e-2 relative
+(bf16 outputs, different split/merge order).  Skipped with fewer than 2 GPUs.
+"""
+
+import os
+import socket
+import tempfile
+import time
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+WORLD = 2
+SHAPES = {
+    "c2": dict(batch=1, num_query_heads=8, num_kv_heads=1, head_dim=256, cold_tokens=32768 + 77,
+               hot_budget=2048, top_pages=32, top_p=512),
+    "c1": dict(batch=1, num_query_heads=28, num_kv_heads=4, head_dim=128, cold_tokens=16384 + 5,
+               hot_budget=1024, top_pages=16, top_p=256),
+}
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _run_step(shape, dev, shard_group):
+    from transformers import PretrainedConfig
+
+    from kiv_b200 import KIVConfig, ModelTopology, TieredKVCache
+    from kiv_b200.synthetic import SynthSpec, make_problem
+
+    p = dict(SHAPES[shape])
+    top_pages, top_p = p.pop("top_pages"), p.pop("top_p")
+    spec = SynthSpec(**p)
+    prob = make_problem(spec, seed=11, dtype=torch.bfloat16)
+    cfg = KIVConfig(hot_budget=spec.hot_budget, page_size=spec.page_size, top_pages=top_pages, top_p=top_p)
+    topo = ModelTopology.manual(global_layer_indices=(0,), independent_kv_layers=(0,), kv_sharing_map={},
+                                num_query_heads=spec.num_query_heads, num_kv_heads=spec.num_kv_heads,
+                                head_dim=spec.head_dim, num_hidden_layers=1)
+    cache = TieredKVCache(PretrainedConfig(num_hidden_layers=1), cfg, topo, dev, shard_group=shard_group)
+    t = lambda x: torch.as_tensor(x).to(dev, torch.bfloat16)
+    cache.update(t(prob.prefill_k), t(prob.prefill_v), 0)
+    cache.mark_prefill_complete()
+    cache.update(t(prob.step_k), t(prob.step_v), 0)
+    store = cache.get_cold_store(0)
+    q = prob.query.to(dev)
+    scaling = spec.head_dim ** -0.5
+    sel, P = store.retrieve_indices(q, scaling, cfg)
+    out = store.attend(q, scaling, cfg)
+    torch.cuda.synchronize(dev)
+    err = store.read_state()[7]
+    return sel[:, :P].cpu().numpy(), out.float().cpu().numpy(), int(err)
+
+
+def _worker(rank, port, out_dir, shape):
+    import datetime
+    import sys
+
+    import torch.distributed as dist
+
+    from kiv_b200.sharding import ShardComm
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    t0 = time.time()
+    log = lambda msg: print(f"[rank {rank} +{time.time() - t0:.1f}s] {msg}", file=sys.stderr, flush=True)
+    # the unsharded reference first, before any collective
+    ref = _run_step(shape, dev, None) if rank == 0 else None
+    log("single-GPU step done")
+    dist.init_process_group("nccl", rank=rank, world_size=WORLD, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    failure = None
+    try:
+        sel_sh, out_sh, err_sh = _run_step(shape, dev, ShardComm())
+        log("sharded step done")
+        if rank == 0:
+            sel_1, out_1, err_1 = ref
+            try:
+                assert err_sh == 0 and err_1 == 0, (err_sh, err_1)
+                assert sel_sh.shape == sel_1.shape, (sel_sh.shape, sel_1.shape)
+                assert np.array_equal(sel_sh, sel_1), "sharded selection differs from the single-GPU selection"
+                rel = np.abs(out_sh - out_1).max() / max(np.abs(out_1).max(), 1e-30)
+                assert rel <= 1e-2, rel
+                with open(os.path.join(out_dir, "ok"), "w") as f:
+                    f.write(f"{rel}")
+            except AssertionError as e:
+                failure = e
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+    if failure is not None:
+        raise failure
+
+
+@pytest.mark.parametrize("shape", sorted(SHAPES))
+def test_sharded_step_matches_single_gpu(shape):
+    if torch.cuda.device_count() < WORLD:
+        pytest.skip(f"needs {WORLD} GPUs")
+    import torch.multiprocessing as mp
+
+    with tempfile.TemporaryDirectory() as d:
+        ctx = mp.start_processes(_worker, args=(_free_port(), d, shape), nprocs=WORLD, join=False,
+                                 start_method="spawn")
+        deadline = time.time() + 300
+        while not ctx.join(timeout=5):
+            if time.time() > deadline:
+                for p in ctx.processes:
+                    if p.is_alive():
+                        p.kill()
+                pytest.fail("sharded ranks did not finish in 300 s")
+        assert os.path.exists(os.path.join(d, "ok"))

@@ -1,0 +1,165 @@
+"""Page-sharded retrieval on CPU ranks (gloo, world size 2).
+
+Every rank holds the same seeded problem, keeps the pages ``p % world ==
+rank`` (and, on its owner, the partial page), and runs the sharded layer-step
+the GPU path runs: local coarse top-k -> all-gather of (score, page) ->
+identical merge -> local fine top-P over its own union pages -> all-gather of
+(score, token) -> identical merge -> attention partials over its own selected
+tokens and its slice of the hot window -> all-gather -> log-sum-exp merge.
+The exchanges go through ``kiv_b200.sharding.ShardComm`` over a real gloo
+process group; the per-rank math is the oracle's.  The merged selections must
+equal the unsharded oracle's exactly and the merged attention must match it
+to 1e-12 (float64).
+"""
+
+import os
+import socket
+import tempfile
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle.kiv_oracle import OracleStore, eager_attention, topk_total_order
+
+WORLD = 2
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _problem(seed=7):
+    rng = np.random.default_rng(seed)
+    B, Hkv, G, D, S = 1, 2, 3, 32, 16
+    n_pages, partial, hot = 41, 5, 24
+    ost = OracleStore(B, Hkv, D, G, S, "f32")
+    T = n_pages * S + partial
+    k = rng.standard_normal((B, Hkv, T, D)).astype(np.float32)
+    v = rng.standard_normal((B, Hkv, T, D)).astype(np.float32)
+    ost.evict_from_hot(k, v)
+    q = rng.standard_normal((B, Hkv * G, 1, D)).astype(np.float32)
+    hk = rng.standard_normal((B, Hkv, hot, D))
+    hv = rng.standard_normal((B, Hkv, hot, D))
+    return ost, q, hk, hv
+
+
+def _merge_topk(scores: np.ndarray, ids: np.ndarray, k: int) -> np.ndarray:
+    """Global top-k of gathered (score, id) lists, ties by lowest id (invalid ids < 0)."""
+    ok = ids >= 0
+    s, i = scores[ok].astype(np.float64), ids[ok]
+    order = np.lexsort((i, -s))
+    return np.sort(i[order[:k]])
+
+
+def _worker(rank, port, out_dir):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=WORLD)
+    try:
+        from kiv_b200.sharding import ShardComm, local_page_count, shard_of_page
+        comm = ShardComm()
+        assert (comm.rank, comm.size) == (rank, WORLD)
+
+        # the wrapper's collectives on CPU tensors
+        t = torch.full((3,), float(rank + 1))
+        got = torch.empty(WORLD, 3)
+        comm.all_gather(got, t)
+        assert got[:, 0].tolist() == [1.0, 2.0]
+        comm.all_reduce_sum(t)
+        assert t.tolist() == [3.0, 3.0, 3.0]
+
+        ost, q, hk, hv = _problem()
+        scaling, top_pages, top_p = 0.25, 6, 50
+        Np, S = ost.num_pages, ost.page_size
+        owned = np.array([p for p in range(Np) if shard_of_page(p, WORLD) == rank], np.int64)
+        assert owned.size == local_page_count(Np, rank, WORLD)
+
+        # ---- coarse: local top-k per row, all-gather, merge
+        union_ref, top_ref, sc = ost.coarse(q, scaling, top_pages)
+        B, Hq, Q, _ = q.shape
+        k = min(top_pages, Np)
+        R = B * Hq * Q
+        rows = sc.reshape(R, Np)
+        ls = np.zeros((R, k), np.float64)
+        lp = np.full((R, k), -1, np.int64)
+        for r in range(R):
+            pos = topk_total_order(rows[r, owned], k)
+            ls[r, :pos.size] = rows[r, owned[pos]]
+            lp[r, :pos.size] = owned[pos]
+        all_s = torch.empty(WORLD, R, k, dtype=torch.float64)
+        all_p = torch.empty(WORLD, R, k, dtype=torch.int64)
+        comm.all_gather(all_s, torch.from_numpy(ls))
+        comm.all_gather(all_p, torch.from_numpy(lp))
+        union = set()
+        for r in range(R):
+            merged = _merge_topk(all_s[:, r].numpy().ravel(), all_p[:, r].numpy().ravel(), k)
+            assert merged.tolist() == np.sort(top_ref.reshape(R, -1)[r]).tolist()
+            union.update(merged.tolist())
+        union = np.array(sorted(union), np.int64)
+        assert union.tolist() == union_ref.tolist()
+
+        # ---- fine: own union pages (+ the partial page on its owner), local top-P, merge
+        cand_ref = ost.candidates(union)
+        agg_ref, sel_ref = ost.fine(q, scaling, cand_ref, top_p)
+        mine = np.array([c for c in cand_ref
+                         if shard_of_page(int(c) // S, WORLD) == rank], np.int64)
+        P = sel_ref.shape[1]
+        agg_mine, _ = ost.fine(q, scaling, mine, top_p) if mine.size else (np.zeros((B, 0)), None)
+        lt = np.full((B, top_p), -1, np.int64)
+        lsc = np.zeros((B, top_p), np.float64)
+        for b in range(B):
+            pos = topk_total_order(agg_mine[b], min(top_p, mine.size))
+            lt[b, :pos.size] = mine[pos]
+            lsc[b, :pos.size] = agg_mine[b, pos]
+        all_t = torch.empty(WORLD, B, top_p, dtype=torch.int64)
+        all_sc = torch.empty(WORLD, B, top_p, dtype=torch.float64)
+        comm.all_gather(all_t, torch.from_numpy(lt))
+        comm.all_gather(all_sc, torch.from_numpy(lsc))
+        for b in range(B):
+            merged = _merge_topk(all_sc[:, b].numpy().ravel(), all_t[:, b].numpy().ravel(), P)
+            assert merged.tolist() == sel_ref[b].tolist()
+
+        # ---- attention: own selected tokens + own slice of the hot window, LSE merge
+        sel_mine = [np.array([t for t in sel_ref[b] if shard_of_page(int(t) // S, WORLD) == rank], np.int64)
+                    for b in range(B)]
+        hot = hk.shape[2]
+        lo, hi = hot * rank // WORLD, hot * (rank + 1) // WORLD
+        G = Hq // ost.num_kv_heads
+        qq = q.astype(np.float64)
+        part = np.zeros((B, Hq, Q, hk.shape[3] + 2))
+        for b in range(B):
+            kc = ost.k[b][:, sel_mine[b], :].astype(np.float64)
+            vc = ost.v[b][:, sel_mine[b], :].astype(np.float64)
+            K = np.repeat(np.concatenate([kc, hk[b][:, lo:hi]], axis=1), G, axis=0)
+            V = np.repeat(np.concatenate([vc, hv[b][:, lo:hi]], axis=1), G, axis=0)
+            s = np.einsum("hqd,hkd->hqk", qq[b], K) * scaling
+            m = s.max(axis=-1) if s.shape[-1] else np.full(s.shape[:2], -np.inf)
+            p = np.exp(s - m[..., None]) if s.shape[-1] else s
+            part[b, ..., :-2] = np.einsum("hqk,hkd->hqd", p, V)
+            part[b, ..., -2] = m
+            part[b, ..., -1] = p.sum(axis=-1)
+        gathered = torch.empty((WORLD,) + part.shape, dtype=torch.float64)
+        comm.all_gather(gathered, torch.from_numpy(part))
+        g = gathered.numpy()
+        M = g[..., -2].max(axis=0)
+        w = np.exp(g[..., -2] - M)
+        out = (g[..., :-2] * w[..., None]).sum(axis=0) / (g[..., -1] * w).sum(axis=0)[..., None]
+        kr, vr = ost.gather(sel_ref)
+        ref = eager_attention(q, kr, vr, hk, hv, scaling)                  # [B, Q, Hq, D]
+        np.testing.assert_allclose(out.transpose(0, 2, 1, 3), ref, rtol=1e-12, atol=1e-12)
+        if rank == 0:
+            with open(os.path.join(out_dir, "ok"), "w") as f:
+                f.write("ok")
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_layer_step_on_gloo_ranks():
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_worker, args=(_free_port(), d), nprocs=WORLD, join=True, start_method="spawn")
+        assert os.path.exists(os.path.join(d, "ok"))
