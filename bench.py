@@ -86,13 +86,17 @@ def measured_peak():
     return 6650.0, "fallback"
 
 
-def committed_traffic(workload):
-    p = os.path.join(ROOT, "profiles", "fine_score_traffic.json")
-    if os.path.exists(p):
-        with open(p) as f:
-            j = json.load(f)
-        return j.get(workload)
-    return None
+# DRAM bytes (read + write) per algorithmic byte of one fine-scoring launch,
+# from the ncu capture of scores_tc_kernel<1, 0> on the c2s workload (profiles
+# directory): 32,821,760 B of traffic for 32,683,179 algorithmic bytes.  The
+# traffic grows with the pages a launch scores, so a launch of another size
+# (c2, a shard of it) is scaled by its own algorithmic bytes.
+FINE_TRAFFIC_PER_ALG_BYTE = {"c2": 32_821_760 / 32_683_179, "c2s": 32_821_760 / 32_683_179}
+
+
+def committed_traffic(workload, alg_bytes):
+    r = FINE_TRAFFIC_PER_ALG_BYTE.get(workload)
+    return None if r is None else r * alg_bytes
 
 
 def smi_id(dev):
@@ -487,9 +491,9 @@ def main():
             "gpu_launches": int(K * L * (7 if world == 1 else 10)),
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "api": "kiv_b200.decode_graph.DecodeGraph.replay with pinned host inputs/outputs"},
-            "roofline": {"bound": "hbm", "kernel": "fine_scores_kernel (fine token scoring)",
+            "roofline": {"bound": "hbm", "kernel": "scores_tc_kernel<bf16, fine> (tcgen05 fine token scoring)",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "peak_kind": peak_kind, "traffic": committed_traffic(args.workload),
+                         "peak_kind": peak_kind, "traffic": committed_traffic(args.workload, fine_bytes_avg),
                          "algorithmic_bytes_per_launch": fine_bytes_avg,
                          "avg_launch_us": fine_avg_ms * 1e3, "launches_timed": n_launch,
                          "mean_union_pages": U_mean},
