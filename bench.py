@@ -507,6 +507,8 @@ def main():
         }
     graph = None
     if world > 1:
+        torch.cuda.synchronize(dev)
+        comm.close()
         dist.barrier()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, n, el, threads = cpu_oracle_rate(w, cpu_oracle_layer(w), seconds=12.0)

@@ -248,6 +248,53 @@ KIV_API kiv_status kiv_retrieve_attend_noalloc(const kiv_store *st, const kiv_qu
                                                const kiv_mask *mask, int32_t *sel, void *out,
                                                void *stream);
 
+/*
+ * Peer-memory exchange for sharded runs (one process per GPU of one box).
+ * No counterpart in the reference (it has no multi-GPU code); replaces the
+ * NCCL all-gathers of the sharded layer-step.
+ *
+ * Every rank allocates an exchange arena of kiv_exchange_bytes() with
+ * kiv_peer_alloc (device memory, zeroed, exported as an IPC handle of
+ * KIV_IPC_HANDLE_BYTES), the ranks swap the handles over any host channel,
+ * and each rank maps the others' arenas with kiv_peer_open.  The
+ * *_exchange_merge calls then store this rank's lists straight into every
+ * rank's arena over NVLink, raise a per-source counter there (release
+ * ordering at system scope), wait for every rank's lists (acquire; each wait
+ * is bounded, a timeout sets KIV_ERRBIT_WAIT_TIMEOUT in the state) and merge,
+ * all in one kernel.  Every rank must make the same sequence of these calls
+ * with the same shapes.  An arena serves one (store shape, query shape);
+ * stores of the same shape may share it when their calls are stream-ordered.
+ */
+#define KIV_MAX_PEERS 8
+#define KIV_IPC_HANDLE_BYTES 64
+typedef struct kiv_exchange {
+  int32_t world;                  /* ranks (== kiv_store.shard_count), <= KIV_MAX_PEERS */
+  int32_t rank;                   /* this rank (== kiv_store.shard_rank) */
+  void *arena[KIV_MAX_PEERS];     /* every rank's arena as mapped in this process */
+  int64_t arena_bytes;            /* size of every arena */
+} kiv_exchange;
+
+KIV_API size_t kiv_exchange_bytes(const kiv_store *st, const kiv_query *q, int32_t world);
+KIV_API kiv_status kiv_peer_alloc(size_t bytes, void **dev_ptr, void *ipc_handle);
+KIV_API kiv_status kiv_peer_open(const void *ipc_handle, void **dev_ptr);
+KIV_API kiv_status kiv_peer_close(void *dev_ptr);
+KIV_API kiv_status kiv_peer_free(void *dev_ptr);
+
+/* kiv_coarse_merge with the lists exchanged through the arenas: row_scores /
+ * row_pages are this rank's lists from kiv_coarse_select. */
+KIV_API kiv_status kiv_coarse_exchange_merge(const kiv_store *st, const kiv_query *q, void *ws, size_t ws_bytes,
+                                             const float *row_scores, const int32_t *row_pages,
+                                             const kiv_exchange *x, void *stream);
+/* kiv_fine_merge with the lists exchanged through the arenas: scores /
+ * tokens are this rank's lists from kiv_fine_select (or kiv_fine_topk). */
+KIV_API kiv_status kiv_fine_exchange_merge(const kiv_store *st, const kiv_query *q, void *ws, size_t ws_bytes,
+                                           const float *scores, const int32_t *tokens, const kiv_exchange *x,
+                                           int32_t *sel, int32_t *sel_local, void *stream);
+/* kiv_attend_merge with the partials exchanged through the arenas: partial is
+ * this rank's [B*Hq*Q, D + 4] from kiv_attend. */
+KIV_API kiv_status kiv_attend_exchange_merge(const kiv_store *st, const kiv_query *q, const float *partial,
+                                             const kiv_exchange *x, void *out, void *stream);
+
 /* Copy the store's device state words to host memory (synchronizes the stream). */
 KIV_API kiv_status kiv_read_state(const kiv_store *st, int64_t *host_words, void *stream);
 

@@ -52,6 +52,14 @@ class MaskDesc(ctypes.Structure):
                 ("causal", c_i32), ("reserved", c_i32)]
 
 
+MAX_PEERS = 8
+IPC_HANDLE_BYTES = 64
+
+
+class ExchangeDesc(ctypes.Structure):
+    _fields_ = [("world", c_i32), ("rank", c_i32), ("arena", c_vp * MAX_PEERS), ("arena_bytes", c_i64)]
+
+
 P = ctypes.POINTER
 # name -> (restype, argtypes)
 SIGNATURES = {
@@ -76,6 +84,16 @@ SIGNATURES = {
                                     c_vp, c_vp]),
     "kiv_retrieve_attend_noalloc": (c_i32, [P(StoreDesc), P(QueryDesc), P(MaskDesc), c_vp, c_vp, c_vp]),
     "kiv_read_state": (c_i32, [P(StoreDesc), P(c_i64), c_vp]),
+    "kiv_exchange_bytes": (c_sz, [P(StoreDesc), P(QueryDesc), c_i32]),
+    "kiv_peer_alloc": (c_i32, [c_sz, P(c_vp), c_vp]),
+    "kiv_peer_open": (c_i32, [c_vp, P(c_vp)]),
+    "kiv_peer_close": (c_i32, [c_vp]),
+    "kiv_peer_free": (c_i32, [c_vp]),
+    "kiv_coarse_exchange_merge": (c_i32, [P(StoreDesc), P(QueryDesc), c_vp, c_sz, c_vp, c_vp, P(ExchangeDesc),
+                                          c_vp]),
+    "kiv_fine_exchange_merge": (c_i32, [P(StoreDesc), P(QueryDesc), c_vp, c_sz, c_vp, c_vp, P(ExchangeDesc),
+                                        c_vp, c_vp, c_vp]),
+    "kiv_attend_exchange_merge": (c_i32, [P(StoreDesc), P(QueryDesc), c_vp, P(ExchangeDesc), c_vp, c_vp]),
 }
 
 _lib = None

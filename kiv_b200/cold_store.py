@@ -24,6 +24,7 @@ from __future__ import annotations
 
 import ctypes
 import math
+import os
 
 import torch
 
@@ -492,10 +493,16 @@ class ColdKVStore:
                                        ws.data_ptr(), ws.numel(), sel_local.data_ptr(),
                                        sel_local.shape[1], self._shard_rank, self._shard_count,
                                        None, part.data_ptr(), s), "attend")
-                gathered = self._buffer("apart_all", (self._shard_count, R, D + 4), torch.float32)
-                self._comm.all_gather(gathered, part)
-                nat.check(L.kiv_attend_merge(ctypes.byref(desc), ctypes.byref(qd), gathered.data_ptr(),
-                                             self._shard_count, out.data_ptr(), s), "attend_merge")
+                x = self._exchange(desc, qd)
+                if x is not None:
+                    nat.check(L.kiv_attend_exchange_merge(ctypes.byref(desc), ctypes.byref(qd), part.data_ptr(),
+                                                          ctypes.byref(x), out.data_ptr(), s),
+                              "attend_exchange_merge")
+                else:
+                    gathered = self._buffer("apart_all", (self._shard_count, R, D + 4), torch.float32)
+                    self._comm.all_gather(gathered, part)
+                    nat.check(L.kiv_attend_merge(ctypes.byref(desc), ctypes.byref(qd), gathered.data_ptr(),
+                                                 self._shard_count, out.data_ptr(), s), "attend_merge")
                 if self._profile is not None:
                     self._profile.record("attend_end")
         return out
@@ -507,12 +514,28 @@ class ColdKVStore:
         ws[lay[4]:lay[4] + 4 * self._batch].zero_()
 
     # ---------------------------------------------------------- sharded steps
+    def _exchange(self, desc, qd):
+        """Peer-memory exchange descriptor for this query shape, or None when the
+        process group's collectives are used (``KIV_SHARD_EXCHANGE=collective``)."""
+        if os.environ.get("KIV_SHARD_EXCHANGE", "peer") == "collective":
+            return None
+        nbytes = nat.lib().kiv_exchange_bytes(ctypes.byref(desc), ctypes.byref(qd), self._shard_count)
+        if nbytes == 0:
+            raise nat.KIVNativeError("kiv_exchange_bytes rejected the store/query shape")
+        return self._comm.exchange(nbytes, self.device)
+
     def _sharded_coarse(self, desc, qd, ws, R: int, K: int, s: int) -> None:
         L = nat.lib()
         sc = self._buffer("crow_s", (R, K), torch.float32)
         pg = self._buffer("crow_p", (R, K), torch.int32)
         nat.check(L.kiv_coarse_select(ctypes.byref(desc), ctypes.byref(qd), ws.data_ptr(), ws.numel(),
                                       sc.data_ptr(), pg.data_ptr(), s), "coarse_select")
+        x = self._exchange(desc, qd)
+        if x is not None:
+            nat.check(L.kiv_coarse_exchange_merge(ctypes.byref(desc), ctypes.byref(qd), ws.data_ptr(), ws.numel(),
+                                                  sc.data_ptr(), pg.data_ptr(), ctypes.byref(x), s),
+                      "coarse_exchange_merge")
+            return
         n = self._shard_count
         all_s = self._buffer("crow_s_all", (n, R, K), torch.float32)
         all_p = self._buffer("crow_p_all", (n, R, K), torch.int32)
@@ -536,12 +559,18 @@ class ColdKVStore:
                                   lt.data_ptr(), ls.data_ptr(), s), "fine_topk")
         if prof is not None:
             prof.record("fine_topk_end")
+        sel_local = self._buffer("sel_local", (B, top_p), torch.int32)
+        x = self._exchange(desc, qd)
+        if x is not None:
+            nat.check(L.kiv_fine_exchange_merge(ctypes.byref(desc), ctypes.byref(qd), ws.data_ptr(), ws.numel(),
+                                                ls.data_ptr(), lt.data_ptr(), ctypes.byref(x), sel.data_ptr(),
+                                                sel_local.data_ptr(), s), "fine_exchange_merge")
+            return sel_local
         n = self._shard_count
         all_t = self._buffer("fl_t_all", (n, B, top_p), torch.int32)
         all_s = self._buffer("fl_s_all", (n, B, top_p), torch.float32)
         self._comm.all_gather(all_t, lt)
         self._comm.all_gather(all_s, ls)
-        sel_local = self._buffer("sel_local", (B, top_p), torch.int32)
         nat.check(L.kiv_fine_merge(ctypes.byref(desc), ctypes.byref(qd), ws.data_ptr(), ws.numel(),
                                    all_s.data_ptr(), all_t.data_ptr(), n, sel.data_ptr(),
                                    sel_local.data_ptr(), s), "fine_merge")

@@ -5,6 +5,7 @@
 
 #include <algorithm>
 
+#include "exchange.cuh"
 #include "internal.h"
 
 namespace kiv {
@@ -313,6 +314,115 @@ kiv_status kiv_retrieve_attend(const kiv_store *st, const kiv_query *q, const ki
   if (!reuse) KIV_TRY(launch_coarse(st, q, w, nullptr, nullptr, s));
   KIV_TRY(launch_fine(st, q, w, sel, nullptr, s));
   return launch_attend(st, q, mask, w, sel, q->top_p, 0, 1, out, nullptr, s);
+}
+
+// ---------------------------------------------------------------- exchange
+size_t kiv_exchange_bytes(const kiv_store *st, const kiv_query *q, int32_t world) {
+  if (check_store(st) != KIV_OK || check_query(st, q) != KIV_OK || world < 1 || world > KIV_MAX_PEERS) return 0;
+  int64_t cb, fb, ab;
+  exchange_payloads(st, q, &cb, &fb, &ab);
+  return (size_t)x_layout(cb, fb, ab, world).total;
+}
+
+kiv_status kiv_peer_alloc(size_t bytes, void **dev_ptr, void *ipc_handle) {
+  if (!dev_ptr || !ipc_handle || bytes == 0) { set_error("bad peer_alloc arguments"); return KIV_ERR_ARG; }
+  static_assert(sizeof(cudaIpcMemHandle_t) <= KIV_IPC_HANDLE_BYTES, "IPC handle size");
+  void *p = nullptr;
+  KIV_TRY(cuda_status(cudaMalloc(&p, bytes), "peer_alloc: cudaMalloc"));
+  kiv_status rc = cuda_status(cudaMemset(p, 0, bytes), "peer_alloc: cudaMemset");
+  cudaIpcMemHandle_t h;
+  if (rc == KIV_OK) rc = cuda_status(cudaIpcGetMemHandle(&h, p), "peer_alloc: cudaIpcGetMemHandle");
+  if (rc != KIV_OK) {
+    cudaFree(p);
+    return rc;
+  }
+  memset(ipc_handle, 0, KIV_IPC_HANDLE_BYTES);
+  memcpy(ipc_handle, &h, sizeof(h));
+  *dev_ptr = p;
+  return KIV_OK;
+}
+
+kiv_status kiv_peer_open(const void *ipc_handle, void **dev_ptr) {
+  if (!dev_ptr || !ipc_handle) { set_error("bad peer_open arguments"); return KIV_ERR_ARG; }
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  return cuda_status(cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess), "peer_open");
+}
+
+kiv_status kiv_peer_close(void *dev_ptr) { return cuda_status(cudaIpcCloseMemHandle(dev_ptr), "peer_close"); }
+
+kiv_status kiv_peer_free(void *dev_ptr) { return cuda_status(cudaFree(dev_ptr), "peer_free"); }
+
+static kiv_status check_exchange(const kiv_store *st, const kiv_query *q, const kiv_exchange *x, int t,
+                                 int64_t ctas, kiv::XArgs &a) {
+  if (!x || x->world != st->shard_count || x->rank != st->shard_rank || x->world < 1 ||
+      x->world > KIV_MAX_PEERS) {
+    set_error("exchange descriptor does not match the store's shard (rank/world)");
+    return KIV_ERR_ARG;
+  }
+  int64_t cb, fb, ab;
+  exchange_payloads(st, q, &cb, &fb, &ab);
+  const kiv::XLayout L = x_layout(cb, fb, ab, x->world);
+  if (x->arena_bytes < L.total) {
+    set_error("exchange arena of %lld bytes, this shape needs %lld", (long long)x->arena_bytes,
+              (long long)L.total);
+    return KIV_ERR_CAPACITY;
+  }
+  // every CTA of a launch waits for every rank's CTAs: all must be resident
+  if (ctas > sm_count()) {
+    set_error("exchange merge of %lld CTAs exceeds the %d SMs", (long long)ctas, sm_count());
+    return KIV_ERR_UNSUPPORTED;
+  }
+  a = kiv::XArgs{};
+  a.world = x->world;
+  a.rank = x->rank;
+  for (int i = 0; i < x->world; ++i) {
+    if (!x->arena[i] || (reinterpret_cast<uintptr_t>(x->arena[i]) & 255)) {
+      set_error("exchange arena %d missing or misaligned", i);
+      return KIV_ERR_ARG;
+    }
+    a.arena[i] = static_cast<char *>(x->arena[i]);
+  }
+  a.off = L.off[t];
+  a.par_bytes = L.par[t];
+  return KIV_OK;
+}
+
+kiv_status kiv_coarse_exchange_merge(const kiv_store *st, const kiv_query *q, void *ws, size_t ws_bytes,
+                                     const float *row_scores, const int32_t *row_pages, const kiv_exchange *x,
+                                     void *stream) {
+  KIV_TRY(check_store(st));
+  KIV_TRY(check_query(st, q));
+  Workspace w;
+  KIV_TRY(check_ws(st, q, ws, ws_bytes, w));
+  if (!row_scores || !row_pages) { set_error("bad merge lists"); return KIV_ERR_ARG; }
+  kiv::XArgs a;
+  KIV_TRY(check_exchange(st, q, x, kiv::X_COARSE, w.R, a));
+  return launch_coarse_merge(st, q, w, row_scores, row_pages, x->world, (cudaStream_t)stream, &a);
+}
+
+kiv_status kiv_fine_exchange_merge(const kiv_store *st, const kiv_query *q, void *ws, size_t ws_bytes,
+                                   const float *scores, const int32_t *tokens, const kiv_exchange *x,
+                                   int32_t *sel, int32_t *sel_local, void *stream) {
+  KIV_TRY(check_store(st));
+  KIV_TRY(check_query(st, q));
+  Workspace w;
+  KIV_TRY(check_ws(st, q, ws, ws_bytes, w));
+  if (!scores || !tokens || !sel || !sel_local) { set_error("bad fine merge arguments"); return KIV_ERR_ARG; }
+  kiv::XArgs a;
+  KIV_TRY(check_exchange(st, q, x, kiv::X_FINE, st->batch, a));
+  return launch_fine_merge(st, q, w, scores, tokens, x->world, sel, sel_local, (cudaStream_t)stream, &a);
+}
+
+kiv_status kiv_attend_exchange_merge(const kiv_store *st, const kiv_query *q, const float *partial,
+                                     const kiv_exchange *x, void *out, void *stream) {
+  KIV_TRY(check_store(st));
+  KIV_TRY(check_query(st, q));
+  if (!partial || !out) { set_error("bad attend_merge arguments"); return KIV_ERR_ARG; }
+  const int64_t rows = (int64_t)st->batch * q->num_query_heads * q->query_len;
+  kiv::XArgs a;
+  KIV_TRY(check_exchange(st, q, x, kiv::X_ATTN, rows * ceil_div(st->head_dim, 64), a));
+  return launch_attend_merge(st, q, partial, x->world, out, (cudaStream_t)stream, &a);
 }
 
 kiv_status kiv_read_state(const kiv_store *st, int64_t *host_words, void *stream) {

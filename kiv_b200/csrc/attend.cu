@@ -15,6 +15,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "exchange.cuh"
 #include "internal.h"
 
 namespace kiv {
@@ -715,10 +716,10 @@ static kiv_status launch_am(const AttnArgs<T> &a, cudaStream_t s) {
 // and the NG groups are merged in a fixed order (deterministic).
 // final_out != nullptr: write out/sum in the store dtype at [B, Q, Hq, D];
 // otherwise write the merged (out, max, sum).
-template <typename T>
+template <typename T, bool X>
 __global__ void __launch_bounds__(CB_THREADS)
 combine_kernel(const float *part, int64_t row_stride, int64_t pstride, int n, int D, int Hq, int Q,
-               T *final_out, float *merged) {
+               T *final_out, float *merged, XArgs x, const float *mine, int64_t rows, int64_t *state) {
   griddep_wait();
   constexpr int C4 = CB_COLS / 4;              // float4 columns per chunk
   constexpr int NG = CB_THREADS / C4;          // partial groups
@@ -727,8 +728,29 @@ combine_kernel(const float *part, int64_t row_stride, int64_t pstride, int n, in
   const int nch = (D + CB_COLS - 1) / CB_COLS;
   const int64_t row = blockIdx.x / nch;        // (b*Hq + h)*Q + t
   const int chunk = blockIdx.x % nch;
-  const float *p = part + row * row_stride;
   const int Dp = partial_stride(D);
+  unsigned long long e = 0;
+  if (X) {
+    // this rank's partial of this (row, column chunk) -> slot [rank] of every
+    // arena; then wait for every rank's partials in this rank's arena
+    e = x_epoch(x, X_ATTN);
+    const int c0 = chunk * CB_COLS, c1 = min(D, c0 + CB_COLS);
+    const float *src = mine + row * Dp;
+    for (int d = 0; d < x.world; ++d) {
+      float *dst = reinterpret_cast<float *>(x_region(x, d, e)) + ((int64_t)x.rank * rows + row) * Dp;
+      for (int c = c0 + threadIdx.x; c < c1; c += CB_THREADS) dst[c] = src[c];
+      if (chunk == 0 && threadIdx.x < 2) dst[D + threadIdx.x] = src[D + threadIdx.x];
+    }
+    x_signal(x, X_ATTN);
+    if (!x_wait(x, X_ATTN, (e + 1) * gridDim.x) && threadIdx.x == 0)
+      atomicOr(reinterpret_cast<unsigned long long *>(state + KIV_ST_ERROR),
+               (unsigned long long)KIV_ERRBIT_WAIT_TIMEOUT);
+    part = reinterpret_cast<const float *>(x_region(x, x.rank, e));
+    row_stride = Dp;
+    pstride = rows;
+    n = x.world;
+  }
+  const float *p = part + row * row_stride;
   const int c4 = threadIdx.x % C4, grp = threadIdx.x / C4;
   const int col = chunk * CB_COLS + c4 * 4;
   const int colc = col < D ? col : 0;          // in-bounds column for the loads
@@ -737,8 +759,8 @@ combine_kernel(const float *part, int64_t row_stride, int64_t pstride, int n, in
 #pragma unroll 4
   for (int i = grp; i < n; i += NG) {
     const float *pi = p + (int64_t)i * pstride * Dp;
-    const float4 v = *reinterpret_cast<const float4 *>(pi + colc);
-    const float mi = pi[D], li = pi[D + 1];
+    const float4 v = __ldcg(reinterpret_cast<const float4 *>(pi + colc));
+    const float mi = __ldcg(pi + D), li = __ldcg(pi + D + 1);
     if (mi == -INFINITY) continue;             // empty partial
     const float mn = fmaxf(m, mi);
     const float a = __expf(m - mn), bi = __expf(mi - mn);   // m == -inf: a = 0
@@ -753,6 +775,7 @@ combine_kernel(const float *part, int64_t row_stride, int64_t pstride, int n, in
   s_m[grp][c4] = m;
   s_l[grp][c4] = l;
   __syncthreads();
+  if (X) x_advance(x, X_ATTN, e);   // every CTA has read its inputs from the arena
   if (grp != 0) return;
   float M = -INFINITY;
 #pragma unroll
@@ -792,8 +815,8 @@ template <typename T>
 static void launch_combine(const float *part, int64_t row_stride, int64_t pstride, int n, int D, int Hq,
                            int Q, int64_t rows, T *final_out, float *merged, cudaStream_t s) {
   const int64_t nch = ceil_div(D, CB_COLS);
-  launch_pdl(combine_kernel<T>, dim3((unsigned)(rows * nch)), dim3(CB_THREADS), 0, s, 1, part, row_stride, pstride,
-             n, D, Hq, Q, final_out, merged);
+  launch_pdl(combine_kernel<T, false>, dim3((unsigned)(rows * nch)), dim3(CB_THREADS), 0, s, 1, part, row_stride,
+             pstride, n, D, Hq, Q, final_out, merged, XArgs{}, (const float *)nullptr, rows, (int64_t *)nullptr);
 }
 
 template <typename T>
@@ -912,9 +935,26 @@ kiv_status launch_attend(const kiv_store *st, const kiv_query *q, const kiv_mask
 }
 
 kiv_status launch_attend_merge(const kiv_store *st, const kiv_query *q, const float *partials,
-                               int32_t n, void *out, cudaStream_t s) {
+                               int32_t n, void *out, cudaStream_t s, const XArgs *x) {
   const int64_t rows = (int64_t)st->batch * q->num_query_heads * q->query_len;
   const int D = st->head_dim, Dp = partial_stride(D);
+  if (x) {
+    // partials: this rank's [R, Dp]; the ranks' partials meet in the arenas
+    const int64_t nch = ceil_div(D, CB_COLS);
+    const dim3 grid((unsigned)(rows * nch));
+#define KIV_XC(TT)                                                                                         \
+  launch_pdl(combine_kernel<TT, true>, grid, dim3(CB_THREADS), 0, s, 1, (const float *)nullptr, (int64_t)Dp,      \
+             rows, x->world, D, q->num_query_heads, q->query_len, (TT *)out, (float *)nullptr, *x, partials, rows, \
+             st->state)
+    switch (st->dtype) {
+      case KIV_DTYPE_F32: KIV_XC(float); break;
+      case KIV_DTYPE_BF16: KIV_XC(__nv_bfloat16); break;
+      case KIV_DTYPE_F16: KIV_XC(__half); break;
+      default: return KIV_ERR_UNSUPPORTED;
+    }
+#undef KIV_XC
+    return cuda_status(cudaGetLastError(), "attend_exchange_merge");
+  }
   // partials [n, R, Dp]: row r of partial i at (i*R + r)*Dp
   switch (st->dtype) {
     case KIV_DTYPE_F32:
@@ -933,6 +973,14 @@ kiv_status launch_attend_merge(const kiv_store *st, const kiv_query *q, const fl
       return KIV_ERR_UNSUPPORTED;
   }
   return cuda_status(cudaGetLastError(), "attend_merge");
+}
+
+// per-rank payload bytes of the three exchanges
+void exchange_payloads(const kiv_store *st, const kiv_query *q, int64_t *cb, int64_t *fb, int64_t *ab) {
+  const int64_t R = (int64_t)st->batch * q->num_query_heads * q->query_len;
+  *cb = R * q->top_pages * 8;
+  *fb = (int64_t)st->batch * q->top_p * 8;
+  *ab = R * partial_stride(st->head_dim) * 4;
 }
 
 kiv_status launch_gather(const kiv_store *st, const int32_t *sel, int32_t sel_stride, int32_t P,

@@ -12,6 +12,7 @@
 
 #include "common.cuh"
 #include "internal.h"
+#include "exchange.cuh"
 #include "select.cuh"
 
 namespace kiv {
@@ -271,9 +272,10 @@ kiv_status launch_union(const kiv_store *st, const Workspace &w, cudaStream_t s)
 // Merge gathered per-row lists [n][R][K] into the global per-row top-k and
 // keep the union pages this shard owns.  Ties at the threshold are broken by
 // the lowest page id.
+template <bool X>
 __global__ void __launch_bounds__(CM_THREADS)
-coarse_merge_kernel(kiv_store st, kiv_query q, Workspace w, const float *ls, const int32_t *lp,
-                    int32_t n) {
+coarse_merge_kernel(kiv_store st, kiv_query q, Workspace w, const float *ls, const int32_t *lp, int32_t n,
+                    XArgs x, const float *mine_s, const int32_t *mine_p) {
   griddep_wait();
   extern __shared__ uint4 dyn_smem[];
   __shared__ SelectSmem<CM_THREADS> sm;
@@ -282,15 +284,38 @@ coarse_merge_kernel(kiv_store st, kiv_query q, Workspace w, const float *ls, con
   const int row = blockIdx.x;
   const int K = q.top_pages;
   const int64_t R = w.R;
+  unsigned long long e = 0;
+  if (X) {
+    // this rank's list of this row -> slot [rank] of every arena; then wait
+    // for every rank's lists in this rank's arena
+    e = x_epoch(x, X_COARSE);
+    const int64_t nf = (int64_t)x.world * R * K;   // floats of a parity, then as many ints
+    for (int d = 0; d < x.world; ++d) {
+      float *fs = reinterpret_cast<float *>(x_region(x, d, e));
+      int32_t *ip = reinterpret_cast<int32_t *>(fs + nf);
+      for (int j = threadIdx.x; j < K; j += CM_THREADS) {
+        const int64_t off = ((int64_t)x.rank * R + row) * K + j;
+        fs[off] = mine_s[(int64_t)row * K + j];
+        ip[off] = mine_p[(int64_t)row * K + j];
+      }
+    }
+    x_signal(x, X_COARSE);
+    if (!x_wait(x, X_COARSE, (e + 1) * gridDim.x) && threadIdx.x == 0)
+      atomicOr(reinterpret_cast<unsigned long long *>(st.state + KIV_ST_ERROR),
+               (unsigned long long)KIV_ERRBIT_WAIT_TIMEOUT);
+    ls = reinterpret_cast<const float *>(x_region(x, x.rank, e));
+    lp = reinterpret_cast<const int32_t *>(ls + nf);
+    n = x.world;
+  }
   const int m = n * K;
   uint32_t *keys = reinterpret_cast<uint32_t *>(dyn_smem);
   int32_t *ids = reinterpret_cast<int32_t *>(keys + m);
   for (int i = threadIdx.x; i < m; i += CM_THREADS) {
     const int src = i / K, j = i % K;
     const int64_t off = ((int64_t)src * R + row) * K + j;
-    const int32_t pg = lp[off];
+    const int32_t pg = __ldcg(lp + off);
     ids[i] = pg;
-    keys[i] = pg >= 0 ? f2key(ls[off]) : 0u;
+    keys[i] = pg >= 0 ? f2key(__ldcg(ls + off)) : 0u;
   }
   __syncthreads();
   const uint32_t k = (uint32_t)(K < np_global ? (int64_t)K : np_global);
@@ -306,14 +331,14 @@ coarse_merge_kernel(kiv_store st, kiv_query q, Workspace w, const float *ls, con
           rank += (keys[j] == T && ids[j] >= 0 && ids[j] < ids[i]) ? 1u : 0u;
         take = rank < need;
       }
-      if (take && ids[i] >= 0 && (ids[i] % st.shard_count) == st.shard_rank)
-      {
-        const int32_t lp = ids[i] / st.shard_count;
-        atomicOr(&w.pbits[lp >> 5], 1u << (lp & 31));
+      if (take && ids[i] >= 0 && (ids[i] % st.shard_count) == st.shard_rank) {
+        const int32_t lpg = ids[i] / st.shard_count;
+        atomicOr(&w.pbits[lpg >> 5], 1u << (lpg & 31));
       }
     }
   }
   if (row == 0 && threadIdx.x == 0) st.state[KIV_ST_UNION_PENDING] = 1;
+  if (X) x_advance(x, X_COARSE, e);
 }
 
 template <typename T, int LPR, int VPL, int RCH>
@@ -382,12 +407,21 @@ kiv_status launch_coarse(const kiv_store *st, const kiv_query *q, const Workspac
 }
 
 kiv_status launch_coarse_merge(const kiv_store *st, const kiv_query *q, const Workspace &w,
-                               const float *ls, const int32_t *lp, int32_t n, cudaStream_t s) {
-  const size_t smem = (size_t)n * q->top_pages * (sizeof(uint32_t) + sizeof(int32_t));
+                               const float *ls, const int32_t *lp, int32_t n, cudaStream_t s,
+                               const XArgs *x) {
+  const int nl = x ? x->world : n;
+  const size_t smem = (size_t)nl * q->top_pages * (sizeof(uint32_t) + sizeof(int32_t));
   if (smem > 200 * 1024) return KIV_ERR_CAPACITY;
-  cudaFuncSetAttribute(coarse_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  const cudaError_t e = launch_pdl(coarse_merge_kernel, dim3((unsigned)w.R), dim3(CM_THREADS), smem, s, 1, *st,
-                                   *q, w, ls, lp, n);
+  cudaError_t e;
+  if (x) {
+    cudaFuncSetAttribute(coarse_merge_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    e = launch_pdl(coarse_merge_kernel<true>, dim3((unsigned)w.R), dim3(CM_THREADS), smem, s, 1, *st, *q, w,
+                   (const float *)nullptr, (const int32_t *)nullptr, nl, *x, ls, lp);
+  } else {
+    cudaFuncSetAttribute(coarse_merge_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    e = launch_pdl(coarse_merge_kernel<false>, dim3((unsigned)w.R), dim3(CM_THREADS), smem, s, 1, *st, *q, w, ls,
+                   lp, n, XArgs{}, (const float *)nullptr, (const int32_t *)nullptr);
+  }
   if (e != cudaSuccess) return cuda_status(e, "coarse_merge");
   return cuda_status(cudaGetLastError(), "coarse_merge");
 }

@@ -16,6 +16,7 @@
 
 #include "common.cuh"
 #include "internal.h"
+#include "exchange.cuh"
 #include "select.cuh"
 
 namespace kiv {
@@ -443,15 +444,40 @@ __device__ void list_prefix(const uint8_t *flag, int n, int L, int32_t *pre) {
 // Merge n gathered lists [n][B][top_p] (ascending ids, tail -1) into the
 // global top-P of each batch row; sel gets all of them (ascending ids),
 // sel_local the ones this shard owns (list index == shard rank).
+template <bool X>
 __global__ void __launch_bounds__(FM_THREADS)
 fine_merge_kernel(kiv_store st, kiv_query q, Workspace w, const float *ls, const int32_t *lt,
-                  int32_t n, int32_t *sel, int32_t *sel_local) {
+                  int32_t n, int32_t *sel, int32_t *sel_local, XArgs x, const float *mine_s,
+                  const int32_t *mine_t) {
   griddep_wait();
   extern __shared__ uint4 fm_dyn[];
   __shared__ SelectSmem<FM_THREADS> sm;
   __shared__ int s_valid[64];
   const int b = blockIdx.x;
   const int L = q.top_p, B = st.batch;
+  unsigned long long e = 0;
+  if (X) {
+    // this rank's list of batch row b -> slot [rank] of every arena (tokens,
+    // then scores); then wait for every rank's lists in this rank's arena
+    e = x_epoch(x, X_FINE);
+    const int64_t ni = (int64_t)x.world * B * L;
+    for (int d = 0; d < x.world; ++d) {
+      int32_t *it = reinterpret_cast<int32_t *>(x_region(x, d, e));
+      float *fs = reinterpret_cast<float *>(it + ni);
+      for (int a = threadIdx.x; a < L; a += FM_THREADS) {
+        const int64_t off = ((int64_t)x.rank * B + b) * L + a;
+        it[off] = mine_t[(int64_t)b * L + a];
+        fs[off] = mine_s[(int64_t)b * L + a];
+      }
+    }
+    x_signal(x, X_FINE);
+    if (!x_wait(x, X_FINE, (e + 1) * gridDim.x) && threadIdx.x == 0)
+      atomicOr(reinterpret_cast<unsigned long long *>(st.state + KIV_ST_ERROR),
+               (unsigned long long)KIV_ERRBIT_WAIT_TIMEOUT);
+    lt = reinterpret_cast<const int32_t *>(x_region(x, x.rank, e));
+    ls = reinterpret_cast<const float *>(lt + ni);
+    n = x.world;
+  }
   const int m = n * L;
   uint32_t *keys = reinterpret_cast<uint32_t *>(fm_dyn);
   int32_t *ids = reinterpret_cast<int32_t *>(keys + m);
@@ -461,8 +487,9 @@ fine_merge_kernel(kiv_store st, kiv_query q, Workspace w, const float *ls, const
   for (int i = threadIdx.x; i < m; i += FM_THREADS) {
     const int j = i / L, a = i % L;
     const int64_t off = ((int64_t)j * B + b) * L + a;
-    ids[i] = lt[off];
-    keys[i] = lt[off] >= 0 ? f2key(ls[off]) : 0u;
+    const int32_t id = __ldcg(lt + off);
+    ids[i] = id;
+    keys[i] = id >= 0 ? f2key(__ldcg(ls + off)) : 0u;
   }
   if (threadIdx.x < 64) s_valid[threadIdx.x] = 0;
   __syncthreads();
@@ -512,6 +539,7 @@ fine_merge_kernel(kiv_store st, kiv_query q, Workspace w, const float *ls, const
       st.state[KIV_ST_SEL_LOCAL] = pre_sel[st.shard_rank * (L + 1) + L];
     }
   }
+  if (X) x_advance(x, X_FINE, e);
 }
 
 template <typename T, int LPR, int VPL, int RCH>
@@ -587,16 +615,24 @@ kiv_status launch_fine_topk(const kiv_store *st, const kiv_query *q, const Works
 
 kiv_status launch_fine_merge(const kiv_store *st, const kiv_query *q, const Workspace &w,
                              const float *ls, const int32_t *lt, int32_t n, int32_t *sel,
-                             int32_t *sel_local, cudaStream_t s) {
-  const int64_t m = (int64_t)n * q->top_p;
-  const size_t smem = (size_t)m * 8 + (size_t)n * (q->top_p + 1) * 8 + (size_t)m * 2 + 16;
-  if (smem > 200 * 1024 || n > 64) {
-    set_error("fine_merge: %d lists of %d entries exceed the shared-memory merge", n, q->top_p);
+                             int32_t *sel_local, cudaStream_t s, const XArgs *x) {
+  const int nl = x ? x->world : n;
+  const int64_t m = (int64_t)nl * q->top_p;
+  const size_t smem = (size_t)m * 8 + (size_t)nl * (q->top_p + 1) * 8 + (size_t)m * 2 + 16;
+  if (smem > 200 * 1024 || nl > 64) {
+    set_error("fine_merge: %d lists of %d entries exceed the shared-memory merge", nl, q->top_p);
     return KIV_ERR_CAPACITY;
   }
-  cudaFuncSetAttribute(fine_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  const cudaError_t e = launch_pdl(fine_merge_kernel, dim3((unsigned)st->batch), dim3(FM_THREADS), smem, s, 1, *st,
-                                   *q, w, ls, lt, n, sel, sel_local);
+  cudaError_t e;
+  if (x) {
+    cudaFuncSetAttribute(fine_merge_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    e = launch_pdl(fine_merge_kernel<true>, dim3((unsigned)st->batch), dim3(FM_THREADS), smem, s, 1, *st, *q, w,
+                   (const float *)nullptr, (const int32_t *)nullptr, nl, sel, sel_local, *x, ls, lt);
+  } else {
+    cudaFuncSetAttribute(fine_merge_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    e = launch_pdl(fine_merge_kernel<false>, dim3((unsigned)st->batch), dim3(FM_THREADS), smem, s, 1, *st, *q, w,
+                   ls, lt, n, sel, sel_local, XArgs{}, (const float *)nullptr, (const int32_t *)nullptr);
+  }
   if (e != cudaSuccess) return cuda_status(e, "fine_merge");
   return cuda_status(cudaGetLastError(), "fine_merge");
 }

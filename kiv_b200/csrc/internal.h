@@ -53,8 +53,10 @@ kiv_status launch_append_evict(const kiv_store *st, const void *k_new, const voi
                                int64_t n_evict_max, cudaStream_t s);
 kiv_status launch_coarse(const kiv_store *st, const kiv_query *q, const Workspace &w,
                          float *row_scores, int32_t *row_pages, cudaStream_t s);
+struct XArgs;   // peer exchange arguments (exchange.cuh)
 kiv_status launch_coarse_merge(const kiv_store *st, const kiv_query *q, const Workspace &w,
-                               const float *ls, const int32_t *lp, int32_t n, cudaStream_t s);
+                               const float *ls, const int32_t *lp, int32_t n, cudaStream_t s,
+                               const XArgs *x = nullptr);
 kiv_status launch_fine(const kiv_store *st, const kiv_query *q, const Workspace &w, int32_t *sel,
                        float *sel_scores, cudaStream_t s);
 kiv_status launch_fine_score(const kiv_store *st, const kiv_query *q, const Workspace &w, cudaStream_t s);
@@ -66,7 +68,7 @@ kiv_status launch_fine_topk(const kiv_store *st, const kiv_query *q, const Works
                             float *sel_scores, cudaStream_t s);
 kiv_status launch_fine_merge(const kiv_store *st, const kiv_query *q, const Workspace &w,
                              const float *ls, const int32_t *lt, int32_t n, int32_t *sel,
-                             int32_t *sel_local, cudaStream_t s);
+                             int32_t *sel_local, cudaStream_t s, const XArgs *x = nullptr);
 kiv_status launch_gather(const kiv_store *st, const int32_t *sel, int32_t sel_stride, int32_t P,
                          void *ok, void *ov, cudaStream_t s);
 kiv_status launch_attend(const kiv_store *st, const kiv_query *q, const kiv_mask *m,
@@ -74,7 +76,9 @@ kiv_status launch_attend(const kiv_store *st, const kiv_query *q, const kiv_mask
                          int32_t hot_slice, int32_t hot_slices, void *out, float *partial_out,
                          cudaStream_t s);
 kiv_status launch_attend_merge(const kiv_store *st, const kiv_query *q, const float *partials,
-                               int32_t n, void *out, cudaStream_t s);
+                               int32_t n, void *out, cudaStream_t s, const XArgs *x = nullptr);
+// per-rank payload bytes of the three exchanges (coarse lists, fine lists, attention partial)
+void exchange_payloads(const kiv_store *st, const kiv_query *q, int64_t *cb, int64_t *fb, int64_t *ab);
 
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 

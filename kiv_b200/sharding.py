@@ -1,27 +1,87 @@
-"""Collectives of the page-sharded cold tier (one process per GPU, NCCL over NVLink).
+"""Exchanges of the page-sharded cold tier (one process per GPU of one box).
 
 The cold tier of a layer is partitioned by page over the GPUs of one box (page
 p lives on rank p % world).  A decode layer-step then needs three small
-exchanges, all all-gathers of a few KB to tens of KB (latency-bound):
-per-row coarse candidates (score, page), per-batch-row fine candidates
-(score, token) and per-row attention partials (out, max, sum).  Each rank
-merges the gathered lists identically, so every rank ends with the exact
-global top-k and the same merged output.
+exchanges of a few KB to tens of KB (latency-bound): per-row coarse
+candidates (score, page), per-batch-row fine candidates (score, token) and
+per-row attention partials (out, max, sum).  Each rank merges the gathered
+lists identically, so every rank ends with the exact global top-k and the same
+merged output.
+
+On CUDA the exchanges go through peer memory: every rank allocates an
+exchange arena, the ranks swap CUDA IPC handles once over the process group,
+and the merge kernels store their lists straight into the peers' arenas over
+NVLink and wait on per-source counters (``kiv_*_exchange_merge`` in the C
+ABI).  ``all_gather`` / ``all_reduce_sum`` (the process group's collectives)
+remain for the API paths that return tensors and for CPU process groups.
 """
 
 from __future__ import annotations
+
+import ctypes
 
 import torch
 import torch.distributed as dist
 
 
 class ShardComm:
-    """Thin wrapper over a ``torch.distributed`` process group."""
+    """A ``torch.distributed`` process group plus the peer-memory exchange arenas."""
 
     def __init__(self, group=None) -> None:
         self.group = group
         self.rank = dist.get_rank(group)
         self.size = dist.get_world_size(group)
+        self._arenas: dict = {}
+
+    def exchange(self, nbytes: int, device: torch.device):
+        """The exchange descriptor of arenas of ``nbytes`` (every rank calls this
+        with the same size; the first call allocates and maps them collectively)."""
+        from . import _native as nat
+
+        key = (int(nbytes), device.index)
+        hit = self._arenas.get(key)
+        if hit is not None:
+            return hit[0]
+        if self.size > nat.MAX_PEERS:
+            raise nat.KIVNativeError(f"peer exchange supports up to {nat.MAX_PEERS} ranks, got {self.size}")
+        L = nat.lib()
+        own = ctypes.c_void_p()
+        handle = (ctypes.c_ubyte * nat.IPC_HANDLE_BYTES)()
+        with torch.cuda.device(device):
+            nat.check(L.kiv_peer_alloc(int(nbytes), ctypes.byref(own), handle), "peer_alloc")
+            handles = [None] * self.size
+            dist.all_gather_object(handles, bytes(handle), group=self.group)
+            arenas, opened = [], []
+            for r, hb in enumerate(handles):
+                if r == self.rank:
+                    arenas.append(own.value)
+                    continue
+                p = ctypes.c_void_p()
+                buf = (ctypes.c_ubyte * nat.IPC_HANDLE_BYTES).from_buffer_copy(hb)
+                nat.check(L.kiv_peer_open(buf, ctypes.byref(p)), "peer_open")
+                arenas.append(p.value)
+                opened.append(p.value)
+            dist.barrier(group=self.group)
+        desc = nat.ExchangeDesc(self.size, self.rank, (ctypes.c_void_p * nat.MAX_PEERS)(*arenas), int(nbytes))
+        self._arenas[key] = (desc, own.value, opened, device)
+        return desc
+
+    def close(self) -> None:
+        """Unmap the peers' arenas and free this rank's (after all exchanges are done)."""
+        from . import _native as nat
+
+        L = nat.lib() if self._arenas else None
+        for desc, own, opened, device in self._arenas.values():
+            with torch.cuda.device(device):
+                torch.cuda.synchronize(device)
+                for p in opened:
+                    L.kiv_peer_close(ctypes.c_void_p(p))
+        if self._arenas:
+            dist.barrier(group=self.group)
+        for desc, own, opened, device in self._arenas.values():
+            with torch.cuda.device(device):
+                L.kiv_peer_free(ctypes.c_void_p(own))
+        self._arenas.clear()
 
     def all_gather(self, out: torch.Tensor, inp: torch.Tensor) -> None:
         """out[n, *inp.shape] <- every rank's ``inp`` (rank order)."""

@@ -42,9 +42,11 @@ int main(void) {{
   printf("kiv_store %zu\\n", sizeof(kiv_store));
   printf("kiv_query %zu\\n", sizeof(kiv_query));
   printf("kiv_mask %zu\\n", sizeof(kiv_mask));
+  printf("kiv_exchange %zu\\n", sizeof(kiv_exchange));
   F(kiv_store, cold_capacity) F(kiv_store, hot_capacity) F(kiv_store, cold_k) F(kiv_store, state)
   F(kiv_query, stride_t) F(kiv_query, scaling) F(kiv_query, top_p)
   F(kiv_mask, stride_t) F(kiv_mask, causal)
+  F(kiv_exchange, arena) F(kiv_exchange, arena_bytes)
   return 0;
 }}''')
     exe = tmp_path / "layout"
@@ -53,10 +55,12 @@ int main(void) {{
     assert int(out["kiv_store"]) == ctypes.sizeof(nat.StoreDesc)
     assert int(out["kiv_query"]) == ctypes.sizeof(nat.QueryDesc)
     assert int(out["kiv_mask"]) == ctypes.sizeof(nat.MaskDesc)
+    assert int(out["kiv_exchange"]) == ctypes.sizeof(nat.ExchangeDesc)
     for key, val in out.items():
         if "." in key:
             struct, field = key.split(".")
-            cls = {"kiv_store": nat.StoreDesc, "kiv_query": nat.QueryDesc, "kiv_mask": nat.MaskDesc}[struct]
+            cls = {"kiv_store": nat.StoreDesc, "kiv_query": nat.QueryDesc, "kiv_mask": nat.MaskDesc,
+                   "kiv_exchange": nat.ExchangeDesc}[struct]
             assert getattr(cls, field).offset == int(val), key
 
 

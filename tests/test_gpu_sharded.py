@@ -2,7 +2,9 @@
 
 Two ranks (one process per GPU) build the same cache with the cold pages
 sharded ``p % 2`` and run one decode layer-step through the public surface
-(retrieve_indices, attend).  Rank 0 also runs the step unsharded on its GPU.
+(retrieve_indices, attend); the ranks exchange their lists and partials
+through peer memory (``KIV_SHARD_EXCHANGE=peer``, the default) or the process
+group's collectives.  Rank 0 also runs the step unsharded on its GPU.
 The global selections must be identical (both sides use the same kernels and
 the sharded merge breaks ties like the single-GPU select: score descending,
 id ascending) and the attention outputs must agree within 1e-2 relative
@@ -64,7 +66,7 @@ def _run_step(shape, dev, shard_group):
     return sel[:, :P].cpu().numpy(), out.float().cpu().numpy(), int(err)
 
 
-def _worker(rank, port, out_dir, shape):
+def _worker(rank, port, out_dir, shape, exchange):
     import datetime
     import sys
 
@@ -74,6 +76,7 @@ def _worker(rank, port, out_dir, shape):
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
+    os.environ["KIV_SHARD_EXCHANGE"] = exchange
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     t0 = time.time()
@@ -84,8 +87,9 @@ def _worker(rank, port, out_dir, shape):
     dist.init_process_group("nccl", rank=rank, world_size=WORLD, timeout=datetime.timedelta(seconds=120),
                             device_id=dev)
     failure = None
+    comm = ShardComm()
     try:
-        sel_sh, out_sh, err_sh = _run_step(shape, dev, ShardComm())
+        sel_sh, out_sh, err_sh = _run_step(shape, dev, comm)
         log("sharded step done")
         if rank == 0:
             sel_1, out_1, err_1 = ref
@@ -100,20 +104,22 @@ def _worker(rank, port, out_dir, shape):
             except AssertionError as e:
                 failure = e
         dist.barrier()
+        comm.close()
     finally:
         dist.destroy_process_group()
     if failure is not None:
         raise failure
 
 
+@pytest.mark.parametrize("exchange", ["peer", "collective"])
 @pytest.mark.parametrize("shape", sorted(SHAPES))
-def test_sharded_step_matches_single_gpu(shape):
+def test_sharded_step_matches_single_gpu(shape, exchange):
     if torch.cuda.device_count() < WORLD:
         pytest.skip(f"needs {WORLD} GPUs")
     import torch.multiprocessing as mp
 
     with tempfile.TemporaryDirectory() as d:
-        ctx = mp.start_processes(_worker, args=(_free_port(), d, shape), nprocs=WORLD, join=False,
+        ctx = mp.start_processes(_worker, args=(_free_port(), d, shape, exchange), nprocs=WORLD, join=False,
                                  start_method="spawn")
         deadline = time.time() + 300
         while not ctx.join(timeout=5):
