@@ -286,7 +286,8 @@ KIV_API kiv_status kiv_coarse_exchange_merge(const kiv_store *st, const kiv_quer
                                              const float *row_scores, const int32_t *row_pages,
                                              const kiv_exchange *x, void *stream);
 /* kiv_fine_merge with the lists exchanged through the arenas: scores /
- * tokens are this rank's lists from kiv_fine_select (or kiv_fine_topk). */
+ * tokens are this rank's lists from kiv_fine_select (or kiv_fine_topk).
+ * sel may be NULL when only this shard's selection (sel_local) is needed. */
 KIV_API kiv_status kiv_fine_exchange_merge(const kiv_store *st, const kiv_query *q, void *ws, size_t ws_bytes,
                                            const float *scores, const int32_t *tokens, const kiv_exchange *x,
                                            int32_t *sel, int32_t *sel_local, void *stream);

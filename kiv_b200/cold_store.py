@@ -344,7 +344,7 @@ class ColdKVStore:
         return p if p <= guaranteed else None
 
     def _select(self, query: torch.Tensor, scaling: float, kiv_config: KIVConfig, step: int,
-                softcap: float | None = None):
+                softcap: float | None = None, global_sel: bool = True):
         """Coarse (or reuse) + fine.  Returns (sel [B, top_p] int32, ws key, ws, qdesc)."""
         B, Hq, Q, _ = query.shape
         top_pages, top_p = kiv_config.top_pages, kiv_config.top_p
@@ -387,7 +387,7 @@ class ColdKVStore:
                 prof.record("fine_topk_end")
             sel_local = sel
         else:
-            sel_local = self._sharded_fine(desc, qd, ws, B, top_p, sel, s)
+            sel_local = self._sharded_fine(desc, qd, ws, B, top_p, sel if global_sel else None, s)
         if not reuse:
             # the fine scorer materializes the page union the coarse pass marked
             if self.num_pages > 0:
@@ -468,7 +468,8 @@ class ColdKVStore:
         with torch.cuda.device(self.device):
             s = nat.stream_ptr(self.device)
             if self._cold_len > 0:
-                sel, sel_local, ws, qd = self._select(query, scaling, kiv_config, step, softcap)
+                sel, sel_local, ws, qd = self._select(query, scaling, kiv_config, step, softcap,
+                                                      global_sel=self._telemetry.enabled)
                 if self._telemetry.enabled:
                     self._record_fine(sel, self._expected_P(kiv_config.top_pages, kiv_config.top_p),
                                       kiv_config.top_p)
@@ -544,7 +545,8 @@ class ColdKVStore:
         nat.check(L.kiv_coarse_merge(ctypes.byref(desc), ctypes.byref(qd), ws.data_ptr(), ws.numel(),
                                      all_s.data_ptr(), all_p.data_ptr(), n, s), "coarse_merge")
 
-    def _sharded_fine(self, desc, qd, ws, B: int, top_p: int, sel: torch.Tensor, s: int) -> torch.Tensor:
+    def _sharded_fine(self, desc, qd, ws, B: int, top_p: int, sel: torch.Tensor | None, s: int) -> torch.Tensor:
+        """Local fine pass + exchange + merge; fills ``sel`` (the global list) when given."""
         L = nat.lib()
         lt = self._buffer("fl_t", (B, top_p), torch.int32)
         ls = self._buffer("fl_s", (B, top_p), torch.float32)
@@ -563,7 +565,8 @@ class ColdKVStore:
         x = self._exchange(desc, qd)
         if x is not None:
             nat.check(L.kiv_fine_exchange_merge(ctypes.byref(desc), ctypes.byref(qd), ws.data_ptr(), ws.numel(),
-                                                ls.data_ptr(), lt.data_ptr(), ctypes.byref(x), sel.data_ptr(),
+                                                ls.data_ptr(), lt.data_ptr(), ctypes.byref(x),
+                                                None if sel is None else sel.data_ptr(),
                                                 sel_local.data_ptr(), s), "fine_exchange_merge")
             return sel_local
         n = self._shard_count
@@ -571,6 +574,8 @@ class ColdKVStore:
         all_s = self._buffer("fl_s_all", (n, B, top_p), torch.float32)
         self._comm.all_gather(all_t, lt)
         self._comm.all_gather(all_s, ls)
+        if sel is None:
+            sel = self._buffer("sel_global_scratch", (B, top_p), torch.int32)
         nat.check(L.kiv_fine_merge(ctypes.byref(desc), ctypes.byref(qd), ws.data_ptr(), ws.numel(),
                                    all_s.data_ptr(), all_t.data_ptr(), n, sel.data_ptr(),
                                    sel_local.data_ptr(), s), "fine_merge")

@@ -408,7 +408,7 @@ kiv_status kiv_fine_exchange_merge(const kiv_store *st, const kiv_query *q, void
   KIV_TRY(check_query(st, q));
   Workspace w;
   KIV_TRY(check_ws(st, q, ws, ws_bytes, w));
-  if (!scores || !tokens || !sel || !sel_local) { set_error("bad fine merge arguments"); return KIV_ERR_ARG; }
+  if (!scores || !tokens || !sel_local) { set_error("bad fine merge arguments"); return KIV_ERR_ARG; }
   kiv::XArgs a;
   KIV_TRY(check_exchange(st, q, x, kiv::X_FINE, st->batch, a));
   return launch_fine_merge(st, q, w, scores, tokens, x->world, sel, sel_local, (cudaStream_t)stream, &a);

@@ -720,6 +720,8 @@ template <typename T, bool X>
 __global__ void __launch_bounds__(CB_THREADS)
 combine_kernel(const float *part, int64_t row_stride, int64_t pstride, int n, int D, int Hq, int Q,
                T *final_out, float *merged, XArgs x, const float *mine, int64_t rows, int64_t *state) {
+  // the epoch was advanced by this type's previous exchange, kernels ago
+  const unsigned long long e = X ? x_epoch(x, X_ATTN) : 0ull;
   griddep_wait();
   constexpr int C4 = CB_COLS / 4;              // float4 columns per chunk
   constexpr int NG = CB_THREADS / C4;          // partial groups
@@ -729,28 +731,26 @@ combine_kernel(const float *part, int64_t row_stride, int64_t pstride, int n, in
   const int64_t row = blockIdx.x / nch;        // (b*Hq + h)*Q + t
   const int chunk = blockIdx.x % nch;
   const int Dp = partial_stride(D);
-  unsigned long long e = 0;
+  bool ok = true;
+  uint32_t flag = 0;
+  const unsigned long long *xin = nullptr;
   if (X) {
     // this rank's partial of this (row, column chunk) -> slot [rank] of every
-    // arena; then wait for every rank's partials in this rank's arena
-    e = x_epoch(x, X_ATTN);
+    // arena, one flagged word per value
+    flag = x_flag(e);
     const int c0 = chunk * CB_COLS, c1 = min(D, c0 + CB_COLS);
     const float *src = mine + row * Dp;
     for (int d = 0; d < x.world; ++d) {
-      float *dst = reinterpret_cast<float *>(x_region(x, d, e)) + ((int64_t)x.rank * rows + row) * Dp;
-      for (int c = c0 + threadIdx.x; c < c1; c += CB_THREADS) dst[c] = src[c];
-      if (chunk == 0 && threadIdx.x < 2) dst[D + threadIdx.x] = src[D + threadIdx.x];
+      unsigned long long *dst = x_region(x, d, e) + ((int64_t)x.rank * rows + row) * Dp;
+      for (int c = c0 + threadIdx.x; c < c1; c += CB_THREADS) ll_store(dst + c, __float_as_uint(src[c]), flag);
+      if (threadIdx.x < 2) ll_store(dst + D + threadIdx.x, __float_as_uint(src[D + threadIdx.x]), flag);
     }
-    x_signal(x, X_ATTN);
-    if (!x_wait(x, X_ATTN, (e + 1) * gridDim.x) && threadIdx.x == 0)
-      atomicOr(reinterpret_cast<unsigned long long *>(state + KIV_ST_ERROR),
-               (unsigned long long)KIV_ERRBIT_WAIT_TIMEOUT);
-    part = reinterpret_cast<const float *>(x_region(x, x.rank, e));
+    xin = x_region(x, x.rank, e);
     row_stride = Dp;
     pstride = rows;
     n = x.world;
   }
-  const float *p = part + row * row_stride;
+  const float *p = X ? nullptr : part + row * row_stride;
   const int c4 = threadIdx.x % C4, grp = threadIdx.x / C4;
   const int col = chunk * CB_COLS + c4 * 4;
   const int colc = col < D ? col : 0;          // in-bounds column for the loads
@@ -758,9 +758,25 @@ combine_kernel(const float *part, int64_t row_stride, int64_t pstride, int n, in
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 4
   for (int i = grp; i < n; i += NG) {
-    const float *pi = p + (int64_t)i * pstride * Dp;
-    const float4 v = __ldcg(reinterpret_cast<const float4 *>(pi + colc));
-    const float mi = __ldcg(pi + D), li = __ldcg(pi + D + 1);
+    float4 v;
+    float mi, li;
+    if (X) {
+      const unsigned long long *wi = xin + row * row_stride + (int64_t)i * pstride * Dp;
+      const unsigned long long w0 = ld_relaxed_sys(wi + colc), w1 = ld_relaxed_sys(wi + colc + 1);
+      const unsigned long long w2 = ld_relaxed_sys(wi + colc + 2), w3 = ld_relaxed_sys(wi + colc + 3);
+      const unsigned long long wm = ld_relaxed_sys(wi + D), wl = ld_relaxed_sys(wi + D + 1);
+      v.x = __uint_as_float(ll_check(wi + colc, w0, flag, ok));
+      v.y = __uint_as_float(ll_check(wi + colc + 1, w1, flag, ok));
+      v.z = __uint_as_float(ll_check(wi + colc + 2, w2, flag, ok));
+      v.w = __uint_as_float(ll_check(wi + colc + 3, w3, flag, ok));
+      mi = __uint_as_float(ll_check(wi + D, wm, flag, ok));
+      li = __uint_as_float(ll_check(wi + D + 1, wl, flag, ok));
+    } else {
+      const float *pi = p + (int64_t)i * pstride * Dp;
+      v = __ldcg(reinterpret_cast<const float4 *>(pi + colc));
+      mi = __ldcg(pi + D);
+      li = __ldcg(pi + D + 1);
+    }
     if (mi == -INFINITY) continue;             // empty partial
     const float mn = fmaxf(m, mi);
     const float a = __expf(m - mn), bi = __expf(mi - mn);   // m == -inf: a = 0
@@ -774,6 +790,9 @@ combine_kernel(const float *part, int64_t row_stride, int64_t pstride, int n, in
   s_acc[grp][c4] = acc;
   s_m[grp][c4] = m;
   s_l[grp][c4] = l;
+  if (X && !ok)
+    atomicOr(reinterpret_cast<unsigned long long *>(state + KIV_ST_ERROR),
+             (unsigned long long)KIV_ERRBIT_WAIT_TIMEOUT);
   __syncthreads();
   if (X) x_advance(x, X_ATTN, e);   // every CTA has read its inputs from the arena
   if (grp != 0) return;
@@ -978,9 +997,10 @@ kiv_status launch_attend_merge(const kiv_store *st, const kiv_query *q, const fl
 // per-rank payload bytes of the three exchanges
 void exchange_payloads(const kiv_store *st, const kiv_query *q, int64_t *cb, int64_t *fb, int64_t *ab) {
   const int64_t R = (int64_t)st->batch * q->num_query_heads * q->query_len;
-  *cb = R * q->top_pages * 8;
-  *fb = (int64_t)st->batch * q->top_p * 8;
-  *ab = R * partial_stride(st->head_dim) * 4;
+  // one flagged 64-bit word per 32-bit value
+  *cb = R * q->top_pages * 16;
+  *fb = (int64_t)st->batch * q->top_p * 16;
+  *ab = R * partial_stride(st->head_dim) * 8;
 }
 
 kiv_status launch_gather(const kiv_store *st, const int32_t *sel, int32_t sel_stride, int32_t P,

@@ -23,6 +23,7 @@ constexpr int TK_THREADS = 512;      // per-row top-k
 constexpr int TK_BND = 1024;         // boundary-bin capacity of the candidate select
 constexpr int TK_SCAP = 16384;       // scores of a row staged in shared memory
 constexpr int CM_THREADS = 256;      // merge of gathered per-row lists
+constexpr int CM_RANK_MAX = 1024;   // merge by direct ranking up to this many entries
 constexpr int UN_THREADS = 1024;     // page union from the page marks
 
 // local finalized pages of this shard given the global finalized count
@@ -276,6 +277,8 @@ template <bool X>
 __global__ void __launch_bounds__(CM_THREADS)
 coarse_merge_kernel(kiv_store st, kiv_query q, Workspace w, const float *ls, const int32_t *lp, int32_t n,
                     XArgs x, const float *mine_s, const int32_t *mine_p) {
+  // the epoch was advanced by this type's previous exchange, kernels ago
+  const unsigned long long e = X ? x_epoch(x, X_COARSE) : 0ull;
   griddep_wait();
   extern __shared__ uint4 dyn_smem[];
   __shared__ SelectSmem<CM_THREADS> sm;
@@ -284,42 +287,84 @@ coarse_merge_kernel(kiv_store st, kiv_query q, Workspace w, const float *ls, con
   const int row = blockIdx.x;
   const int K = q.top_pages;
   const int64_t R = w.R;
-  unsigned long long e = 0;
+  bool ok = true;
+  uint32_t flag = 0;
   if (X) {
-    // this rank's list of this row -> slot [rank] of every arena; then wait
-    // for every rank's lists in this rank's arena
-    e = x_epoch(x, X_COARSE);
-    const int64_t nf = (int64_t)x.world * R * K;   // floats of a parity, then as many ints
+    // this rank's list of this row -> slot [rank] of every arena, as
+    // (score, page) word pairs carrying the epoch's flag
+    flag = x_flag(e);
     for (int d = 0; d < x.world; ++d) {
-      float *fs = reinterpret_cast<float *>(x_region(x, d, e));
-      int32_t *ip = reinterpret_cast<int32_t *>(fs + nf);
+      unsigned long long *reg = x_region(x, d, e) + (((int64_t)x.rank * R + row) * K) * 2;
       for (int j = threadIdx.x; j < K; j += CM_THREADS) {
-        const int64_t off = ((int64_t)x.rank * R + row) * K + j;
-        fs[off] = mine_s[(int64_t)row * K + j];
-        ip[off] = mine_p[(int64_t)row * K + j];
+        ll_store(reg + 2 * j, __float_as_uint(mine_s[(int64_t)row * K + j]), flag);
+        ll_store(reg + 2 * j + 1, (uint32_t)mine_p[(int64_t)row * K + j], flag);
       }
     }
-    x_signal(x, X_COARSE);
-    if (!x_wait(x, X_COARSE, (e + 1) * gridDim.x) && threadIdx.x == 0)
-      atomicOr(reinterpret_cast<unsigned long long *>(st.state + KIV_ST_ERROR),
-               (unsigned long long)KIV_ERRBIT_WAIT_TIMEOUT);
-    ls = reinterpret_cast<const float *>(x_region(x, x.rank, e));
-    lp = reinterpret_cast<const int32_t *>(ls + nf);
     n = x.world;
   }
   const int m = n * K;
   uint32_t *keys = reinterpret_cast<uint32_t *>(dyn_smem);
   int32_t *ids = reinterpret_cast<int32_t *>(keys + m);
-  for (int i = threadIdx.x; i < m; i += CM_THREADS) {
-    const int src = i / K, j = i % K;
-    const int64_t off = ((int64_t)src * R + row) * K + j;
-    const int32_t pg = __ldcg(lp + off);
-    ids[i] = pg;
-    keys[i] = pg >= 0 ? f2key(__ldcg(ls + off)) : 0u;
+  const unsigned long long *mine = X ? x_region(x, x.rank, e) : nullptr;
+  constexpr int CB = 4;   // entries per thread per batch (independent loads)
+  for (int i0 = 0; i0 < m; i0 += CM_THREADS * CB) {
+    unsigned long long wv[2 * CB];
+    int64_t offs[CB];
+#pragma unroll
+    for (int k = 0; k < CB; ++k) {
+      const int i = i0 + k * CM_THREADS + threadIdx.x;
+      const int src = i / K, j = i % K;
+      offs[k] = ((int64_t)src * R + row) * K + j;
+      if (X && i < m) {
+        wv[2 * k] = ld_relaxed_sys(mine + 2 * offs[k]);
+        wv[2 * k + 1] = ld_relaxed_sys(mine + 2 * offs[k] + 1);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < CB; ++k) {
+      const int i = i0 + k * CM_THREADS + threadIdx.x;
+      if (i >= m) continue;
+      int32_t pg;
+      float sc;
+      if (X) {
+        sc = __uint_as_float(ll_check(mine + 2 * offs[k], wv[2 * k], flag, ok));
+        pg = (int32_t)ll_check(mine + 2 * offs[k] + 1, wv[2 * k + 1], flag, ok);
+      } else {
+        sc = __ldcg(ls + offs[k]);
+        pg = __ldcg(lp + offs[k]);
+      }
+      ids[i] = pg;
+      keys[i] = pg >= 0 ? f2key(sc) : 0u;
+    }
   }
+  if (X && !ok)
+    atomicOr(reinterpret_cast<unsigned long long *>(st.state + KIV_ST_ERROR),
+             (unsigned long long)KIV_ERRBIT_WAIT_TIMEOUT);
   __syncthreads();
   const uint32_t k = (uint32_t)(K < np_global ? (int64_t)K : np_global);
-  if (k > 0) {
+  auto mark = [&](int32_t id) {
+    if ((id % st.shard_count) == st.shard_rank) {
+      const int32_t lpg = id / st.shard_count;
+      atomicOr(&w.pbits[lpg >> 5], 1u << (lpg & 31));
+    }
+  };
+  if (k > 0 && m <= CM_RANK_MAX) {
+    // few entries: each one's rank in the total order (score desc, page asc)
+    // by comparison with all of them, in one pass
+    for (int i = threadIdx.x; i < m; i += CM_THREADS) {
+      const int32_t pi = ids[i];
+      if (pi < 0) continue;
+      const uint32_t ki = keys[i];
+      uint32_t rank = 0;
+#pragma unroll 4
+      for (int j = 0; j < m; ++j) {
+        const uint32_t kj = keys[j];
+        const int32_t pj = ids[j];
+        rank += (pj >= 0 && (kj > ki || (kj == ki && pj < pi))) ? 1u : 0u;
+      }
+      if (rank < k) mark(pi);
+    }
+  } else if (k > 0) {
     uint32_t T = 0, need = 0;
     radix_threshold<CM_THREADS, 1>(keys, m, k, sm, T, need);
     // entries == T: take the `need` lowest page ids
@@ -331,10 +376,7 @@ coarse_merge_kernel(kiv_store st, kiv_query q, Workspace w, const float *ls, con
           rank += (keys[j] == T && ids[j] >= 0 && ids[j] < ids[i]) ? 1u : 0u;
         take = rank < need;
       }
-      if (take && ids[i] >= 0 && (ids[i] % st.shard_count) == st.shard_rank) {
-        const int32_t lpg = ids[i] / st.shard_count;
-        atomicOr(&w.pbits[lpg >> 5], 1u << (lpg & 31));
-      }
+      if (take && ids[i] >= 0) mark(ids[i]);
     }
   }
   if (row == 0 && threadIdx.x == 0) st.state[KIV_ST_UNION_PENDING] = 1;

@@ -3,18 +3,18 @@
 // Every rank owns an arena that all ranks map (CUDA IPC over NVLink).  Arena
 // layout (identical on every rank):
 //   header  [3 types][16] u64: word 0 the type's epoch (exchanges done),
-//           word 1 a CTA counter (last CTA of a launch), words 8 + src the
-//           number of CTAs of rank src that have delivered into this arena;
+//           word 1 a CTA counter (last CTA of a launch);
 //   regions one per type, two parities each (epoch & 1), holding the lists
-//           of every rank at slot [src].
+//           of every rank at slot [src], as 64-bit words (flag << 32 | data).
 // A merge launch of epoch e: each CTA stores its part of this rank's lists
-// into slot [rank] of parity e & 1 of every arena, fences at system scope and
-// adds 1 to counter [rank] of every arena (release); then it waits until
-// every counter of its own arena reaches (e + 1) x CTAs (acquire, bounded),
-// merges from its own arena, and the launch's last CTA sets the epoch to
-// e + 1.  Two parities suffice: a rank can only start epoch e + 2 after it
-// has received every rank's epoch e + 1 lists, which each rank sends only
-// after finishing its merge of epoch e.
+// into slot [rank] of parity e & 1 of every arena, each 32-bit value in one
+// 64-bit store together with the flag e + 1 (a single-copy atomic access, so
+// no fence is needed: a reader that sees the flag sees the value); it then
+// reads every rank's lists from its own arena, waiting (bounded) on each word
+// until its flag is e + 1, merges, and the launch's last CTA sets the epoch
+// to e + 1.  Two parities suffice: a rank can only start epoch e + 2 after it
+// has read every rank's epoch e + 1 lists, which each rank sends only after
+// finishing its merge of epoch e.
 #pragma once
 
 #include "../../include/kiv_b200.h"
@@ -53,50 +53,41 @@ __host__ __device__ inline XLayout x_layout(int64_t cb, int64_t fb, int64_t ab, 
 __device__ __forceinline__ unsigned long long *x_word(char *arena, int t, int i) {
   return reinterpret_cast<unsigned long long *>(arena) + t * 16 + i;
 }
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
+__device__ __forceinline__ unsigned long long ld_relaxed_sys(const unsigned long long *p) {
   unsigned long long v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
-}
-__device__ __forceinline__ void red_release_sys_add(unsigned long long *p, unsigned long long v) {
-  asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 __device__ __forceinline__ unsigned long long x_epoch(const XArgs &x, int t) {
   return *reinterpret_cast<volatile unsigned long long *>(x_word(x.arena[x.rank], t, 0));
 }
-// region (parity of epoch e) of rank d's arena
-__device__ __forceinline__ char *x_region(const XArgs &x, int d, unsigned long long e) {
-  return x.arena[d] + x.off + (int64_t)(e & 1ull) * x.par_bytes;
+// region (parity of epoch e) of rank d's arena, as 64-bit words
+__device__ __forceinline__ unsigned long long *x_region(const XArgs &x, int d, unsigned long long e) {
+  return reinterpret_cast<unsigned long long *>(x.arena[d] + x.off + (int64_t)(e & 1ull) * x.par_bytes);
 }
-// after this CTA's stores into the arenas: count the CTA in every arena
-__device__ __forceinline__ void x_signal(const XArgs &x, int t) {
-  __threadfence_system();
-  __syncthreads();
-  if (threadIdx.x == 0)
-    for (int d = 0; d < x.world; ++d) red_release_sys_add(x_word(x.arena[d], t, 8 + x.rank), 1ull);
+__device__ __forceinline__ uint32_t x_flag(unsigned long long e) { return (uint32_t)(e + 1ull); }
+// one value with its flag, in one single-copy atomic 64-bit store
+__device__ __forceinline__ void ll_store(unsigned long long *p, uint32_t data, uint32_t flag) {
+  const unsigned long long v = ((unsigned long long)flag << 32) | data;
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
-// wait until every rank has counted `target` CTAs in this rank's arena;
-// false after a bounded wait without it
-__device__ __forceinline__ bool x_wait(const XArgs &x, int t, unsigned long long target) {
-  __shared__ int s_ok;
-  if (threadIdx.x == 0) s_ok = 1;
-  __syncthreads();
-  if ((int)threadIdx.x < x.world) {
-    const unsigned long long *f = x_word(x.arena[x.rank], t, 8 + threadIdx.x);
-    if (ld_acquire_sys(f) < target) {
-      const long long t0 = clock64();
-      while (ld_acquire_sys(f) < target) {
-        if (clock64() - t0 > (1ll << 31)) {
-          s_ok = 0;
-          break;
-        }
-        __nanosleep(32);
+// v was loaded from p: if its flag is not `flag` yet, reload until it is (a
+// bounded wait, after which ok turns false and later checks stop waiting);
+// returns the value.  Callers load a batch of words first (independent loads,
+// one round trip) and check them afterwards.
+__device__ __forceinline__ uint32_t ll_check(const unsigned long long *p, unsigned long long v, uint32_t flag,
+                                             bool &ok) {
+  if ((uint32_t)(v >> 32) != flag && ok) {
+    const long long t0 = clock64();
+    do {
+      v = ld_relaxed_sys(p);
+      if (clock64() - t0 > (1ll << 31)) {
+        ok = false;
+        break;
       }
-    }
+    } while ((uint32_t)(v >> 32) != flag);
   }
-  __syncthreads();
-  __threadfence();
-  return s_ok != 0;
+  return (uint32_t)v;
 }
 // the launch's last CTA moves the epoch of type t past e
 __device__ __forceinline__ void x_advance(const XArgs &x, int t, unsigned long long e) {

@@ -418,27 +418,40 @@ __device__ __forceinline__ int lower_bound_ids(const int32_t *ids, int n, int32_
   return lo;
 }
 
-// per-list exclusive prefix of flags: pre[j*(L+1) + a] = #flags in list j before a
-__device__ void list_prefix(const uint8_t *flag, int n, int L, int32_t *pre) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  for (int j = warp; j < n; j += nw) {
-    const int per = (L + 31) / 32;
-    const int a0 = min(L, lane * per), a1 = min(L, a0 + per);
-    int c = 0;
-    for (int a = a0; a < a1; ++a) c += flag[j * L + a];
-    int incl = c;
+// Per-list exclusive prefix of flags over the n concatenated lists of L
+// entries, with one block-wide scan: gp[i] = flags in [0, i) overall, then
+// pre[j*(L+1) + a] = flags of list j before a (a = L: the list's total).
+// Ends with a barrier.
+__device__ void list_prefix_block(const uint8_t *flag, int m, int n, int L, int32_t *gp, int32_t *pre,
+                                  typename cub::BlockScan<int, FM_THREADS>::TempStorage &tmp) {
+  constexpr int IPT = 4;
+  int base = 0;
+#pragma unroll 1
+  for (int t0 = 0; t0 < m; t0 += FM_THREADS * IPT) {
+    const int i0 = t0 + threadIdx.x * IPT;
+    int f[IPT], c = 0;
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(KIV_FULL_MASK, incl, o);
-      if (lane >= o) incl += y;
+    for (int k = 0; k < IPT; ++k) {
+      f[k] = (i0 + k < m) ? flag[i0 + k] : 0;
+      c += f[k];
     }
-    int run = incl - c;
-    for (int a = a0; a < a1; ++a) {
-      pre[j * (L + 1) + a] = run;
-      run += flag[j * L + a];
+    int before, total;
+    cub::BlockScan<int, FM_THREADS>(tmp).ExclusiveSum(c, before, total);
+    int run = base + before;
+#pragma unroll
+    for (int k = 0; k < IPT; ++k) {
+      if (i0 + k < m) gp[i0 + k] = run;
+      run += f[k];
     }
-    if (lane == 31) pre[j * (L + 1) + L] = incl;
+    base += total;
+    __syncthreads();
   }
+  for (int e = threadIdx.x; e < n * (L + 1); e += FM_THREADS) {
+    const int j = e / (L + 1), a = e % (L + 1);
+    const int v = a < L ? gp[j * L + a] : ((j + 1) * L < m ? gp[(j + 1) * L] : base);
+    pre[e] = v - gp[j * L];
+  }
+  __syncthreads();
 }
 
 // Merge n gathered lists [n][B][top_p] (ascending ids, tail -1) into the
@@ -449,33 +462,28 @@ __global__ void __launch_bounds__(FM_THREADS)
 fine_merge_kernel(kiv_store st, kiv_query q, Workspace w, const float *ls, const int32_t *lt,
                   int32_t n, int32_t *sel, int32_t *sel_local, XArgs x, const float *mine_s,
                   const int32_t *mine_t) {
+  // the epoch was advanced by this type's previous exchange, kernels ago
+  const unsigned long long e = X ? x_epoch(x, X_FINE) : 0ull;
   griddep_wait();
   extern __shared__ uint4 fm_dyn[];
   __shared__ SelectSmem<FM_THREADS> sm;
+  __shared__ typename cub::BlockScan<int, FM_THREADS>::TempStorage fm_scan;
   __shared__ int s_valid[64];
   const int b = blockIdx.x;
   const int L = q.top_p, B = st.batch;
-  unsigned long long e = 0;
+  bool ok = true;
+  uint32_t flag = 0;
   if (X) {
-    // this rank's list of batch row b -> slot [rank] of every arena (tokens,
-    // then scores); then wait for every rank's lists in this rank's arena
-    e = x_epoch(x, X_FINE);
-    const int64_t ni = (int64_t)x.world * B * L;
+    // this rank's list of batch row b -> slot [rank] of every arena, as
+    // (token, score) word pairs carrying the epoch's flag
+    flag = x_flag(e);
     for (int d = 0; d < x.world; ++d) {
-      int32_t *it = reinterpret_cast<int32_t *>(x_region(x, d, e));
-      float *fs = reinterpret_cast<float *>(it + ni);
+      unsigned long long *reg = x_region(x, d, e) + (((int64_t)x.rank * B + b) * L) * 2;
       for (int a = threadIdx.x; a < L; a += FM_THREADS) {
-        const int64_t off = ((int64_t)x.rank * B + b) * L + a;
-        it[off] = mine_t[(int64_t)b * L + a];
-        fs[off] = mine_s[(int64_t)b * L + a];
+        ll_store(reg + 2 * a, (uint32_t)mine_t[(int64_t)b * L + a], flag);
+        ll_store(reg + 2 * a + 1, __float_as_uint(mine_s[(int64_t)b * L + a]), flag);
       }
     }
-    x_signal(x, X_FINE);
-    if (!x_wait(x, X_FINE, (e + 1) * gridDim.x) && threadIdx.x == 0)
-      atomicOr(reinterpret_cast<unsigned long long *>(st.state + KIV_ST_ERROR),
-               (unsigned long long)KIV_ERRBIT_WAIT_TIMEOUT);
-    lt = reinterpret_cast<const int32_t *>(x_region(x, x.rank, e));
-    ls = reinterpret_cast<const float *>(lt + ni);
     n = x.world;
   }
   const int m = n * L;
@@ -483,18 +491,54 @@ fine_merge_kernel(kiv_store st, kiv_query q, Workspace w, const float *ls, const
   int32_t *ids = reinterpret_cast<int32_t *>(keys + m);
   int32_t *pre_eq = ids + m;
   int32_t *pre_sel = pre_eq + n * (L + 1);
-  uint8_t *fl = reinterpret_cast<uint8_t *>(pre_sel + n * (L + 1));
-  for (int i = threadIdx.x; i < m; i += FM_THREADS) {
-    const int j = i / L, a = i % L;
-    const int64_t off = ((int64_t)j * B + b) * L + a;
-    const int32_t id = __ldcg(lt + off);
-    ids[i] = id;
-    keys[i] = id >= 0 ? f2key(__ldcg(ls + off)) : 0u;
+  int32_t *gp = pre_sel + n * (L + 1);
+  uint8_t *fl = reinterpret_cast<uint8_t *>(gp + m);
+  const unsigned long long *mine = X ? x_region(x, x.rank, e) : nullptr;
+  constexpr int CB = 4;   // entries per thread per batch (independent loads)
+  for (int i0 = 0; i0 < m; i0 += FM_THREADS * CB) {
+    unsigned long long wv[2 * CB];
+    int64_t offs[CB];
+#pragma unroll
+    for (int k = 0; k < CB; ++k) {
+      const int i = i0 + k * FM_THREADS + threadIdx.x;
+      const int j = i / L, a = i % L;
+      offs[k] = ((int64_t)j * B + b) * L + a;
+      if (X && i < m) {
+        wv[2 * k] = ld_relaxed_sys(mine + 2 * offs[k]);
+        wv[2 * k + 1] = ld_relaxed_sys(mine + 2 * offs[k] + 1);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < CB; ++k) {
+      const int i = i0 + k * FM_THREADS + threadIdx.x;
+      if (i >= m) continue;
+      int32_t id;
+      float sc;
+      if (X) {
+        id = (int32_t)ll_check(mine + 2 * offs[k], wv[2 * k], flag, ok);
+        sc = __uint_as_float(ll_check(mine + 2 * offs[k] + 1, wv[2 * k + 1], flag, ok));
+      } else {
+        id = __ldcg(lt + offs[k]);
+        sc = __ldcg(ls + offs[k]);
+      }
+      ids[i] = id;
+      keys[i] = id >= 0 ? f2key(sc) : 0u;
+    }
   }
+  if (X && !ok)
+    atomicOr(reinterpret_cast<unsigned long long *>(st.state + KIV_ST_ERROR),
+             (unsigned long long)KIV_ERRBIT_WAIT_TIMEOUT);
   if (threadIdx.x < 64) s_valid[threadIdx.x] = 0;
   __syncthreads();
-  for (int i = threadIdx.x; i < m; i += FM_THREADS)
-    if (ids[i] >= 0) atomicAdd(&s_valid[i / L], 1);
+  // valid entries per list, one shared atomic per warp and list
+  for (int i0 = threadIdx.x & ~31; i0 < m; i0 += FM_THREADS) {
+    const int i = i0 + (threadIdx.x & 31);
+    const bool v = i < m && ids[i] >= 0;
+    const int j = (i < m ? i : m - 1) / L;
+    const unsigned grp = __match_any_sync(KIV_FULL_MASK, j);
+    const int c = __popc(__ballot_sync(KIV_FULL_MASK, v) & grp);
+    if ((int)(threadIdx.x & 31) == __ffs(grp) - 1 && c) atomicAdd(&s_valid[j], c);
+  }
   __syncthreads();
   int valid = 0;
   for (int j = 0; j < n; ++j) valid += s_valid[j];
@@ -506,8 +550,7 @@ fine_merge_kernel(kiv_store st, kiv_query q, Workspace w, const float *ls, const
   for (int i = threadIdx.x; i < m; i += FM_THREADS)
     fl[i] = (ids[i] >= 0 && !all && keys[i] == T) ? 1 : 0;
   __syncthreads();
-  list_prefix(fl, n, L, pre_eq);
-  __syncthreads();
+  list_prefix_block(fl, m, n, L, gp, pre_eq, fm_scan);
   uint8_t *take = fl + m;
   for (int i = threadIdx.x; i < m; i += FM_THREADS) {
     const int j = i / L, a = i % L;
@@ -521,15 +564,17 @@ fine_merge_kernel(kiv_store st, kiv_query q, Workspace w, const float *ls, const
     take[i] = s ? 1 : 0;
   }
   __syncthreads();
-  list_prefix(take, n, L, pre_sel);
-  __syncthreads();
+  list_prefix_block(take, m, n, L, gp, pre_sel, fm_scan);
   for (int i = threadIdx.x; i < m; i += FM_THREADS) {
     if (!take[i]) continue;
     const int j = i / L, a = i % L;
-    int pos = pre_sel[j * (L + 1) + a];
-    for (int o = 0; o < n; ++o)
-      if (o != j) pos += pre_sel[o * (L + 1) + lower_bound_ids(ids + o * L, s_valid[o], ids[i])];
-    sel[(int64_t)b * L + pos] = ids[i];
+    if (sel) {
+      // global position: selected entries of every list with a smaller id
+      int pos = pre_sel[j * (L + 1) + a];
+      for (int o = 0; o < n; ++o)
+        if (o != j) pos += pre_sel[o * (L + 1) + lower_bound_ids(ids + o * L, s_valid[o], ids[i])];
+      sel[(int64_t)b * L + pos] = ids[i];
+    }
     if (j == st.shard_rank) sel_local[(int64_t)b * L + pre_sel[j * (L + 1) + a]] = ids[i];
   }
   if (threadIdx.x == 0) {
@@ -618,7 +663,7 @@ kiv_status launch_fine_merge(const kiv_store *st, const kiv_query *q, const Work
                              int32_t *sel_local, cudaStream_t s, const XArgs *x) {
   const int nl = x ? x->world : n;
   const int64_t m = (int64_t)nl * q->top_p;
-  const size_t smem = (size_t)m * 8 + (size_t)nl * (q->top_p + 1) * 8 + (size_t)m * 2 + 16;
+  const size_t smem = (size_t)m * 12 + (size_t)nl * (q->top_p + 1) * 8 + (size_t)m * 2 + 16;
   if (smem > 200 * 1024 || nl > 64) {
     set_error("fine_merge: %d lists of %d entries exceed the shared-memory merge", nl, q->top_p);
     return KIV_ERR_CAPACITY;
