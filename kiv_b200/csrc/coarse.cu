@@ -165,11 +165,12 @@ coarse_topk_kernel(kiv_store st, kiv_query q, Workspace w, float *row_scores, in
     mbar_fence_init();
     s_fail = 0;
   }
-  __syncthreads();
-  griddep_wait();
+  // the cold length was published by the eviction, two kernels back
   const int S = st.page_size;
   const int64_t np_global = st_ld(st.state, KIV_ST_COLD_LEN) / S;
   const int64_t np = local_pages(np_global, st.shard_rank, st.shard_count);
+  __syncthreads();
+  griddep_wait();
   const int row = blockIdx.x;
   const int K = q.top_pages;
   const int rank = st.shard_rank, nsh = st.shard_count;

@@ -273,32 +273,43 @@ fine_select_kernel(kiv_store st, kiv_query q, Workspace w, int32_t *sel, float *
     s_fail = 0;
   }
   __syncthreads();
+  // the cold length was published by the eviction, kernels back
+  const int64_t cold = st_ld(st.state, KIV_ST_COLD_LEN);
   griddep_wait();
   const int b = blockIdx.x / CL;
   const int r = cl_rank<CL>();
   const int S = st.page_size;
-  const FineGeom f = fine_geom(st);
-  const int64_t C = f.U * S + (f.part_owned ? f.partial : 0);
-  const int64_t chunk = ((C + CL - 1) / CL + 15) / 16 * 16;
-  const int64_t lo = std::min<int64_t>(C, r * chunk);
-  const int n_local = (int)(std::min<int64_t>(C, lo + chunk) - lo);
+  // This CTA's index range is fixed by the candidate capacity, so the input
+  // copies start before the candidate count is known (one round trip for
+  // the copies and the state read together); keys past the count are unused.
+  const int64_t chunk = ((w.c_cap + CL - 1) / CL + 15) / 16 * 16;
+  const int64_t lo = std::min<int64_t>(w.c_cap, r * chunk);
+  const int64_t n_cap = std::min<int64_t>(w.c_cap, lo + chunk) - lo;
   const uint32_t *src = w.agg + (int64_t)b * w.c_cap + lo;
-  const int64_t P = std::min<int64_t>(q.top_p, C);
-  const bool all = P >= C;
   uint32_t *hb = w.fhist + (int64_t)b * SEL_BINS;
-  int32_t *out = sel + (int64_t)b * q.top_p;
-  float *osc = scores ? scores + (int64_t)b * q.top_p : nullptr;
-  // ---- inputs -> shared memory (one round trip)
-  const bool kstaged = n_local > 0 && n_local <= kcap && (reinterpret_cast<uintptr_t>(src) & 15) == 0;
-  const bool ustaged = r == 0 && f.U > 0 && f.U <= ucap;
+  const bool kstaged = n_cap > 0 && n_cap <= kcap && (reinterpret_cast<uintptr_t>(src) & 15) == 0;
   if (threadIdx.x == 0) {
-    const uint32_t kb = kstaged ? (uint32_t)((n_local * 4 + 15) & ~15) : 0u;
-    const uint32_t ub = ustaged ? (uint32_t)((f.U * 4 + 15) & ~15) : 0u;
+    const uint32_t kb = kstaged ? (uint32_t)((n_cap * 4 + 15) & ~15ll) : 0u;
+    const uint32_t ub = r == 0 && ucap > 0 ? (uint32_t)((ucap * 4 + 15) & ~15) : 0u;
     mbar_arrive_tx(&bar, SEL_BINS * 4 + kb + ub);
     bulk_g2s(cs.hist, hb, SEL_BINS * 4, &bar);
     if (kb) bulk_g2s(skey, src, kb, &bar);
     if (ub) bulk_g2s(suni, w.uni, ub, &bar);
   }
+  FineGeom f;
+  f.U = st_ld(st.state, KIV_ST_UNION);
+  f.np_global = cold / S;
+  f.partial = cold % S;
+  f.part_owned = f.partial > 0 && (f.np_global % st.shard_count) == st.shard_rank;
+  f.per_b = f.U + (f.part_owned ? 1 : 0);
+  f.items = (int64_t)st.batch * f.per_b;
+  const int64_t C = f.U * S + (f.part_owned ? f.partial : 0);
+  const int n_local = (int)std::max<int64_t>(0, std::min<int64_t>(C, lo + n_cap) - lo);
+  const int64_t P = std::min<int64_t>(q.top_p, C);
+  const bool all = P >= C;
+  const bool ustaged = r == 0 && f.U > 0 && f.U <= ucap;
+  int32_t *out = sel + (int64_t)b * q.top_p;
+  float *osc = scores ? scores + (int64_t)b * q.top_p : nullptr;
   // cleanup inputs, loaded while the copies fly
   unsigned long long st_mk = 0, st_sb = 0;
   int64_t pending = 0;

@@ -110,8 +110,11 @@ scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_que
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = s_tmem;
+  // fine pass: the cold length was published by the eviction, kernels back
+  int64_t cold = COARSE ? 0 : st_ld(st.state, KIV_ST_COLD_LEN);
   // ---- the previous kernel's results (state, union) are needed from here on
   griddep_wait();
+  if (COARSE) cold = st_ld(st.state, KIV_ST_COLD_LEN);
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     st.state[COARSE ? KIV_ST_COARSE_MAX : KIV_ST_FINE_MAX] = 0;
     st.state[COARSE ? KIV_ST_COARSE_SUM : KIV_ST_FINE_SUM] = 0;
@@ -119,7 +122,6 @@ scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_que
 
   TcGeom f;
   const int32_t *pages = w.uni;
-  const int64_t cold = st_ld(st.state, KIV_ST_COLD_LEN);
   f.np_global = cold / S;
   f.partial = cold % S;
   f.part_owned = f.partial > 0 && (f.np_global % st.shard_count) == st.shard_rank;
@@ -128,33 +130,40 @@ scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_que
   if (COARSE) {
     clear_stale_marks(st, w, np_local);
     f.U = 0;
-  } else if (union_inline && st_ld(st.state, KIV_ST_UNION_PENDING) != 0) {
-    // a new coarse pass marked its pages: every CTA builds the sorted union
-    // from the page marks; CTA 0 also publishes it (the select kernel and the
-    // reuse path read it from the workspace)
-    // the page marks come in with one bulk copy into the (still unused) stage ring
+  } else if (union_inline) {
+    // The page marks of a new coarse pass come in with one bulk copy into the
+    // (still unused) stage ring, issued before knowing whether a coarse pass
+    // is pending so that both reads share one round trip.  When one is, every
+    // CTA builds the sorted union from the marks and CTA 0 also publishes it
+    // (the select kernel and the reuse path read it from the workspace).
     const uint32_t fbytes = (uint32_t)((((np_local + 31) / 32) * 4 + 15) & ~15ll);
     const bool bulk = np_local > 0 && (int64_t)fbytes <= (int64_t)stages * tile_bytes && fbytes < (1u << 20);
-    if (bulk) {
-      if (threadIdx.x == 0) {
-        mbar_arrive_tx(&ubar, fbytes);
-        bulk_g2s(stage_mem, w.pbits, fbytes, &ubar);
+    if (bulk && threadIdx.x == 0) {
+      mbar_arrive_tx(&ubar, fbytes);
+      bulk_g2s(stage_mem, w.pbits, fbytes, &ubar);
+    }
+    const bool pending = st_ld(st.state, KIV_ST_UNION_PENDING) != 0;
+    if (bulk && !mbar_wait_bounded(&ubar, 0)) s_fail = 1;
+    if (pending) {
+      if (bulk)
+        f.U = union_from_bits<TC_THREADS, true>(reinterpret_cast<const uint32_t *>(stage_mem), np_local, ulist,
+                                                (int)w.u_cap, st.shard_rank, st.shard_count, s_psum);
+      else
+        f.U = union_from_bits<TC_THREADS, false>(w.pbits, np_local, ulist, (int)w.u_cap, st.shard_rank,
+                                                 st.shard_count, s_psum);
+      if (blockIdx.x == 0) {
+        for (int i = threadIdx.x; i < f.U; i += TC_THREADS) w.uni[i] = ulist[i];
+        if (threadIdx.x == 0) st.state[KIV_ST_UNION] = f.U;
       }
-      if (!mbar_wait_bounded(&ubar, 0)) s_fail = 1;
-      f.U = union_from_bits<TC_THREADS, true>(reinterpret_cast<const uint32_t *>(stage_mem), np_local, ulist,
-                                              (int)w.u_cap, st.shard_rank, st.shard_count, s_psum);
+      pages = ulist;
+    } else {
+      f.U = st_ld(st.state, KIV_ST_UNION);
+    }
+    if (bulk) {
       // the stage ring is written by TMA next: order these generic reads first
       tc::fence_proxy_async_smem();
       __syncthreads();
-    } else {
-      f.U = union_from_bits<TC_THREADS, false>(w.pbits, np_local, ulist, (int)w.u_cap, st.shard_rank,
-                                               st.shard_count, s_psum);
     }
-    if (blockIdx.x == 0) {
-      for (int i = threadIdx.x; i < f.U; i += TC_THREADS) w.uni[i] = ulist[i];
-      if (threadIdx.x == 0) st.state[KIV_ST_UNION] = f.U;
-    }
-    pages = ulist;
   } else {
     f.U = st_ld(st.state, KIV_ST_UNION);
   }
