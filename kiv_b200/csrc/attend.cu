@@ -23,7 +23,8 @@ namespace kiv {
 constexpr int AT_THREADS = 256;
 constexpr int AT_STAGES = 2;
 constexpr int CB_THREADS = 256;
-constexpr int CB_COLS = 64;        // output columns per combine CTA
+constexpr int CB_COLS_SPLIT = 16;  // output columns per CTA, merge of one rank's splits
+constexpr int CB_COLS_X = 64;      // output columns per CTA, merge across ranks
 
 template <typename T>
 struct AttnArgs {
@@ -716,7 +717,7 @@ static kiv_status launch_am(const AttnArgs<T> &a, cudaStream_t s) {
 // and the NG groups are merged in a fixed order (deterministic).
 // final_out != nullptr: write out/sum in the store dtype at [B, Q, Hq, D];
 // otherwise write the merged (out, max, sum).
-template <typename T, bool X>
+template <typename T, bool X, int CB_COLS>
 __global__ void __launch_bounds__(CB_THREADS)
 combine_kernel(const float *part, int64_t row_stride, int64_t pstride, int n, int D, int Hq, int Q,
                T *final_out, float *merged, XArgs x, const float *mine, int64_t rows, int64_t *state) {
@@ -833,8 +834,8 @@ combine_kernel(const float *part, int64_t row_stride, int64_t pstride, int n, in
 template <typename T>
 static void launch_combine(const float *part, int64_t row_stride, int64_t pstride, int n, int D, int Hq,
                            int Q, int64_t rows, T *final_out, float *merged, cudaStream_t s) {
-  const int64_t nch = ceil_div(D, CB_COLS);
-  launch_pdl(combine_kernel<T, false>, dim3((unsigned)(rows * nch)), dim3(CB_THREADS), 0, s, 1, part, row_stride,
+  const int64_t nch = ceil_div(D, CB_COLS_SPLIT);
+  launch_pdl(combine_kernel<T, false, CB_COLS_SPLIT>, dim3((unsigned)(rows * nch)), dim3(CB_THREADS), 0, s, 1, part, row_stride,
              pstride, n, D, Hq, Q, final_out, merged, XArgs{}, (const float *)nullptr, rows, (int64_t *)nullptr);
 }
 
@@ -959,10 +960,10 @@ kiv_status launch_attend_merge(const kiv_store *st, const kiv_query *q, const fl
   const int D = st->head_dim, Dp = partial_stride(D);
   if (x) {
     // partials: this rank's [R, Dp]; the ranks' partials meet in the arenas
-    const int64_t nch = ceil_div(D, CB_COLS);
+    const int64_t nch = ceil_div(D, CB_COLS_X);
     const dim3 grid((unsigned)(rows * nch));
 #define KIV_XC(TT)                                                                                         \
-  launch_pdl(combine_kernel<TT, true>, grid, dim3(CB_THREADS), 0, s, 1, (const float *)nullptr, (int64_t)Dp,      \
+  launch_pdl(combine_kernel<TT, true, CB_COLS_X>, grid, dim3(CB_THREADS), 0, s, 1, (const float *)nullptr, (int64_t)Dp,      \
              rows, x->world, D, q->num_query_heads, q->query_len, (TT *)out, (float *)nullptr, *x, partials, rows, \
              st->state)
     switch (st->dtype) {
