@@ -17,8 +17,9 @@
 //          store, and the first radix-select histogram + score stats of the
 //          batch row (so the select kernel skips its first pass).
 // The query rows are written once into shared memory in the same swizzled
-// K-major layout.  Every load targets only this CTA.  Used when the store is 16-bit,
-// page_size == 128, head_dim is a multiple of 64 (<= 256), batch == 1 and
+// K-major layout.  Every load targets only this CTA.  CTAs are grouped by
+// batch row (each group stages its row's queries once).  Used when the store
+// is 16-bit, page_size == 128, head_dim is a multiple of 64 (<= 256) and
 // G*Q <= 32; otherwise fine_scores_kernel runs.
 #include <algorithm>
 
@@ -43,7 +44,7 @@ struct TcGeom {
 template <bool BF16, bool COARSE>
 __global__ void __launch_bounds__(TC_THREADS, 1)
 scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_query q, Workspace w,
-                 int ncols, int stages, int union_inline) {
+                 int ncols, int stages, int union_inline, int cpb) {
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   extern __shared__ uint8_t tc_dyn[];
   __shared__ uint64_t full[4], empty[4], acc_full[2], acc_empty[2], ubar;
@@ -59,6 +60,9 @@ scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_que
   const int nbox = D / 64;
   const uint32_t tile_bytes = (uint32_t)TC_PAGE * D * sizeof(T);
   const uint32_t qbox_bytes = (uint32_t)ncols * 128;
+  // CTAs are grouped by batch row: cpb consecutive CTAs serve batch row b,
+  // whose query rows are staged once
+  const int b = blockIdx.x / cpb, cj = blockIdx.x % cpb;
 
   // 1024-byte aligned carve-up: [stages][tile] [H][nbox][qbox] [hist 2048] [union list]
   const uint32_t base_addr = smem_u32(tc_dyn);
@@ -89,8 +93,8 @@ scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_que
     tc::tmem_relinquish();
   }
   if (threadIdx.x == 32 * 4) tc::prefetch_map(&kmap);
-  // query rows of batch row 0 -> swizzled K-major tiles [kvh][box][ncols x 128 B]
-  const T *qb = reinterpret_cast<const T *>(q.q);
+  // query rows of batch row b -> swizzled K-major tiles [kvh][box][ncols x 128 B]
+  const T *qb = reinterpret_cast<const T *>(q.q) + (int64_t)b * q.stride_b;
   for (int e = threadIdx.x; e < H * ncols * (D / 8); e += TC_THREADS) {
     const int chunk = e % (D / 8);            // 16-byte chunk along D
     const int n = (e / (D / 8)) % ncols;      // query row within the KV head
@@ -168,11 +172,13 @@ scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_que
     f.U = st_ld(st.state, KIV_ST_UNION);
   }
   f.per_b = f.U + (f.part_owned ? 1 : 0);
-  // batch 1.  FINE: one unit per candidate page (tiles = its KV heads);
-  // COARSE: one unit per block of 128 finalized local pages (tiles = KV heads)
+  // per batch row b.  FINE: one unit per candidate page (tiles = its KV
+  // heads); COARSE: one unit per block of 128 finalized local pages (tiles =
+  // KV heads).  CTA cj of the row's cpb takes units cj, cj + cpb, ...
   const int64_t units = COARSE ? (np_local + TC_PAGE - 1) / TC_PAGE : f.per_b;
-  const int64_t my_units = units > blockIdx.x ? (units - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+  const int64_t my_units = units > cj ? (units - cj + cpb - 1) / cpb : 0;
   const int64_t my_tiles = my_units * H;
+  const int64_t bh0 = (int64_t)b * H;
 
   if (warp == 4) {
     if (lane == 0) {
@@ -183,15 +189,15 @@ scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_que
           s_fail = 1;
           break;
         }
-        const int64_t u = blockIdx.x + (t / H) * gridDim.x;
+        const int64_t u = cj + (t / H) * cpb;
         const int kvh = (int)(t % H);
         int32_t y;
         if (COARSE) {
-          y = (int32_t)((int64_t)kvh * w.np_cap + u * TC_PAGE);
+          y = (int32_t)((bh0 + kvh) * w.np_cap + u * TC_PAGE);
         } else {
           const int64_t page = u < f.U ? (int64_t)pages[u] : f.np_global;
           const int64_t lp = page / st.shard_count;
-          y = (int32_t)((int64_t)kvh * st.cold_capacity + lp * S);
+          y = (int32_t)((bh0 + kvh) * st.cold_capacity + lp * S);
         }
         mbar_arrive_tx(&full[s], tile_bytes);
         for (int j = 0; j < nbox; ++j)
@@ -236,7 +242,7 @@ scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_que
       uint32_t r[16];
       if (COARSE) {
         // one score per (query row, page): thread tok holds page u*128 + tok
-        const int64_t u = blockIdx.x + (t / H) * gridDim.x;
+        const int64_t u = cj + (t / H) * cpb;
         const int kvh = (int)(t % H);
         const int64_t p = u * TC_PAGE + tok;
         for (int c0 = 0; c0 < ncols; c0 += 16) {
@@ -249,7 +255,7 @@ scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_que
               if (rr < rows_kv) {
                 const float sc = __uint_as_float(r[c]) * q.scaling;
                 const int h = kvh * G + rr / Q, tq = rr % Q;
-                const int64_t R_idx = (int64_t)h * Q + tq;
+                const int64_t R_idx = ((int64_t)b * Hq + h) * Q + tq;
                 w.scores[R_idx * w.np_cap + p] = sc;
                 const uint32_t key = f2key(sc);
                 hist_add(w.chist + R_idx * SEL_BINS, key >> 21);
@@ -275,11 +281,11 @@ scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_que
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[a]);
       if ((t % H) == H - 1) {
-        const int64_t u = blockIdx.x + (t / H) * gridDim.x;
+        const int64_t u = cj + (t / H) * cpb;
         const int n_tok = u < f.U ? TC_PAGE : (int)f.partial;
         if (tok < n_tok) {
           const uint32_t key = f2key(m);
-          w.agg[u * S + tok] = key;
+          w.agg[(int64_t)b * w.c_cap + u * S + tok] = key;
           hist_add(hist, key >> 21);
           kmax = key > kmax ? key : kmax;
           ksum += m;
@@ -302,7 +308,7 @@ scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_que
   // publish the histogram and the stats of batch row 0 for the select kernel
   if (!COARSE) {
     for (int i = threadIdx.x; i < SEL_BINS; i += TC_THREADS)
-      if (hist[i]) atomicAdd(&w.fhist[i], hist[i]);
+      if (hist[i]) atomicAdd(&w.fhist[(int64_t)b * SEL_BINS + i], hist[i]);
   }
   if (threadIdx.x == 0) {
     uint32_t mk = 0;
@@ -316,8 +322,8 @@ scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_que
         atomicMax(reinterpret_cast<unsigned long long *>(&w.cstat[0]), (unsigned long long)mk);
         atomicAdd(reinterpret_cast<double *>(&w.cstat[1]), sm);
       } else {
-        atomicMax(reinterpret_cast<unsigned long long *>(&w.fstat[0]), (unsigned long long)mk);
-        atomicAdd(reinterpret_cast<double *>(&w.fstat[1]), sm);
+        atomicMax(reinterpret_cast<unsigned long long *>(&w.fstat[2 * b]), (unsigned long long)mk);
+        atomicAdd(reinterpret_cast<double *>(&w.fstat[2 * b + 1]), sm);
       }
     }
     if (s_fail)
@@ -348,8 +354,8 @@ bool fine_tc_eligible(const kiv_store *st, const kiv_query *q) {
   const int ncols = rows_kv <= 16 ? 16 : 32;
   const size_t qbytes = (size_t)st->num_kv_heads * ncols * st->head_dim * 2;
   return (st->dtype == KIV_DTYPE_BF16 || st->dtype == KIV_DTYPE_F16) && st->page_size == TC_PAGE &&
-         st->head_dim % 64 == 0 && st->head_dim <= 256 && st->batch == 1 && rows_kv <= 32 &&
-         qbytes <= 32 * 1024 && (int64_t)st->num_kv_heads * st->cold_capacity < (1ll << 31) &&
+         st->head_dim % 64 == 0 && st->head_dim <= 256 && rows_kv <= 32 && qbytes <= 32 * 1024 &&
+         (int64_t)st->batch * st->num_kv_heads * st->cold_capacity < (1ll << 31) &&
          getenv("KIV_DISABLE_TCGEN05") == nullptr;
 }
 
@@ -361,7 +367,8 @@ static kiv_status launch_scores_tc(const kiv_store *st, const kiv_query *q, cons
   const int rows_kv = (q->num_query_heads / st->num_kv_heads) * q->query_len;
   const int ncols = rows_kv <= 16 ? 16 : 32;
   CUtensorMap map;
-  const int64_t rows = coarse ? (int64_t)st->num_kv_heads * w.np_cap : (int64_t)st->num_kv_heads * st->cold_capacity;
+  const int64_t bh = (int64_t)st->batch * st->num_kv_heads;
+  const int64_t rows = coarse ? bh * w.np_cap : bh * st->cold_capacity;
   const cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)D * 2};
   const cuuint32_t box[2] = {64, TC_PAGE};
@@ -384,13 +391,15 @@ static kiv_status launch_scores_tc(const kiv_store *st, const kiv_query *q, cons
   const int stages = (int)std::min<size_t>(4, (200 * 1024 - fixed) / tile);
   if (stages < 2) return KIV_ERR_UNSUPPORTED;
   const size_t smem = fixed + (size_t)stages * tile;
+  // per batch row: cpb CTAs (about the SMs shared out over the rows)
   const int64_t units_cap = coarse ? ceil_div(w.np_cap, TC_PAGE) : w.u_cap + 1;
-  const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(units_cap, sm_count()));
+  const int64_t cpb = std::max<int64_t>(1, std::min<int64_t>(units_cap, sm_count() / st->batch));
+  const int64_t grid = (int64_t)st->batch * cpb;
 #define KIV_TC_LAUNCH(BF, CO)                                                                          \
   do {                                                                                                 \
     cudaFuncSetAttribute(scores_tc_kernel<BF, CO>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
     e = launch_pdl(scores_tc_kernel<BF, CO>, dim3((unsigned)grid), dim3(TC_THREADS), smem, s, 1, map, *st, *q, w, \
-                   ncols, stages, union_inline);                                                        \
+                   ncols, stages, union_inline, (int)cpb);                                              \
   } while (0)
   const bool bf = st->dtype == KIV_DTYPE_BF16;
   cudaError_t e = cudaSuccess;

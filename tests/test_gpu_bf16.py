@@ -2,8 +2,9 @@
 and the CUDA-core scoring and attention) against the oracle run on the same
 bf16-valued inputs in float64 math.
 
-Shapes are the c1 (Qwen2.5-7B: Hq 28 / Hkv 4 / D 128) and c2 (Gemma-style MQA:
-Hq 8 / Hkv 1 / D 256) decode shapes with a reduced cold length.  Index sets
+Shapes are the c1 (Qwen2.5-7B: Hq 28 / Hkv 4 / D 128), c2 (Gemma-style MQA:
+Hq 8 / Hkv 1 / D 256) and c3 (Llama-3-8B, batch of sequences: Hq 32 / Hkv 8 /
+D 128, 4 sequences) decode shapes with a reduced cold length.  Index sets
 must match except ties within 1e-6 relative of the k-th score (the tensor
 cores and the CUDA cores accumulate in fp32 in different orders, the oracle in
 float64); attention within 2e-2 relative (bf16 output).
@@ -24,6 +25,9 @@ SHAPES = {
                      hot_budget=2048), dict(top_pages=32, top_p=512)),
     "c2": (SynthSpec(batch=1, num_query_heads=8, num_kv_heads=1, head_dim=256, cold_tokens=65536,
                      hot_budget=2048), dict(top_pages=64, top_p=1024)),
+    # c3 (Llama-3-8B shape, batched decode) with 4 sequences and a shorter cold tier
+    "c3": (SynthSpec(batch=4, num_query_heads=32, num_kv_heads=8, head_dim=128, cold_tokens=16384 + 37,
+                     hot_budget=1024), dict(top_pages=32, top_p=512)),
 }
 
 
