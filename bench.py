@@ -58,6 +58,9 @@ WORKLOADS = {
     "tiny": dict(layers=3, hq=8, hkv=1, d=256, cold=65536, hot=2048, top_pages=64, top_p=1024),
     # c2 per-layer shapes at full size, 3 layers (a few GB: small enough for ncu captures)
     "c2s": dict(layers=3, hq=8, hkv=1, d=256, cold=1048576, hot=2048, top_pages=64, top_p=1024),
+    # c3 (Llama-3-8B shape, 64 sequences x 262,144 cold + 4096 hot) one layer: the full
+    # model's cold tier (2.2 TB) does not fit one GPU; one layer holds 69 GB
+    "c3l": dict(layers=1, hq=32, hkv=8, d=128, cold=262144, hot=4096, top_pages=32, top_p=512, batch=64),
 }
 PAGE = 128
 SEGMENT = 512
@@ -161,14 +164,14 @@ class ClockSampler:
 
 def step_algorithmic_bytes(w, U, partial, e=2):
     """Bytes one layer-step must move (each element read or written once)."""
-    row = w["hkv"] * w["d"] * e
+    row = w.get("batch", 1) * w["hkv"] * w["d"] * e
     npg = (w["cold"]) // PAGE
     return (npg * row                      # coarse: page summaries
             + (U * PAGE + partial) * row   # fine: candidate K rows
             + 2 * w["top_p"] * row         # attention: selected K and V rows
             + 2 * w["hot"] * row           # attention: hot K and V
             + 2 * row                      # eviction: one K/V row written
-            + w["hq"] * w["d"] * 2 * e)    # query in, output out
+            + w.get("batch", 1) * w["hq"] * w["d"] * 2 * e)    # query in, output out
 
 
 # --------------------------------------------------------------- the cache
@@ -188,26 +191,28 @@ def build_cache(w, dev, kcfg, comm, queries0):
                                 num_kv_heads=w["hkv"], head_dim=d, num_hidden_layers=L)
     cache = TieredKVCache(PretrainedConfig(num_hidden_layers=L), kcfg, topo, dev, shard_group=comm)
     T = w["cold"] + w["hot"]
-    chunk = 65536
+    B = w.get("batch", 1)
+    chunk = max(4096, 65536 // B)
     for li in range(L):
         gen = torch.Generator(device=dev)
         gen.manual_seed(1000 + li)
         n_seg = (T + w["hot"] + SEGMENT) // SEGMENT + 2
-        cent = torch.randn(w["hkv"], n_seg, d, generator=gen, device=dev) / math.sqrt(64.0)
+        cent = torch.randn(B, w["hkv"], n_seg, d, generator=gen, device=dev) / math.sqrt(64.0)
         needle = int(torch.randint(0, w["cold"] // PAGE, (1,), generator=gen, device=dev).item())
         G = w["hq"] // w["hkv"]
-        qm = queries0[li].float().reshape(w["hkv"], G, d).mean(dim=1)
+        qm = queries0[li].float().reshape(B, w["hkv"], G, d).mean(dim=2)
         qhat = qm / qm.norm(dim=-1, keepdim=True)
         for a in range(0, T, chunk):
             n = min(chunk, T - a)
-            k = torch.stack([keys_for(gen, n, d, cent[h], a, dev) for h in range(w["hkv"])])
-            v = torch.randn(w["hkv"], n, d, generator=gen, device=dev)
+            seg = torch.arange(a, a + n, device=dev) // SEGMENT
+            k = cent[:, :, seg] + 0.3 * torch.randn(B, w["hkv"], n, d, generator=gen, device=dev)
+            v = torch.randn(B, w["hkv"], n, d, generator=gen, device=dev)
             lo, hi = needle * PAGE, (needle + 1) * PAGE
             if lo < a + n and hi > a:
                 s0, s1 = max(lo, a) - a, min(hi, a + n) - a
-                k[:, s0:s1] = 2.0 * qhat[:, None, :] + 0.3 * torch.randn(
-                    w["hkv"], s1 - s0, d, generator=gen, device=dev)
-            cache.update(k[None].to(torch.bfloat16), v[None].to(torch.bfloat16), li)
+                k[:, :, s0:s1] = 2.0 * qhat[:, :, None, :] + 0.3 * torch.randn(
+                    B, w["hkv"], s1 - s0, d, generator=gen, device=dev)
+            cache.update(k.to(torch.bfloat16), v.to(torch.bfloat16), li)
             cache._evict_to_cap(w["hot"])
         del k, v
     cache._prefill_complete = True
@@ -220,10 +225,11 @@ def make_inputs(w, dev, n, seed=7):
     g = torch.Generator(device=dev)
     g.manual_seed(seed)
     L, d = w["layers"], w["d"]
-    q = torch.randn(n, L, 1, w["hq"], 1, d, generator=g, device=dev).to(torch.bfloat16)
-    cent = torch.randn(L, 1, w["hkv"], 1, d, generator=g, device=dev) / math.sqrt(64.0)
-    k = (cent[None] + 0.3 * torch.randn(n, L, 1, w["hkv"], 1, d, generator=g, device=dev)).to(torch.bfloat16)
-    v = torch.randn(n, L, 1, w["hkv"], 1, d, generator=g, device=dev).to(torch.bfloat16)
+    B = w.get("batch", 1)
+    q = torch.randn(n, L, B, w["hq"], 1, d, generator=g, device=dev).to(torch.bfloat16)
+    cent = torch.randn(L, B, w["hkv"], 1, d, generator=g, device=dev) / math.sqrt(64.0)
+    k = (cent[None] + 0.3 * torch.randn(n, L, B, w["hkv"], 1, d, generator=g, device=dev)).to(torch.bfloat16)
+    v = torch.randn(n, L, B, w["hkv"], 1, d, generator=g, device=dev).to(torch.bfloat16)
     return q, k, v
 
 
@@ -349,7 +355,7 @@ def main():
                      telemetry=False)
     q_pool, k_pool, v_pool = make_inputs(w, dev, INPUT_POOL)
     t_build = time.perf_counter()
-    cache = build_cache(w, dev, kcfg, comm, q_pool[0, :, 0, :, 0, :])
+    cache = build_cache(w, dev, kcfg, comm, q_pool[0, :, :, :, 0, :])
     t_build = time.perf_counter() - t_build
     scaling = w["d"] ** -0.5
     layers = list(range(L))
@@ -390,7 +396,7 @@ def main():
             m = dict(rec[li].marks)
             t_fine = m["fine_score_begin"].elapsed_time(m["fine_score_end"])
             fine_ms += t_fine
-            fine_bytes += (U * PAGE + own_partial) * w["hkv"] * w["d"] * 2
+            fine_bytes += w.get("batch", 1) * (U * PAGE + own_partial) * w["hkv"] * w["d"] * 2
             for a, b, name in (("update_begin", "coarse_begin", "update"),
                                ("coarse_begin", "fine_score_begin", "coarse"),
                                ("fine_score_begin", "fine_score_end", "fine_score"),
@@ -410,7 +416,7 @@ def main():
     static_q = torch.empty_like(q_pool[0])
     static_k = torch.empty_like(k_pool[0])
     static_v = torch.empty_like(v_pool[0])
-    out = torch.empty(L, 1, 1, w["hq"], w["d"], dtype=torch.bfloat16, device=dev)
+    out = torch.empty(L, w.get("batch", 1), 1, w["hq"], w["d"], dtype=torch.bfloat16, device=dev)
     i0 = (W + R) % INPUT_POOL
     static_q.copy_(q_pool[i0]); static_k.copy_(k_pool[i0]); static_v.copy_(v_pool[i0])
     graph = DecodeGraph(cache, layers, scaling, static_q, static_k, static_v, out, max_steps=2 * K + 4)
@@ -484,7 +490,7 @@ def main():
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": f"{args.workload}: {L} layers, Hq={w['hq']} Hkv={w['hkv']} D={w['d']}, "
                                    f"{w['cold']} cold + {w['hot']} hot tokens per layer, page={PAGE}, "
-                                   f"top_pages={w['top_pages']}, top_p={w['top_p']}, batch 1",
+                                   f"top_pages={w['top_pages']}, top_p={w['top_p']}, batch {w.get('batch', 1)}",
                        "parallelism": f"cold pages sharded over {world} GPU(s)" if world > 1 else "1 GPU",
                        "l2": "inputs larger than L2 (each step touches 35 layers x ~39 MB)",
                        "timing": "CUDA graph of one 35-layer step replayed, CUDA events, max over ranks"},
