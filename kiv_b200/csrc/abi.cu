@@ -55,7 +55,7 @@ Workspace workspace_layout(const kiv_store *st, const kiv_query *q, void *base) 
   w.selcnt = reinterpret_cast<int32_t *>(take((int64_t)st->batch * 4));
   w.fhist = reinterpret_cast<uint32_t *>(take((int64_t)st->batch * 2048 * 4));
   w.fstat = reinterpret_cast<uint64_t *>(take((int64_t)st->batch * 16));
-  w.chist = reinterpret_cast<uint32_t *>(take(w.R * 2048 * 4));
+  w.chist = reinterpret_cast<uint32_t *>(take(prefill_shape(st, q) ? 0 : w.R * 2048 * 4));
   w.cstat = reinterpret_cast<uint64_t *>(take(16));
   w.part = reinterpret_cast<float *>(take(w.R * w.split_cap * partial_stride(st->head_dim) * 4));
   w.bytes = (size_t)off;

@@ -899,6 +899,291 @@ static kiv_status dispatch_at(AttnArgs<T> a, cudaStream_t s) {
   return KIV_ERR_UNSUPPORTED;
 }
 
+// ---------------------------------------------------------------------------
+// Prefill-shaped attention (more than 16 query rows per KV head, e.g. a
+// 4096-position chunk): flash-style, no split partials.  CTA = (batch row, KV
+// head, 64 of its G*Q query rows); 4 warps own 16 rows each and run over all
+// keys [selected cold ; hot] in tiles of 64: K and V rows gathered by
+// cp.async into a 2-stage ring (padded rows), S = Q K^T and O += P V on
+// m16n8k16 MMAs with the query fragments held in registers, online softmax in
+// registers (P rounded to the store dtype for the second MMA, the running sum
+// kept in fp32).  Hot rows past the last causally visible one of the tile are
+// not loaded.  Masking and soft-capping as attend_mma_kernel: soft-cap on the
+// scaled score, then the causal rule / additive mask on hot columns only.
+constexpr int AP_THREADS = 128;
+constexpr int AP_ROWS = 64;
+constexpr int AP_KEYS = 64;
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(AP_THREADS)
+attend_prefill_kernel(AttnArgs<T> a, T *out, float *partial_out) {
+  extern __shared__ __align__(128) uint8_t ap_smem[];
+  using Op = MmaOp<T>;
+  constexpr int PITCH = D * 2 + 16;            // bytes per staged row (conflict-free ldmatrix)
+  constexpr int NC = D / 8;                    // 16-byte chunks per row
+  constexpr int KD = D / 16;                   // k-steps of S = Q K^T
+  constexpr int NO = D / 8;                    // 8-column output tiles
+  const kiv_store &st = a.st;
+  const kiv_query &q = a.q;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 2, t4 = lane & 3;
+  const int H = st.num_kv_heads, S = st.page_size;
+  const int Hq = q.num_query_heads, G = Hq / H, Q = q.query_len;
+  const int rows_kv = G * Q;
+  const int nrt = (rows_kv + AP_ROWS - 1) / AP_ROWS;
+  const int rt = blockIdx.x % nrt;
+  const int bhi = blockIdx.x / nrt;
+  const int b = bhi / H, kvh = bhi % H;
+  const int r0 = rt * AP_ROWS;
+  uint8_t *qs = ap_smem;                       // [64][PITCH]
+  uint8_t *ks = qs + AP_ROWS * PITCH;          // [2][64][PITCH]
+  uint8_t *vs = ks + 2 * AP_KEYS * PITCH;      // [2][64][PITCH]
+
+  // ---- prologue: the query tile and the hot window were written before the step
+  {
+    const T *qb = reinterpret_cast<const T *>(q.q);
+    for (int e = threadIdx.x; e < AP_ROWS * NC; e += AP_THREADS) {
+      const int rr = e / NC, c = e % NC, r = r0 + rr;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (r < rows_kv) {
+        const int h = kvh * G + r / Q, tq = r % Q;
+        v = ld16(qb + b * q.stride_b + h * q.stride_h + tq * q.stride_t + c * 8);
+      }
+      *reinterpret_cast<uint4 *>(qs + rr * PITCH + c * 16) = v;
+    }
+  }
+  const int64_t hot_len = st_ld(st.state, KIV_ST_HOT_LEN);
+  const int64_t hot_start = st_ld(st.state, KIV_ST_HOT_START);
+  const int64_t hot_lo = hot_len * a.hot_slice / a.hot_slices;
+  const int64_t hot_hi = hot_len * (a.hot_slice + 1) / a.hot_slices;
+  // ---- the selection (previous kernel) is needed from here on
+  griddep_wait();
+  const int64_t ncold = a.w.selcnt[b];
+  int64_t hot_use = hot_hi - hot_lo;
+  if (a.mask.causal && a.mask.add == nullptr) {
+    const int rlast = min(rows_kv, r0 + AP_ROWS) - 1;
+    const int tq_max = (r0 / Q != rlast / Q) ? Q - 1 : rlast % Q;
+    hot_use = std::max<int64_t>(0, std::min<int64_t>(hot_use, hot_len - Q + tq_max + 1 - hot_lo));
+  }
+  const int64_t nkeys = ncold + hot_use;
+  const int ntile = (int)((nkeys + AP_KEYS - 1) / AP_KEYS);
+  const T *cold_k = reinterpret_cast<const T *>(st.cold_k);
+  const T *cold_v = reinterpret_cast<const T *>(st.cold_v);
+  const T *hot_k = reinterpret_cast<const T *>(st.hot_k);
+  const T *hot_v = reinterpret_cast<const T *>(st.hot_v);
+  const int32_t *selb = a.sel + (int64_t)b * a.sel_stride;
+  const int64_t bhk = (int64_t)b * H + kvh;
+  auto issue = [&](int t) {
+    const int stage = t & 1;
+    const int64_t k0 = (int64_t)t * AP_KEYS;
+    for (int e = threadIdx.x; e < AP_KEYS * NC; e += AP_THREADS) {
+      const int kr = e / NC, c = e % NC;
+      const int64_t k = k0 + kr;
+      uint8_t *dk = ks + ((size_t)stage * AP_KEYS + kr) * PITCH + c * 16;
+      uint8_t *dv = vs + ((size_t)stage * AP_KEYS + kr) * PITCH + c * 16;
+      if (k < nkeys) {
+        int64_t off;
+        const T *bk, *bv;
+        if (k < ncold) {
+          const int64_t tok = selb[k], p = tok / S;
+          off = (bhk * st.cold_capacity + (p / st.shard_count) * S + tok % S) * D;
+          bk = cold_k;
+          bv = cold_v;
+        } else {
+          const int64_t slot = (hot_start + hot_lo + (k - ncold)) % st.hot_capacity;
+          off = (bhk * st.hot_capacity + slot) * D;
+          bk = hot_k;
+          bv = hot_v;
+        }
+        cp_async16(dk, bk + off + c * 8);
+        cp_async16(dv, bv + off + c * 8);
+      } else {
+        // past the last key: zero rows (P is 0 there, V must not be NaN)
+        *reinterpret_cast<uint4 *>(dk) = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4 *>(dv) = make_uint4(0, 0, 0, 0);
+      }
+    }
+    cp_async_commit();
+  };
+  if (ntile > 0) issue(0);
+  if (ntile > 1) issue(1);
+  __syncthreads();   // query tile staged
+  uint32_t qf[KD][4];
+#pragma unroll
+  for (int kk = 0; kk < KD; ++kk)
+    ldsm_x4(qf[kk], qs + (warp * 16 + (lane & 15)) * PITCH + (kk * 16 + 8 * (lane >> 4)) * 2);
+  float o[NO][4];
+#pragma unroll
+  for (int i = 0; i < NO; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+  // the two query rows of this thread: (head, position) and causal limits
+  int rrow[2], hrow[2], tqrow[2];
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    rrow[hh] = r0 + warp * 16 + g + 8 * hh;
+    hrow[hh] = kvh * G + rrow[hh] / Q;
+    tqrow[hh] = rrow[hh] % Q;
+  }
+
+  for (int t = 0; t < ntile; ++t) {
+    if (t + 1 < ntile) cp_async_wait<1>();
+    else cp_async_wait<0>();
+    __syncthreads();
+    const int stage = t & 1;
+    const uint8_t *kst = ks + (size_t)stage * AP_KEYS * PITCH;
+    const uint8_t *vst = vs + (size_t)stage * AP_KEYS * PITCH;
+    // ---- S = Q K^T: 16 rows x 64 keys per warp
+    float s[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < KD; ++kk) {
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {
+        uint32_t kb[4];
+        ldsm_x4(kb, kst + (np * 16 + (lane >> 4) * 8 + (lane & 7)) * PITCH + (kk * 16 + ((lane >> 3) & 1) * 8) * 2);
+        Op::mma(s[2 * np], qf[kk], kb[0], kb[1]);
+        Op::mma(s[2 * np + 1], qf[kk], kb[2], kb[3]);
+      }
+    }
+    // ---- scale, soft-cap, mask; online softmax per row
+    const int64_t k0 = (int64_t)t * AP_KEYS;
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int hh = i >> 1;
+        const int64_t k = k0 + j * 8 + 2 * t4 + (i & 1);
+        float sc = -INFINITY;
+        if (k < nkeys && rrow[hh] < rows_kv) {
+          sc = s[j][i] * q.scaling;
+          if (q.softcap > 0.f) sc = q.softcap * tanhf(sc / q.softcap);
+          if (k >= ncold) {
+            const int64_t jh = hot_lo + (k - ncold);
+            if (a.mask.causal && jh > hot_len - Q + tqrow[hh]) sc = -INFINITY;
+            if (a.mask.add != nullptr)
+              sc += a.mask.add[b * a.mask.stride_b + hrow[hh] * a.mask.stride_h + tqrow[hh] * a.mask.stride_t + jh];
+          }
+        }
+        s[j][i] = sc;
+        mx[hh] = fmaxf(mx[hh], sc);
+      }
+    }
+    float alpha[2];
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      mx[hh] = fmaxf(mx[hh], __shfl_xor_sync(KIV_FULL_MASK, mx[hh], 1));
+      mx[hh] = fmaxf(mx[hh], __shfl_xor_sync(KIV_FULL_MASK, mx[hh], 2));
+      const float mn = fmaxf(mrow[hh], mx[hh]);
+      alpha[hh] = mn == -INFINITY ? 1.f : __expf(mrow[hh] - mn);   // mrow == -inf: 0
+      mrow[hh] = mn;
+    }
+    float lsum[2] = {0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int hh = i >> 1;
+        const float p = (s[j][i] == -INFINITY) ? 0.f : __expf(s[j][i] - mrow[hh]);
+        s[j][i] = p;
+        lsum[hh] += p;
+      }
+    }
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) lrow[hh] = lrow[hh] * alpha[hh] + lsum[hh];
+#pragma unroll
+    for (int i = 0; i < NO; ++i) {
+      o[i][0] *= alpha[0];
+      o[i][1] *= alpha[0];
+      o[i][2] *= alpha[1];
+      o[i][3] *= alpha[1];
+    }
+    // ---- O += P V (P from the S accumulators, rounded to the store dtype)
+#pragma unroll
+    for (int kc = 0; kc < 4; ++kc) {
+      uint32_t pa[4];
+      pa[0] = Op::pack2(s[2 * kc][0], s[2 * kc][1]);
+      pa[1] = Op::pack2(s[2 * kc][2], s[2 * kc][3]);
+      pa[2] = Op::pack2(s[2 * kc + 1][0], s[2 * kc + 1][1]);
+      pa[3] = Op::pack2(s[2 * kc + 1][2], s[2 * kc + 1][3]);
+      const uint8_t *vrow = vst + (kc * 16 + (lane & 15)) * PITCH + 8 * (lane >> 4) * 2;
+#pragma unroll
+      for (int nt = 0; nt < NO; nt += 2) {
+        uint32_t vb[4];
+        ldsm_x4_t(vb, vrow + nt * 16);
+        Op::mma(o[nt], pa, vb[0], vb[1]);
+        Op::mma(o[nt + 1], pa, vb[2], vb[3]);
+      }
+    }
+    __syncthreads();   // stage consumed
+    if (t + 2 < ntile) issue(t + 2);
+  }
+  // ---- rows: final output [B, Q, Hq, D] or the (out, max, sum) partial
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    float l = lrow[hh];
+    l += __shfl_xor_sync(KIV_FULL_MASK, l, 1);
+    l += __shfl_xor_sync(KIV_FULL_MASK, l, 2);
+    if (rrow[hh] >= rows_kv) continue;
+    if (out) {
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      T *dst = out + (((int64_t)b * Q + tqrow[hh]) * Hq + hrow[hh]) * D + 2 * t4;
+#pragma unroll
+      for (int nt = 0; nt < NO; ++nt)
+        *reinterpret_cast<uint32_t *>(dst + nt * 8) = Op::pack2(o[nt][2 * hh] * inv, o[nt][2 * hh + 1] * inv);
+    } else {
+      const int Dp = partial_stride(D);
+      float *dst = partial_out + (((int64_t)b * Hq + hrow[hh]) * Q + tqrow[hh]) * Dp;
+#pragma unroll
+      for (int nt = 0; nt < NO; ++nt)
+        *reinterpret_cast<float2 *>(dst + nt * 8 + 2 * t4) = make_float2(o[nt][2 * hh], o[nt][2 * hh + 1]);
+      if (t4 == 0) {
+        dst[D] = mrow[hh];
+        dst[D + 1] = l;
+      }
+    }
+  }
+}
+
+template <typename T>
+static bool attend_prefill_eligible(const kiv_store *st, const kiv_query *q) {
+  const int64_t rows_kv = (int64_t)(q->num_query_heads / st->num_kv_heads) * q->query_len;
+  const int D = st->head_dim;
+  return sizeof(T) == 2 && rows_kv > AM_ROWS && (D == 64 || D == 96 || D == 128) &&
+         getenv("KIV_DISABLE_MMA_ATTN") == nullptr;
+}
+
+template <typename T>
+static kiv_status launch_ap(const AttnArgs<T> &a, T *out, float *partial_out, cudaStream_t s) {
+  const int D = a.st.head_dim;
+  const int64_t rows_kv = (int64_t)(a.q.num_query_heads / a.st.num_kv_heads) * a.q.query_len;
+  const int64_t grid = (int64_t)a.st.batch * a.st.num_kv_heads * ceil_div(rows_kv, AP_ROWS);
+  if (grid > 0x7fffffff) return KIV_ERR_ARG;
+  const size_t smem = (size_t)(AP_ROWS + 4 * AP_KEYS) * (D * 2 + 16);
+  cudaError_t e;
+#define KIV_AP(DD)                                                                                       \
+  do {                                                                                                   \
+    cudaFuncSetAttribute(attend_prefill_kernel<T, DD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+    e = launch_pdl(attend_prefill_kernel<T, DD>, dim3((unsigned)grid), dim3(AP_THREADS), smem, s, 1, a, out, \
+                   partial_out);                                                                         \
+  } while (0)
+  if (D == 64) KIV_AP(64);
+  else if (D == 96) KIV_AP(96);
+  else KIV_AP(128);
+#undef KIV_AP
+  return cuda_status(e, "attend_prefill");
+}
+
 template <typename T>
 static kiv_status attend_t(const kiv_store *st, const kiv_query *q, const kiv_mask *m,
                            const Workspace &w, const int32_t *sel, int32_t sel_stride,
@@ -926,6 +1211,8 @@ static kiv_status attend_t(const kiv_store *st, const kiv_query *q, const kiv_ma
       1, std::min<int64_t>({w.split_cap, ceil_div(keys_hint, ATT_TILE), ceil_div(sm_count(), base)}));
   kiv_status rc;
   if constexpr (sizeof(T) == 2) {
+    if (attend_prefill_eligible<T>(st, q))
+      return launch_ap<T>(a, partial_out ? nullptr : reinterpret_cast<T *>(out), partial_out, s);
     rc = attend_mma_eligible<T>(st, q) ? launch_am<T>(a, s) : dispatch_at<T>(a, s);
   } else {
     rc = dispatch_at<T>(a, s);

@@ -147,7 +147,7 @@ coarse_scores_kernel(kiv_store st, kiv_query q, Workspace w) {
 // page order for the all-gather.
 __global__ void __launch_bounds__(TK_THREADS)
 coarse_topk_kernel(kiv_store st, kiv_query q, Workspace w, float *row_scores, int32_t *row_pages, int cap,
-                   int scap) {
+                   int scap, int self_hist) {
   extern __shared__ uint4 dyn_smem[];
   __shared__ __align__(16) CandSmem<TK_THREADS> cs;
   __shared__ SelectSmem<TK_THREADS> rs;
@@ -174,7 +174,9 @@ coarse_topk_kernel(kiv_store st, kiv_query q, Workspace w, float *row_scores, in
   const int row = blockIdx.x;
   const int K = q.top_pages;
   const int rank = st.shard_rank, nsh = st.shard_count;
-  const uint32_t *pre = w.chist + (int64_t)row * SEL_BINS;
+  // self_hist: the scorer left no histogram (prefill-shaped scoring); it is
+  // built here from the staged scores
+  const uint32_t *pre = self_hist ? nullptr : w.chist + (int64_t)row * SEL_BINS;
   float *src = w.scores + (int64_t)row * w.np_cap;
   float *ls = row_scores ? row_scores + (int64_t)row * K : nullptr;
   int32_t *lpg = row_pages ? row_pages + (int64_t)row * K : nullptr;
@@ -191,12 +193,22 @@ coarse_topk_kernel(kiv_store st, kiv_query q, Workspace w, float *row_scores, in
   const bool staged = np > 0 && np <= scap && (reinterpret_cast<uintptr_t>(src) & 15) == 0;
   if (threadIdx.x == 0 && np > 0) {
     const uint32_t sb = staged ? (uint32_t)((np * 4 + 15) & ~15ll) : 0u;
-    mbar_arrive_tx(&bar, SEL_BINS * 4 + sb);
-    bulk_g2s(cs.hist, pre, SEL_BINS * 4, &bar);
-    if (sb) bulk_g2s(sscore, src, sb, &bar);
+    const uint32_t hb = pre ? SEL_BINS * 4 : 0u;
+    if (hb + sb) {
+      mbar_arrive_tx(&bar, hb + sb);
+      if (hb) bulk_g2s(cs.hist, pre, hb, &bar);
+      if (sb) bulk_g2s(sscore, src, sb, &bar);
+    }
   }
-  if (np > 0 && !mbar_wait_bounded(&bar, 0)) s_fail = 1;
+  if (!pre)
+    for (int i = threadIdx.x; i < SEL_BINS; i += TK_THREADS) cs.hist[i] = 0;
+  if (np > 0 && (pre || staged) && !mbar_wait_bounded(&bar, 0)) s_fail = 1;
   auto score_at = [&](int64_t i) { return staged ? sscore[i] : __ldcg(src + i); };
+  if (!pre && np > 0 && (int64_t)k < np) {
+    __syncthreads();
+    for (int64_t i = threadIdx.x; i < np; i += TK_THREADS) hist_add(cs.hist, f2key(score_at(i)) >> 21);
+    __syncthreads();
+  }
   if (np > 0 && (int64_t)k >= np) {
     for (int64_t i = threadIdx.x; i < np; i += TK_THREADS) emit_page(i, (uint32_t)i, f2key(score_at(i)));
   } else if (np > 0) {
@@ -236,7 +248,8 @@ coarse_topk_kernel(kiv_store st, kiv_query q, Workspace w, float *row_scores, in
   }
   // this row's first-pass histogram has been used: clear it for the next pass
   __syncthreads();
-  for (int i = threadIdx.x; i < SEL_BINS; i += TK_THREADS) w.chist[(int64_t)row * SEL_BINS + i] = 0;
+  if (pre)
+    for (int i = threadIdx.x; i < SEL_BINS; i += TK_THREADS) w.chist[(int64_t)row * SEL_BINS + i] = 0;
   if (row == 0 && threadIdx.x == 0) {
     if (nsh == 1) st.state[KIV_ST_UNION_PENDING] = 1;
     const unsigned long long mk = w.cstat[0], sb = w.cstat[1];
@@ -421,7 +434,16 @@ static kiv_status dispatch_cs(const kiv_store *st, const kiv_query *q, const Wor
 kiv_status launch_coarse(const kiv_store *st, const kiv_query *q, const Workspace &w,
                          float *row_scores, int32_t *row_pages, cudaStream_t s) {
   kiv_status rc;
-  if (fine_tc_eligible(st, q)) {
+  // prefill-shaped queries: tensor-core scoring, no per-row histograms (the
+  // workspace holds none for this shape)
+  const int self_hist = prefill_shape(st, q) ? 1 : 0;
+  if (self_hist && !prefill_tc_eligible(st, q)) {
+    set_error("prefill-shaped query needs a 16-byte aligned base and strides that are multiples of 8 elements");
+    return KIV_ERR_ARG;
+  }
+  if (self_hist) {
+    rc = launch_prefill_coarse_scores(st, q, w, s);
+  } else if (fine_tc_eligible(st, q)) {
     rc = launch_coarse_score_tc(st, q, w, s);
   } else switch (st->dtype) {
     case KIV_DTYPE_F32: rc = dispatch_cs<float>(st, q, w, s); break;
@@ -444,7 +466,7 @@ kiv_status launch_coarse(const kiv_store *st, const kiv_query *q, const Workspac
   const size_t smem = (size_t)cap * 9 + (size_t)fixed;
   cudaFuncSetAttribute(coarse_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   const cudaError_t e = launch_pdl(coarse_topk_kernel, dim3((unsigned)w.R), dim3(TK_THREADS), smem, s, 1, *st, *q,
-                                   w, row_scores, row_pages, cap, scap);
+                                   w, row_scores, row_pages, cap, scap, self_hist);
   if (e != cudaSuccess) return cuda_status(e, "coarse_topk");
   return cuda_status(cudaGetLastError(), "coarse");
 }

@@ -639,6 +639,7 @@ static kiv_status dispatch_fs(const kiv_store *st, const kiv_query *q, const Wor
 
 kiv_status launch_fine_score(const kiv_store *st, const kiv_query *q, const Workspace &w, cudaStream_t s) {
   if (fine_tc_eligible(st, q)) return launch_fine_score_tc(st, q, w, s);
+  if (prefill_tc_eligible(st, q)) return launch_prefill_fine_scores(st, q, w, s);
   KIV_CHECK(launch_union(st, w, s));
   switch (st->dtype) {
     case KIV_DTYPE_F32: return dispatch_fs<float>(st, q, w, s);

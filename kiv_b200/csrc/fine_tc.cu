@@ -349,6 +349,27 @@ static kiv_status encode_fn() {
   return KIV_OK;
 }
 
+kiv_status encode_tiled(CUtensorMap *map, int dtype, int rank, const void *base, const uint64_t *dims,
+                        const uint64_t *strides, const uint32_t *box, CUtensorMapSwizzle swizzle) {
+  KIV_CHECK(encode_fn());
+  cuuint64_t d[5], st[4];
+  cuuint32_t b[5], e[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    e[i] = 1;
+    if (i + 1 < rank) st[i] = strides[i];
+  }
+  const CUresult r = g_encode(map, dtype == KIV_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                              (cuuint32_t)rank, const_cast<void *>(base), d, st, b, e, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return KIV_ERR_CUDA;
+  }
+  return KIV_OK;
+}
+
 bool fine_tc_eligible(const kiv_store *st, const kiv_query *q) {
   const int rows_kv = (q->num_query_heads / st->num_kv_heads) * q->query_len;
   const int ncols = rows_kv <= 16 ? 16 : 32;

@@ -6,6 +6,7 @@
 #include <stdint.h>
 #include <stdlib.h>
 
+#include <algorithm>
 #include <utility>
 
 #include "../../include/kiv_b200.h"
@@ -63,6 +64,10 @@ kiv_status launch_fine_score(const kiv_store *st, const kiv_query *q, const Work
 kiv_status launch_union(const kiv_store *st, const Workspace &w, cudaStream_t s);
 bool fine_tc_eligible(const kiv_store *st, const kiv_query *q);
 kiv_status launch_fine_score_tc(const kiv_store *st, const kiv_query *q, const Workspace &w, cudaStream_t s);
+bool prefill_shape(const kiv_store *st, const kiv_query *q);        // prefill-shaped scoring applies
+bool prefill_tc_eligible(const kiv_store *st, const kiv_query *q);  // ... and the query suits TMA
+kiv_status launch_prefill_coarse_scores(const kiv_store *st, const kiv_query *q, const Workspace &w, cudaStream_t s);
+kiv_status launch_prefill_fine_scores(const kiv_store *st, const kiv_query *q, const Workspace &w, cudaStream_t s);
 kiv_status launch_coarse_score_tc(const kiv_store *st, const kiv_query *q, const Workspace &w, cudaStream_t s);
 kiv_status launch_fine_topk(const kiv_store *st, const kiv_query *q, const Workspace &w, int32_t *sel,
                             float *sel_scores, cudaStream_t s);
@@ -140,9 +145,14 @@ inline int64_t align_up(int64_t a, int64_t b) { return ceil_div(a, b) * b; }
 inline int elem_bytes(int dtype) { return dtype == KIV_DTYPE_F32 ? 4 : 2; }
 
 // number of attention splits per (b, kvh, row chunk) for this shape
+// attention splits per query row: at most one tile of keys per split, and no
+// more than the SMs spread over the CTAs of one split (prefill-shaped queries
+// use no splits at all, but the bound keeps their workspace small too)
 inline int64_t attn_split_cap(const kiv_store *st, const kiv_query *q) {
   const int64_t keys = (int64_t)q->top_p + st->hot_capacity;
-  return ceil_div(keys > 0 ? keys : 1, ATT_TILE);
+  const int64_t rows_kv = (int64_t)(q->num_query_heads / st->num_kv_heads) * q->query_len;
+  const int64_t base = (int64_t)st->batch * st->num_kv_heads * ceil_div(rows_kv, 16);
+  return std::min<int64_t>(ceil_div(keys > 0 ? keys : 1, ATT_TILE), ceil_div(sm_count(), std::max<int64_t>(1, base)));
 }
 
 }  // namespace kiv

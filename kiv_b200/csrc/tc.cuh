@@ -53,6 +53,20 @@ __device__ __forceinline__ uint64_t sdesc_k128(uint32_t smem_addr) {
   return d;
 }
 
+// The same for the 64-byte swizzled layout a SWIZZLE_64B TMA box of 32
+// 16-bit elements writes: rows 64 B apart, 8-row groups 512 B apart (SBO),
+// 16-byte chunks XOR-ed with (row / 2) % 4.  Base 512-byte aligned; advancing
+// K by 16 elements inside the 64-byte row adds 32 bytes.
+__device__ __forceinline__ uint64_t sdesc_k64(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr & 0x3FFFF) >> 4);        // start address, bits [0,14)
+  d |= (uint64_t)1 << 16;                              // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(512 >> 4) << 32;                     // stride byte offset: 8 rows x 64 B
+  d |= (uint64_t)1 << 46;                              // descriptor version (sm_100)
+  d |= (uint64_t)4 << 61;                              // layout: SWIZZLE_64B
+  return d;
+}
+
 // kind::f16 instruction descriptor: fp32 accumulate, A and B of the same
 // 16-bit type (bf16 when `bf16`, else fp16), both K-major, shape M x N.
 __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int M, int N) {
@@ -102,9 +116,24 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
       : "memory");
 }
+// 4-D tiled bulk load into this CTA (x innermost, same alignment rule)
+__device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, int32_t x, int32_t y, int32_t z,
+                                            int32_t w, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar))
+      : "memory");
+}
 __device__ __forceinline__ void prefetch_map(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
 }  // namespace tc
+
+// host: encode a tiled tensor map (rank 2-5) of a 16-bit store dtype; strides
+// in bytes for dimensions 1..rank-1; no interleave, zero fill out of bounds
+kiv_status encode_tiled(CUtensorMap *map, int dtype, int rank, const void *base, const uint64_t *dims,
+                        const uint64_t *strides, const uint32_t *box, CUtensorMapSwizzle swizzle);
+
 }  // namespace kiv
