@@ -61,7 +61,16 @@ WORKLOADS = {
     # c3 (Llama-3-8B shape, 64 sequences x 262,144 cold + 4096 hot) one layer: the full
     # model's cold tier (2.2 TB) does not fit one GPU; one layer holds 69 GB
     "c3l": dict(layers=1, hq=32, hkv=8, d=128, cold=262144, hot=4096, top_pages=32, top_p=512, batch=64),
+    # c4 (Phi-3.5 MHA chunked prefill, retrieval on every 4096-token chunk) at sampled cold lengths
+    "c4": dict(kind="prefill", layers=1, hq=32, hkv=32, d=96, cold=1048576, hot=2048, chunk=4096,
+               top_pages=32, top_p=256, segment=2048),
+    "c4m": dict(kind="prefill", layers=1, hq=32, hkv=32, d=96, cold=262144, hot=2048, chunk=4096,
+                top_pages=32, top_p=256, segment=2048),
+    "c4s": dict(kind="prefill", layers=1, hq=32, hkv=32, d=96, cold=65536, hot=2048, chunk=4096,
+                top_pages=32, top_p=256, segment=2048),
 }
+PREFILL_METRIC = "chunked-prefill tokens/s per layer with retrieval on every chunk (Phi-3.5 MHA, bf16)"
+PREFILL_UNIT = "tokens/s"
 PAGE = 128
 SEGMENT = 512
 INPUT_POOL = 256     # distinct per-step inputs, cycled
@@ -330,6 +339,8 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if w.get("kind") == "prefill":
+        return run_prefill(args, w, rank, world)
     if args.impl == "reference":
         return run_reference(args, w, rank, world)
 
@@ -523,6 +534,297 @@ def main():
             "sample": f"1 of {L} layers at full size, {n} layer-steps in {el:.1f} s "
                       f"(numpy oracle port, fp32 math on bf16 values, {cpu_model()})"}
     if rank == 0:
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+# ------------------------------------------------------ chunked prefill (c4)
+def prefill_flops(w, C, np_pages, hot0):
+    """Tensor FLOPs of one chunk-step: coarse scores, fine scores, attention.
+
+    The attention of query position i covers the P selected cold rows and the
+    hot rows up to i (hot0 rows before the chunk plus i + 1 of its own)."""
+    hq, d, q, p = w["hq"], w["d"], w["chunk"], w["top_p"]
+    coarse = 2.0 * hq * q * np_pages * d
+    fine = 2.0 * hq * q * C * d
+    keys = q * (p + hot0) + q * (q + 1) / 2.0
+    attn = 4.0 * hq * keys * d
+    return coarse, fine, attn
+
+
+def prefill_inputs(w, dev, n, seed=11):
+    """n chunks: queries N(0,1), keys topic centroid + N(0, 0.3^2) (topic switch
+    every `segment` tokens), values N(0,1); [n, 1, H, chunk, D] bf16."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    Q, d = w["chunk"], w["d"]
+    q = torch.randn(n, 1, w["hq"], Q, d, generator=g, device=dev).to(torch.bfloat16)
+    nseg = (Q + w["segment"] - 1) // w["segment"]
+    cent = torch.randn(n, 1, w["hkv"], nseg, d, generator=g, device=dev) / math.sqrt(64.0)
+    seg = torch.arange(Q, device=dev) // w["segment"]
+    k = (cent[:, :, :, seg] + 0.3 * torch.randn(n, 1, w["hkv"], Q, d, generator=g, device=dev)).to(torch.bfloat16)
+    v = torch.randn(n, 1, w["hkv"], Q, d, generator=g, device=dev).to(torch.bfloat16)
+    return q, k, v
+
+
+def prefill_cpu_sample(w, seconds=15.0):
+    """The oracle port on a bounded sample of the chunk-step: the c4 head shape
+    with a 256-position chunk over 16,384 cold + 2048 hot tokens (the port
+    materializes every score, [Hq, Q, C] floats).  Returns the sample's
+    chunk-step time, its FLOPs and the threads used."""
+    from kiv_b200.synthetic import SynthSpec, make_problem
+    from oracle.kiv_oracle import OracleLayer, OracleStore, causal_hot_mask, decode_step
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    q_len, cold = 256, 16384
+    spec = SynthSpec(batch=1, num_query_heads=w["hq"], num_kv_heads=w["hkv"], head_dim=w["d"], cold_tokens=cold,
+                     hot_budget=w["hot"], page_size=PAGE, query_len=q_len, segment=w["segment"], needle=False)
+    prob = make_problem(spec, seed=0, dtype=torch.bfloat16)
+    store = OracleStore(1, w["hkv"], w["d"], spec.groups, PAGE, "bf16", compute=np.float32)
+    layer = OracleLayer(store, w["hot"])
+    layer.update(prob.prefill_k.float().numpy(), prob.prefill_v.float().numpy())
+    layer.mark_prefill_complete()
+    layer.prefill_complete = False          # a chunk is appended without eviction
+    q = prob.query.float().numpy()
+    k, v = prob.step_k.float().numpy(), prob.step_v.float().numpy()
+    scaling = w["d"] ** -0.5
+    n, t0 = 0, time.perf_counter()
+    while True:
+        hot0 = layer.hot_k.shape[2]
+        mask = causal_hot_mask(1, q_len, hot0 + q_len)
+        decode_step(layer, q, k, v, scaling, w["top_pages"], w["top_p"], hot_mask=mask)
+        layer.hot_k, layer.hot_v = layer.hot_k[:, :, :hot0], layer.hot_v[:, :, :hot0]
+        n += 1
+        if time.perf_counter() - t0 >= seconds and n >= 2:
+            break
+    el = (time.perf_counter() - t0) / n
+    wq = dict(w, chunk=q_len)
+    flops = sum(prefill_flops(wq, cold, cold // PAGE, w["hot"]))
+    return el, flops, os.cpu_count() or 1, f"{n} chunk-steps of {q_len} positions over {cold} cold tokens"
+
+
+def run_prefill(args, w, rank, world):
+    """Chunked-prefill retrieval, one layer: each step appends a chunk of
+    `chunk` positions to the hot window (no eviction inside the chunk), runs the
+    retrieval attention of all its positions (coarse + fine selection over the
+    cold tier, attention over [selected cold ; hot] with the causal rule), then
+    moves the hot overflow to the cold tier -- the reference server's chunked
+    reuse prefill (kiv/server/generation.py:123-180) on one layer.  With N GPUs
+    every rank runs its own replica (independent sequences)."""
+    import torch.distributed as dist
+    from transformers import PretrainedConfig
+
+    from kiv_b200 import KIVConfig, ModelTopology, TieredKVCache
+    from kiv_b200 import _native as nat
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    Q, d = w["chunk"], w["d"]
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        el, flops, threads, what = prefill_cpu_sample(w, seconds=min(60.0, 5.0 * max(1, args.steps)))
+        c_full = w["cold"]
+        full = sum(prefill_flops(w, c_full, c_full // PAGE, w["hot"]))
+        rate = Q / (el * full / flops)
+        print(json.dumps({
+            "metric": PREFILL_METRIC, "value": rate, "unit": PREFILL_UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000.0 * Q / rate, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "impl": "reference",
+            "config": {"workload": f"{args.workload}: chunk {Q}, Hq=Hkv={w['hq']}, D={d}, {w['cold']} cold + "
+                                   f"{w['hot']} hot", "parallelism": "cpu"},
+            "cpu_baseline": {"value": rate, "unit": PREFILL_UNIT, "cores": threads, "kind": "port",
+                             "sample": what + "; time scaled to the full chunk-step by its tensor FLOPs"},
+            "e2e": {"value": rate, "unit": PREFILL_UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+            flush=True)
+        return 0
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    K, W = args.steps, max(3, args.warmup)
+    R = max(1, args.roofline_steps)
+    n_total = W + 2 * K + R + 2
+    kcfg = KIVConfig(hot_budget=w["hot"], top_p=w["top_p"], page_size=PAGE, top_pages=w["top_pages"],
+                     cold_capacity=w["cold"] + n_total * Q + w["hot"] + 4 * PAGE, hot_slack=Q + PAGE,
+                     telemetry=False)
+    topo = ModelTopology.manual(global_layer_indices=(0,), num_query_heads=w["hq"], num_kv_heads=w["hkv"],
+                                head_dim=d, num_hidden_layers=1)
+    cache = TieredKVCache(PretrainedConfig(num_hidden_layers=1), kcfg, topo, dev)
+    t_build = time.perf_counter()
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1000 + rank)
+    T = w["cold"] + w["hot"]
+    nseg = (T + w["segment"] - 1) // w["segment"] + 1
+    cent = torch.randn(1, w["hkv"], nseg, d, generator=gen, device=dev) / math.sqrt(64.0)
+    for a in range(0, T, 65536):
+        n = min(65536, T - a)
+        seg = torch.arange(a, a + n, device=dev) // w["segment"]
+        k = cent[:, :, seg] + 0.3 * torch.randn(1, w["hkv"], n, d, generator=gen, device=dev)
+        v = torch.randn(1, w["hkv"], n, d, generator=gen, device=dev)
+        cache.update(k.to(torch.bfloat16), v.to(torch.bfloat16), 0)
+        cache._evict_to_cap(w["hot"])
+    del k, v, cent
+    cache._prefill_complete = True
+    cache._evict_excess_all_layers()
+    torch.cuda.synchronize(dev)
+    t_build = time.perf_counter() - t_build
+    store = cache.get_cold_store(0)
+    NP = 4
+    qp, kp, vp = prefill_inputs(w, dev, NP, seed=11 + rank)
+    scaling = d ** -0.5
+
+    def step(i, out=None):
+        cache._prefill_complete = False
+        cache.update(kp[i], vp[i], 0)
+        o = store.attend(qp[i], scaling, kcfg, causal=True, out=out)
+        cache._prefill_complete = True
+        cache._evict_excess_all_layers()
+        return o
+
+    out = torch.empty(1, Q, w["hq"], d, dtype=torch.bfloat16, device=dev)
+    for s in range(W):
+        step(s % NP, out)
+    torch.cuda.synchronize(dev)
+
+    # ---- stage timing pass: events at the store's stage marks
+    rec = StageRecorder()
+    stage_ms, fine_flops, fine_ms, cs, nps = {}, 0.0, 0.0, [], []
+    for s in range(R):
+        i = (W + s) % NP
+        store._profile = rec
+        rec.marks.clear()
+        torch.cuda._sleep(2_000_000)
+        rec.record("update_begin")
+        hot0 = store.hot_length
+        step(i, out)
+        rec.record("step_end")
+        store._profile = None
+        torch.cuda.synchronize(dev)
+        words = store.read_state()
+        U = words[nat.ST_UNION]
+        # the step's retrieval saw the cold tier before this step's overflow moved in
+        cold_seen = store.cold_length - Q
+        C = U * PAGE + cold_seen % PAGE
+        m = dict(rec.marks)
+        t_f = m["fine_score_begin"].elapsed_time(m["fine_score_end"])
+        fine_ms += t_f
+        fine_flops += prefill_flops(w, C, cold_seen // PAGE, hot0)[1]
+        cs.append(C)
+        nps.append(cold_seen // PAGE)
+        for a, b, name in (("update_begin", "coarse_begin", "update"),
+                           ("coarse_begin", "fine_score_begin", "coarse"),
+                           ("fine_score_begin", "fine_score_end", "fine_score"),
+                           ("fine_score_end", "fine_topk_end", "fine_topk"),
+                           ("fine_topk_end", "attend_end", "attend"),
+                           ("attend_end", "step_end", "evict")):
+            if a in m and b in m:
+                stage_ms[name] = stage_ms.get(name, 0.0) + m[a].elapsed_time(m[b])
+    peak_t = None
+    pj = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(pj):
+        with open(pj) as f:
+            peak_t, peak_kind = float(json.load(f)["bf16_tflops_sustained"]), "measured (sustained)"
+    if peak_t is None:
+        peak_t, peak_kind = 1400.0, "fallback (sustained)"
+    achieved_t = fine_flops / (fine_ms * 1e-3) / 1e12
+
+    # ---- timed region: K chunk-steps, device inputs
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    sampler = ClockSampler(smi_id(dev))
+    barrier()
+    torch.cuda.synchronize(dev)
+    sampler.start()
+    time.sleep(0.3)
+    cold_before = store.cold_length
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for s in range(K):
+        step((W + R + s) % NP, out)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    value = world * K * Q / (ms * 1e-3)
+    cold_mean = cold_before + Q * (K - 1) / 2.0
+
+    # ---- e2e: chunk inputs from pinned host memory, output read back
+    hq_, hk_, hv_ = (x.cpu().pin_memory() for x in (qp, kp, vp))
+    sq, sk, sv = torch.empty_like(qp[0]), torch.empty_like(kp[0]), torch.empty_like(vp[0])
+    hout = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    barrier()
+    torch.cuda.synchronize(dev)
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record()
+    for s in range(K):
+        i = s % NP
+        sq.copy_(hq_[i], non_blocking=True)
+        sk.copy_(hk_[i], non_blocking=True)
+        sv.copy_(hv_[i], non_blocking=True)
+        cache._prefill_complete = False
+        cache.update(sk, sv, 0)
+        store.attend(sq, scaling, kcfg, causal=True, out=out)
+        cache._prefill_complete = True
+        cache._evict_excess_all_layers()
+        hout.copy_(out, non_blocking=True)
+    e3.record()
+    torch.cuda.synchronize(dev)
+    barrier()
+    ms_e2e = max_over_ranks(e2.elapsed_time(e3))
+    assert torch.isfinite(hout.float()).all(), "non-finite attention output"
+    assert store.read_state()[nat.ST_ERROR] == 0, "kernel error bits set"
+
+    if rank == 0:
+        C_mean = float(np.mean(cs))
+        co, fi, at = prefill_flops(w, C_mean, float(np.mean(nps)), w["hot"])
+        result = {
+            "metric": PREFILL_METRIC, "value": value, "unit": PREFILL_UNIT, "n_gpus": world, "steps": K,
+            "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"{args.workload}: one Phi-3.5-shape layer (Hq=Hkv={w['hq']}, D={d}), chunks of "
+                                   f"{Q} positions over ~{int(cold_mean)} cold + {w['hot']} hot tokens, "
+                                   f"top_pages={w['top_pages']}, top_p={w['top_p']}, page={PAGE}",
+                       "parallelism": f"{world} independent replica(s)" if world > 1 else "1 GPU",
+                       "l2": f"inputs larger than L2 (each chunk-step reads the ~{int(cold_mean * 2 * 32 * 96 * 2 / 1e9)} GB "
+                             "cold tier's candidate keys)",
+                       "timing": "eager public API per chunk-step, CUDA events, max over ranks"},
+            "gpu_launches": int(K * 10),
+            "e2e": {"value": world * K * Q / (ms_e2e * 1e-3), "unit": PREFILL_UNIT,
+                    "h2d_bytes_per_step": (sq.numel() + sk.numel() + sv.numel()) * 2,
+                    "d2h_bytes_per_step": out.numel() * 2,
+                    "api": "TieredKVCache.update + ColdKVStore.attend(causal=True) with pinned host chunks"},
+            "roofline": {"bound": "tensor", "kernel": "prefill_scores_kernel<bf16, fine> (tcgen05 fine scoring)",
+                         "achieved": achieved_t, "peak": peak_t, "unit": "TFLOP/s", "frac": achieved_t / peak_t,
+                         "peak_kind": peak_kind, "traffic": None,
+                         "flops_per_launch": fine_flops / R, "avg_launch_us": fine_ms * 1e3 / R,
+                         "launches_timed": R, "mean_candidates": C_mean,
+                         "note": "time = the fine-scoring stage (union, key reset, tcgen05 scoring, histogram)"},
+            "step_tensor_flops": {"coarse": co, "fine": fi, "attention": at,
+                                  "achieved_TFLOPs": (co + fi + at) / (ms / K * 1e-3) / 1e12},
+            "stages_us_per_step": {k2: v2 * 1e3 / R for k2, v2 in stage_ms.items()},
+            "clocks": clocks,
+            "build_s": t_build,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            el, flops, threads, what = prefill_cpu_sample(w)
+            full = co + fi + at
+            result["cpu_baseline"] = {
+                "value": Q / (el * full / flops), "unit": PREFILL_UNIT, "cores": threads, "kind": "port",
+                "sample": f"{what} (numpy oracle port, fp32 math on bf16 values, {cpu_model()}); time scaled to "
+                          f"the full chunk-step by its tensor FLOPs"}
         print(json.dumps(result), flush=True)
     if world > 1:
         dist.destroy_process_group()

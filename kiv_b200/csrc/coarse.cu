@@ -262,6 +262,205 @@ coarse_topk_kernel(kiv_store st, kiv_query q, Workspace w, float *row_scores, in
     atomicOr(reinterpret_cast<unsigned long long *>(st.state + KIV_ST_ERROR), (unsigned long long)KIV_ERRBIT_WAIT_TIMEOUT);
 }
 
+// Per-row top-k for prefill-shaped coarse scoring (thousands of query rows of
+// a few thousand pages each): one warp per row, persistent CTAs.  Exact, with
+// the same order as coarse_topk_kernel (score descending, lowest page first on
+// ties): a radix select over the order-preserving keys finds the boundary --
+// levels of 11, 11 and 10 bits, each a histogram in the warp's shared memory
+// over the keys that match the levels so far, stopping once the boundary bin
+// holds at most RT_CAND keys -- then one pass marks every key above the
+// boundary and compacts the boundary keys (index order), which are ranked by
+// comparison (or, when all of them are equal, taken lowest page first).
+// Union marks collect in a CTA bitmap and reach w.pbits once per CTA.
+constexpr int RT_THREADS = 256;
+constexpr int RT_WARPS = RT_THREADS / 32;
+constexpr int RT_CAND = 256;          // boundary keys resolved by ranking; also the largest top_pages
+constexpr int RT_UNROLL = 16;         // independent loads in flight per lane
+
+__global__ void __launch_bounds__(RT_THREADS)
+coarse_rows_topk_kernel(kiv_store st, kiv_query q, Workspace w, float *row_scores, int32_t *row_pages,
+                        int nwords) {
+  extern __shared__ uint32_t rt_smem[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t *hist = rt_smem + warp * SEL_BINS;
+  uint32_t *ckey = rt_smem + RT_WARPS * SEL_BINS + warp * RT_CAND;
+  int32_t *cidx = reinterpret_cast<int32_t *>(rt_smem + RT_WARPS * (SEL_BINS + RT_CAND)) + warp * RT_CAND;
+  uint8_t *cflag = reinterpret_cast<uint8_t *>(rt_smem + RT_WARPS * (SEL_BINS + 2 * RT_CAND)) + warp * RT_CAND;
+  uint32_t *bits = rt_smem + RT_WARPS * (SEL_BINS + 2 * RT_CAND) + RT_WARPS * RT_CAND / 4;   // [nwords]
+  for (int i = threadIdx.x; i < nwords; i += RT_THREADS) bits[i] = 0;
+  const int S = st.page_size;
+  const int nsh = st.shard_count, rank = st.shard_rank;
+  griddep_wait();
+  const int64_t np_global = st_ld(st.state, KIV_ST_COLD_LEN) / S;
+  const int64_t np = local_pages(np_global, rank, nsh);
+  const int K = q.top_pages;
+  const uint32_t k = (uint32_t)(K < np ? (int64_t)K : np);
+  const unsigned lt = (1u << lane) - 1u;
+  __syncthreads();
+  auto mark = [&](int64_t i) {
+    if (nwords > 0) atomicOr(&bits[i >> 5], 1u << (i & 31));
+    else atomicOr(&w.pbits[i >> 5], 1u << (i & 31));
+  };
+  for (int64_t row = (int64_t)blockIdx.x * RT_WARPS + warp; row < w.R; row += (int64_t)gridDim.x * RT_WARPS) {
+    const float *src = w.scores + row * w.np_cap;
+    float *ls = row_scores ? row_scores + row * K : nullptr;
+    int32_t *lpg = row_pages ? row_pages + row * K : nullptr;
+    uint32_t prefix = 0, mask = 0, remaining = k;
+    bool all = (int64_t)k >= np;
+    if (!all) {
+#pragma unroll 1
+      for (int level = 0; level < 3; ++level) {
+        const int sh = level == 0 ? 21 : (level == 1 ? 10 : 0);
+        const int nbins = level == 2 ? 1024 : 2048;
+        for (int i = lane; i < nbins; i += 32) hist[i] = 0;
+        __syncwarp();
+        for (int64_t base = 0; base < np; base += 32 * RT_UNROLL) {
+          float v[RT_UNROLL];
+#pragma unroll
+          for (int x = 0; x < RT_UNROLL; ++x) {
+            const int64_t i = base + x * 32 + lane;
+            v[x] = i < np ? __ldcg(src + i) : 0.f;
+          }
+#pragma unroll
+          for (int x = 0; x < RT_UNROLL; ++x) {
+            const uint32_t key = f2key(v[x]);
+            if (base + x * 32 + lane < np && (key & mask) == prefix) atomicAdd(&hist[(key >> sh) & (nbins - 1)], 1u);
+          }
+        }
+        __syncwarp();
+        // boundary bin: lane l owns bins [hi - per + 1, hi], lane 0 the highest
+        const int per = nbins / 32;
+        const int hi = nbins - 1 - lane * per;
+        uint32_t tot = 0;
+        for (int x = 0; x < per; ++x) tot += hist[hi - x];
+        uint32_t incl = tot;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const uint32_t y = __shfl_up_sync(KIV_FULL_MASK, incl, o);
+          if (lane >= o) incl += y;
+        }
+        const uint32_t excl = incl - tot;
+        const unsigned own = __ballot_sync(KIV_FULL_MASK, excl < remaining && incl >= remaining);
+        const int sl = own ? __ffs(own) - 1 : 0;
+        int bin = 0;
+        uint32_t above = 0, cnt = 0;
+        if (lane == sl) {
+          uint32_t acc = excl;
+          for (int x = 0; x < per; ++x) {
+            const uint32_t h = hist[hi - x];
+            if (acc + h >= remaining) {
+              bin = hi - x;
+              above = acc;
+              cnt = h;
+              break;
+            }
+            acc += h;
+          }
+        }
+        bin = __shfl_sync(KIV_FULL_MASK, bin, sl);
+        above = __shfl_sync(KIV_FULL_MASK, above, sl);
+        cnt = __shfl_sync(KIV_FULL_MASK, cnt, sl);
+        __syncwarp();
+        remaining -= above;
+        prefix |= (uint32_t)bin << sh;
+        mask |= (uint32_t)(nbins - 1) << sh;
+        if (cnt <= RT_CAND) break;
+      }
+    }
+    // keys above the boundary are selected; the boundary keys ((key & mask) ==
+    // prefix) are compacted in index order
+    int nb = 0;
+    for (int64_t base = 0; base < np; base += 32 * RT_UNROLL) {
+      float v[RT_UNROLL];
+#pragma unroll
+      for (int x = 0; x < RT_UNROLL; ++x) {
+        const int64_t i = base + x * 32 + lane;
+        v[x] = i < np ? __ldcg(src + i) : 0.f;
+      }
+#pragma unroll
+      for (int x = 0; x < RT_UNROLL; ++x) {
+        const int64_t i = base + x * 32 + lane;
+        const uint32_t key = f2key(v[x]);
+        const bool in = i < np;
+        const bool up = in && (all || (key & mask) > prefix);
+        const bool bnd = in && !all && (key & mask) == prefix;
+        if (up && nsh == 1) mark(i);
+        const unsigned bb = __ballot_sync(KIV_FULL_MASK, bnd);
+        if (bnd) {
+          const int pos = nb + __popc(bb & lt);
+          if (pos < RT_CAND) {
+            ckey[pos] = key;
+            cidx[pos] = (int32_t)i;
+          }
+        }
+        nb += __popc(bb);
+      }
+    }
+    __syncwarp();
+    // boundary: `remaining` of the nb keys, score descending then lowest page
+    const int nbc = nb < RT_CAND ? nb : RT_CAND;
+    for (int j = lane; j < nbc; j += 32) {
+      bool take;
+      if (mask == 0xFFFFFFFFu) {
+        take = (uint32_t)j < remaining;             // all equal: index order
+      } else {
+        const uint32_t kj = ckey[j];
+        uint32_t r = 0;
+        for (int x = 0; x < nbc; ++x) {
+          const uint32_t kx = ckey[x];
+          r += (kx > kj) || (kx == kj && x < j);
+        }
+        take = r < remaining;
+      }
+      cflag[j] = take ? 1 : 0;
+      if (take && nsh == 1) mark(cidx[j]);
+    }
+    __syncwarp();
+    if (nsh > 1) {
+      // this rank's list of the row, (score, global page) in page order
+      int pos = 0, bi = 0;
+      for (int64_t base = 0; base < np; base += 32) {
+        const int64_t i = base + lane;
+        const bool in = i < np;
+        const float sc = in ? __ldcg(src + i) : 0.f;
+        const uint32_t key = f2key(sc);
+        const bool up = in && (all || (key & mask) > prefix);
+        const bool bnd = in && !all && (key & mask) == prefix;
+        const unsigned bb = __ballot_sync(KIV_FULL_MASK, bnd);
+        const int bpos = bi + __popc(bb & lt);
+        const bool sel = up || (bnd && bpos < RT_CAND && cflag[bpos]);
+        const unsigned sb = __ballot_sync(KIV_FULL_MASK, sel);
+        if (sel) {
+          const int p = pos + __popc(sb & lt);
+          if (p < K) {
+            ls[p] = sc;
+            lpg[p] = (int32_t)(i * nsh + rank);
+          }
+        }
+        pos += __popc(sb);
+        bi += __popc(bb);
+      }
+      for (int j = (int)k + lane; j < K; j += 32) {
+        ls[j] = 0.f;
+        lpg[j] = -1;
+      }
+    }
+    __syncwarp();
+  }
+  __syncthreads();
+  if (nwords > 0)
+    for (int i = threadIdx.x; i < nwords; i += RT_THREADS)
+      if (bits[i]) atomicOr(&w.pbits[i], bits[i]);
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    if (nsh == 1) st.state[KIV_ST_UNION_PENDING] = 1;
+    const unsigned long long mk = w.cstat[0], sb = w.cstat[1];
+    if (mk) atomicMax(reinterpret_cast<unsigned long long *>(st.state + KIV_ST_COARSE_MAX), mk);
+    atomicAdd(reinterpret_cast<double *>(st.state + KIV_ST_COARSE_SUM), __longlong_as_double((long long)sb));
+    w.cstat[0] = 0;
+    w.cstat[1] = 0;
+  }
+}
+
 // Sorted page union from the marks the coarse pass set (single CTA): used
 // ahead of the scorers that do not build it themselves.  Clears the marks and
 // the pending word; a no-op when no coarse pass is pending (reused union).
@@ -455,6 +654,18 @@ kiv_status launch_coarse(const kiv_store *st, const kiv_query *q, const Workspac
   if (q->top_pages > 8192) {
     set_error("coarse: top_pages %d exceeds the shared-memory select (max 8192)", q->top_pages);
     return KIV_ERR_CAPACITY;
+  }
+  if (self_hist && q->top_pages <= RT_CAND) {
+    // prefill-shaped rows: one warp per row
+    const int64_t words = ceil_div(w.np_cap, 32);
+    const int nwords = words <= 4096 ? (int)words : 0;
+    const size_t smem = 4 * (size_t)RT_WARPS * (SEL_BINS + 2 * RT_CAND) + (size_t)RT_WARPS * RT_CAND +
+                        4 * (size_t)nwords;
+    const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(ceil_div(w.R, RT_WARPS), 2 * (int64_t)sm_count()));
+    cudaFuncSetAttribute(coarse_rows_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    return cuda_status(launch_pdl(coarse_rows_topk_kernel, dim3((unsigned)grid), dim3(RT_THREADS), smem, s, 1, *st,
+                                  *q, w, row_scores, row_pages, nwords),
+                       "coarse_rows_topk");
   }
   // candidate buffer (key + index + flag per page), the boundary scratch, the
   // chosen list and the staged scores of the row

@@ -35,7 +35,8 @@
 
 namespace kiv {
 
-constexpr int PF_THREADS = 192;       // warps 0-3 epilogue, 4 TMA producer, 5 MMA issuer
+constexpr int PF_EPI = 8;             // epilogue warps: two per TMEM lane quadrant (column halves)
+constexpr int PF_THREADS = 32 * (PF_EPI + 2);   // + warp 8 TMA producer, warp 9 MMA issuer
 constexpr int PF_TILE = 128;          // tile rows (MMA M): tokens of a page, or page summaries
 constexpr int PF_BOX = 32;            // elements per TMA box along D (64 bytes, SWIZZLE_64B)
 constexpr int PF_MAX_STAGES = 6;
@@ -60,8 +61,9 @@ prefill_scores_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
   __shared__ uint64_t full[PF_MAX_STAGES], empty[PF_MAX_STAGES], acc_full[2], acc_empty[2], q_full, q_empty;
   __shared__ uint32_t s_tmem;
   __shared__ int s_fail;
-  __shared__ uint32_t s_wmax[4];
-  __shared__ float s_wsum[4];
+  __shared__ uint32_t s_wmax[PF_EPI];
+  __shared__ float s_wsum[PF_EPI];
+  __shared__ float s_half[2][PF_TILE];   // column-half maxima of the tile rows (two tiles in flight)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int D = st.head_dim, H = st.num_kv_heads, S = st.page_size;
   const int Hq = q.num_query_heads, Q = q.query_len, G = Hq / H;
@@ -88,7 +90,7 @@ prefill_scores_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 4);
+      mbar_init(&acc_empty[a], PF_EPI);
     }
     mbar_init(&q_full, 1);
     mbar_init(&q_empty, 1);
@@ -99,7 +101,7 @@ prefill_scores_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
     tc::tmem_alloc(&s_tmem, tcols);
     tc::tmem_relinquish();
   }
-  if (threadIdx.x == 32 * 4) {
+  if (threadIdx.x == 32 * PF_EPI) {
     tc::prefetch_map(&kmap);
     tc::prefetch_map(&qmap);
   }
@@ -131,7 +133,7 @@ prefill_scores_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
   const int64_t BH = (int64_t)st.batch * H;
 
   bool ok = true;
-  if (warp == 4) {
+  if (warp == PF_EPI) {
     if (lane == 0 && my_units > 0) {
       // ------------------------------------------------ TMA producer
       int64_t t = 0;
@@ -167,7 +169,7 @@ prefill_scores_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
       }
       if (!ok) s_fail = 1;
     }
-  } else if (warp == 5) {
+  } else if (warp == PF_EPI + 1) {
     if (lane == 0 && my_units > 0) {
       // ------------------------------------------------ MMA issuer
       const uint32_t idesc = tc::idesc_f16(BF16, PF_TILE, g.nt);
@@ -200,37 +202,45 @@ prefill_scores_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
       if (!ok) s_fail = 1;
     }
   } else {
-    // -------------------------------------------------- epilogue, warps 0-3
-    const int row = warp * 32 + lane;   // tile row: token of the page (fine), page of the block (coarse)
+    // ------------------------------------------ epilogue, warps 0..PF_EPI-1
+    // warp e reads TMEM lanes 32 * (e % 4) .. (its tile rows) and the 16-column
+    // chunks e / 4, e / 4 + 2, ... of every accumulator
+    const int quad = warp & 3, half = warp >> 2;
+    const int row = quad * 32 + lane;   // tile row: token of the page (fine), page of the block (coarse)
     uint32_t kmax = 0;
     float ksum = 0.f;
-    int64_t c = 0;
-    for (int64_t bh = 0; bh < BH && ok; ++bh) {
+    int64_t c = 0, tile = 0;
+    // A failed wait (a bug upstream) turns `ok` off: the loops still run to the
+    // end, without waiting, so the two warps of a quadrant meet at every barrier.
+    for (int64_t bh = 0; bh < BH; ++bh) {
       const int b = (int)(bh / H), kvh = (int)(bh % H);
-      for (int64_t k = 0; k < my_units && ok; ++k) {
+      for (int64_t k = 0; k < my_units; ++k, ++tile) {
         const int64_t u = j + k * g.nj;
-        float m = -INFINITY;
+        // independent partial maxima: the fmax chain is not one long dependency
+        float m[8];
+#pragma unroll
+        for (int x = 0; x < 8; ++x) m[x] = -INFINITY;
         for (int i = 0; i < nb; ++i, ++c) {
           const int a = (int)(c & 1);
-          if (!mbar_wait_bounded(&acc_full[a], (uint32_t)((c >> 1) & 1))) { ok = false; break; }
+          if (ok && !mbar_wait_bounded(&acc_full[a], (uint32_t)((c >> 1) & 1))) ok = false;
+          if (!ok) continue;
           tc::fence_after_sync();
           const int rbi = rb0 + i, gi = rbi / g.tblocks, t0 = (rbi % g.tblocks) * g.nt;
           const int valid = min(g.nt, Q - t0);
-          const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(a * g.nt);
+          const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(a * g.nt);
           if (COARSE) {
             const int64_t p = u * PF_TILE + row;
             const bool live = p < np_local;
             float *dst = w.scores + (((int64_t)b * Hq + kvh * G + gi) * Q + t0) * w.np_cap + p;
-            for (int c0 = 0; c0 < g.nt; c0 += 32) {
-              uint32_t r0[16], r1[16];
-              tc::ld_32x16(taddr + c0, r0);
-              tc::ld_32x16(taddr + c0 + 16, r1);
+            for (int c0 = 16 * half; c0 < g.nt; c0 += 32) {
+              uint32_t r[16];
+              tc::ld_32x16(taddr + c0, r);
               tc::wait_ld();
               if (live) {
 #pragma unroll
-                for (int cc = 0; cc < 32; ++cc) {
+                for (int cc = 0; cc < 16; ++cc) {
                   if (c0 + cc < valid) {
-                    const float sc = __uint_as_float(cc < 16 ? r0[cc] : r1[cc - 16]) * q.scaling;
+                    const float sc = __uint_as_float(r[cc]) * q.scaling;
                     dst[(int64_t)(c0 + cc) * w.np_cap] = sc;
                     const uint32_t key = f2key(sc);
                     kmax = key > kmax ? key : kmax;
@@ -239,25 +249,44 @@ prefill_scores_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
                 }
               }
             }
-          } else {
-            for (int c0 = 0; c0 < g.nt; c0 += 32) {
+          } else if (valid == g.nt) {
+            for (int c0 = 16 * half; c0 < g.nt; c0 += 64) {
               uint32_t r0[16], r1[16];
               tc::ld_32x16(taddr + c0, r0);
-              tc::ld_32x16(taddr + c0 + 16, r1);
+              if (c0 + 32 < g.nt) tc::ld_32x16(taddr + c0 + 32, r1);
               tc::wait_ld();
 #pragma unroll
-              for (int cc = 0; cc < 32; ++cc)
-                if (c0 + cc < valid) m = fmaxf(m, __uint_as_float(cc < 16 ? r0[cc] : r1[cc - 16]));
+              for (int cc = 0; cc < 16; ++cc) m[cc & 7] = fmaxf(m[cc & 7], __uint_as_float(r0[cc]));
+              if (c0 + 32 < g.nt) {
+#pragma unroll
+                for (int cc = 0; cc < 16; ++cc) m[cc & 7] = fmaxf(m[cc & 7], __uint_as_float(r1[cc]));
+              }
+            }
+          } else {
+            for (int c0 = 16 * half; c0 < g.nt; c0 += 32) {
+              uint32_t r[16];
+              tc::ld_32x16(taddr + c0, r);
+              tc::wait_ld();
+#pragma unroll
+              for (int cc = 0; cc < 16; ++cc)
+                if (c0 + cc < valid) m[cc & 7] = fmaxf(m[cc & 7], __uint_as_float(r[cc]));
             }
           }
           tc::fence_before_sync();
           __syncwarp();
           if (lane == 0) mbar_arrive(&acc_empty[a]);
         }
-        if (!COARSE && ok) {
-          // scaling > 0: the max of the scaled scores is the scaled max
-          const int n_tok = u < U ? PF_TILE : (int)partial;
-          if (row < n_tok) atomicMax(&w.agg[(int64_t)b * w.c_cap + u * S + row], f2key(m * q.scaling));
+        if (!COARSE) {
+          float mx = fmaxf(fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3])), fmaxf(fmaxf(m[4], m[5]), fmaxf(m[6], m[7])));
+          // the two column halves of a row meet in shared memory (named barrier per quadrant)
+          if (half == 1) s_half[tile & 1][row] = mx;
+          asm volatile("bar.sync %0, 64;" ::"r"(1 + quad) : "memory");
+          if (half == 0) {
+            mx = fmaxf(mx, s_half[tile & 1][row]);
+            // scaling > 0: the max of the scaled scores is the scaled max
+            const int n_tok = u < U ? PF_TILE : (int)partial;
+            if (ok && row < n_tok) atomicMax(&w.agg[(int64_t)b * w.c_cap + u * S + row], f2key(mx * q.scaling));
+          }
         }
       }
     }
@@ -277,7 +306,7 @@ prefill_scores_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
     if (COARSE && my_units > 0) {
       uint32_t mk = 0;
       double sm = 0.0;
-      for (int i = 0; i < 4; ++i) {
+      for (int i = 0; i < PF_EPI; ++i) {
         mk = s_wmax[i] > mk ? s_wmax[i] : mk;
         sm += s_wsum[i];
       }
