@@ -1033,6 +1033,13 @@ attend_prefill_kernel(AttnArgs<T> a, T *out, float *partial_out) {
     hrow[hh] = kvh * G + rrow[hh] / Q;
     tqrow[hh] = rrow[hh] % Q;
   }
+  // tiles whose every (row, key) of this warp is visible skip the per-element
+  // masking: all 16 rows exist, and (causal) the tile's last hot row is visible
+  // to the warp's earliest position
+  const bool rows_full = r0 + warp * 16 + 15 < rows_kv;
+  int tq_min = min(tqrow[0], tqrow[1]);
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) tq_min = min(tq_min, __shfl_xor_sync(KIV_FULL_MASK, tq_min, o));
 
   for (int t = 0; t < ntile; ++t) {
     if (t + 1 < ntile) cp_async_wait<1>();
@@ -1058,6 +1065,21 @@ attend_prefill_kernel(AttnArgs<T> a, T *out, float *partial_out) {
     // ---- scale, soft-cap, mask; online softmax per row
     const int64_t k0 = (int64_t)t * AP_KEYS;
     float mx[2] = {-INFINITY, -INFINITY};
+    const int64_t k_last = k0 + AP_KEYS - 1;
+    const bool fast = rows_full && a.mask.add == nullptr && k_last < nkeys &&
+                      (!a.mask.causal || k_last < ncold || hot_lo + (k_last - ncold) <= hot_len - Q + tq_min);
+    if (fast) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float sc = s[j][i] * q.scaling;
+          if (q.softcap > 0.f) sc = q.softcap * tanhf(sc / q.softcap);
+          s[j][i] = sc;
+          mx[i >> 1] = fmaxf(mx[i >> 1], sc);
+        }
+      }
+    } else
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
 #pragma unroll

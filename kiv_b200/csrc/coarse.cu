@@ -276,17 +276,20 @@ constexpr int RT_THREADS = 256;
 constexpr int RT_WARPS = RT_THREADS / 32;
 constexpr int RT_CAND = 256;          // boundary keys resolved by ranking; also the largest top_pages
 constexpr int RT_UNROLL = 16;         // independent loads in flight per lane
+constexpr int RT_HWORDS = SEL_BINS + SEL_BINS / 64;   // histogram with one pad word per 64 bins
+// bin -> word: lane l scans bins [64 l, 64 l + 64) of the 2048, which start 65 words apart
+__device__ __forceinline__ int rt_hidx(int bin) { return bin + (bin >> 6); }
 
 __global__ void __launch_bounds__(RT_THREADS)
 coarse_rows_topk_kernel(kiv_store st, kiv_query q, Workspace w, float *row_scores, int32_t *row_pages,
                         int nwords) {
   extern __shared__ uint32_t rt_smem[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  uint32_t *hist = rt_smem + warp * SEL_BINS;
-  uint32_t *ckey = rt_smem + RT_WARPS * SEL_BINS + warp * RT_CAND;
-  int32_t *cidx = reinterpret_cast<int32_t *>(rt_smem + RT_WARPS * (SEL_BINS + RT_CAND)) + warp * RT_CAND;
-  uint8_t *cflag = reinterpret_cast<uint8_t *>(rt_smem + RT_WARPS * (SEL_BINS + 2 * RT_CAND)) + warp * RT_CAND;
-  uint32_t *bits = rt_smem + RT_WARPS * (SEL_BINS + 2 * RT_CAND) + RT_WARPS * RT_CAND / 4;   // [nwords]
+  uint32_t *hist = rt_smem + warp * RT_HWORDS;
+  uint32_t *ckey = rt_smem + RT_WARPS * RT_HWORDS + warp * RT_CAND;
+  int32_t *cidx = reinterpret_cast<int32_t *>(rt_smem + RT_WARPS * (RT_HWORDS + RT_CAND)) + warp * RT_CAND;
+  uint8_t *cflag = reinterpret_cast<uint8_t *>(rt_smem + RT_WARPS * (RT_HWORDS + 2 * RT_CAND)) + warp * RT_CAND;
+  uint32_t *bits = rt_smem + RT_WARPS * (RT_HWORDS + 2 * RT_CAND) + RT_WARPS * RT_CAND / 4;   // [nwords]
   for (int i = threadIdx.x; i < nwords; i += RT_THREADS) bits[i] = 0;
   const int S = st.page_size;
   const int nsh = st.shard_count, rank = st.shard_rank;
@@ -312,7 +315,7 @@ coarse_rows_topk_kernel(kiv_store st, kiv_query q, Workspace w, float *row_score
       for (int level = 0; level < 3; ++level) {
         const int sh = level == 0 ? 21 : (level == 1 ? 10 : 0);
         const int nbins = level == 2 ? 1024 : 2048;
-        for (int i = lane; i < nbins; i += 32) hist[i] = 0;
+        for (int i = lane; i < RT_HWORDS; i += 32) hist[i] = 0;
         __syncwarp();
         for (int64_t base = 0; base < np; base += 32 * RT_UNROLL) {
           float v[RT_UNROLL];
@@ -324,7 +327,7 @@ coarse_rows_topk_kernel(kiv_store st, kiv_query q, Workspace w, float *row_score
 #pragma unroll
           for (int x = 0; x < RT_UNROLL; ++x) {
             const uint32_t key = f2key(v[x]);
-            if (base + x * 32 + lane < np && (key & mask) == prefix) atomicAdd(&hist[(key >> sh) & (nbins - 1)], 1u);
+            if (base + x * 32 + lane < np && (key & mask) == prefix) atomicAdd(&hist[rt_hidx((key >> sh) & (nbins - 1))], 1u);
           }
         }
         __syncwarp();
@@ -332,7 +335,7 @@ coarse_rows_topk_kernel(kiv_store st, kiv_query q, Workspace w, float *row_score
         const int per = nbins / 32;
         const int hi = nbins - 1 - lane * per;
         uint32_t tot = 0;
-        for (int x = 0; x < per; ++x) tot += hist[hi - x];
+        for (int x = 0; x < per; ++x) tot += hist[rt_hidx(hi - x)];
         uint32_t incl = tot;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -347,7 +350,7 @@ coarse_rows_topk_kernel(kiv_store st, kiv_query q, Workspace w, float *row_score
         if (lane == sl) {
           uint32_t acc = excl;
           for (int x = 0; x < per; ++x) {
-            const uint32_t h = hist[hi - x];
+            const uint32_t h = hist[rt_hidx(hi - x)];
             if (acc + h >= remaining) {
               bin = hi - x;
               above = acc;
@@ -659,7 +662,7 @@ kiv_status launch_coarse(const kiv_store *st, const kiv_query *q, const Workspac
     // prefill-shaped rows: one warp per row
     const int64_t words = ceil_div(w.np_cap, 32);
     const int nwords = words <= 4096 ? (int)words : 0;
-    const size_t smem = 4 * (size_t)RT_WARPS * (SEL_BINS + 2 * RT_CAND) + (size_t)RT_WARPS * RT_CAND +
+    const size_t smem = 4 * (size_t)RT_WARPS * (RT_HWORDS + 2 * RT_CAND) + (size_t)RT_WARPS * RT_CAND +
                         4 * (size_t)nwords;
     const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(ceil_div(w.R, RT_WARPS), 2 * (int64_t)sm_count()));
     cudaFuncSetAttribute(coarse_rows_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

@@ -250,16 +250,25 @@ prefill_scores_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
               }
             }
           } else if (valid == g.nt) {
-            for (int c0 = 16 * half; c0 < g.nt; c0 += 64) {
-              uint32_t r0[16], r1[16];
-              tc::ld_32x16(taddr + c0, r0);
-              if (c0 + 32 < g.nt) tc::ld_32x16(taddr + c0 + 32, r1);
-              tc::wait_ld();
+            // this half's chunks (half, half + 2, ...; at most 8) in two TMEM
+            // round trips of four (the register file of one SM sub-partition
+            // holds three warps of this kernel)
+            const int nch = (g.nt / 16 + 1 - half) / 2;
 #pragma unroll
-              for (int cc = 0; cc < 16; ++cc) m[cc & 7] = fmaxf(m[cc & 7], __uint_as_float(r0[cc]));
-              if (c0 + 32 < g.nt) {
+            for (int x0 = 0; x0 < 8; x0 += 4) {
+              if (x0 < nch) {
+                uint32_t r[4][16];
 #pragma unroll
-                for (int cc = 0; cc < 16; ++cc) m[cc & 7] = fmaxf(m[cc & 7], __uint_as_float(r1[cc]));
+                for (int x = 0; x < 4; ++x)
+                  if (x0 + x < nch) tc::ld_32x16(taddr + (uint32_t)((half + 2 * (x0 + x)) * 16), r[x]);
+                tc::wait_ld();
+#pragma unroll
+                for (int x = 0; x < 4; ++x) {
+                  if (x0 + x < nch) {
+#pragma unroll
+                    for (int cc = 0; cc < 16; ++cc) m[cc & 7] = fmaxf(m[cc & 7], __uint_as_float(r[x][cc]));
+                  }
+                }
               }
             }
           } else {
