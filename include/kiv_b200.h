@@ -22,6 +22,16 @@
  *                                                 at slot (hot_start + j) % hot_capacity
  * Sharding: global page p lives on shard p % shard_count at local page
  * p / shard_count; with shard_count == 1 local == global.
+ *
+ * Host overflow tier (host_capacity > 0): the HBM cold slots hold a ring of
+ * the newest R = cold_capacity / S - stage_pages local pages (local page lp at
+ * ring page lp % R) plus stage_pages staging pages after it; older pages live
+ * in pinned, device-mapped host memory, page lp at rows [lp*S, lp*S + S) of
+ *   host_k, host_v  [B, Hkv, host_capacity, D]
+ * and the summaries cover all R + host_capacity / S local pages.  The
+ * eviction kernel copies a ring page to the host tier just before the ring
+ * slot is reused; a retrieval gathers the union's host pages (K) and its
+ * selected host rows (V) into the staging pages before the kernels read them.
  */
 #ifndef KIV_B200_H
 #define KIV_B200_H
@@ -72,6 +82,7 @@ typedef int32_t kiv_status;
 #define KIV_ERRBIT_UNION_CAPACITY 2   /* union larger than the workspace: truncated */
 #define KIV_ERRBIT_CAND_CAPACITY 4    /* candidates larger than the workspace */
 #define KIV_ERRBIT_WAIT_TIMEOUT 8     /* a bounded wait on a bulk copy gave up */
+#define KIV_ERRBIT_STAGE_CAPACITY 16  /* more host pages in the union than staging pages */
 
 typedef struct kiv_store {
   int32_t batch;
@@ -87,6 +98,11 @@ typedef struct kiv_store {
   void *cold_k, *cold_v, *summaries;
   void *hot_k, *hot_v;
   int64_t *state;           /* device, KIV_STATE_WORDS words */
+  /* host overflow tier (all zero / NULL: none) */
+  int64_t host_capacity;    /* token slots of the pinned host tier (multiple of page_size) */
+  void *host_k, *host_v;    /* pinned, device-mapped host memory [B, Hkv, host_capacity, D] */
+  int32_t stage_pages;      /* staging pages at the end of the HBM cold slots */
+  int32_t reserved;
 } kiv_store;
 
 typedef struct kiv_query {
@@ -298,6 +314,13 @@ KIV_API kiv_status kiv_attend_exchange_merge(const kiv_store *st, const kiv_quer
 
 /* Copy the store's device state words to host memory (synchronizes the stream). */
 KIV_API kiv_status kiv_read_state(const kiv_store *st, int64_t *host_words, void *stream);
+
+/* Host overflow tier: pinned host memory mapped into the device address space
+ * (UVA), usable as kiv_store.host_k / host_v; freed with kiv_host_free.
+ * No reference counterpart (the reference keeps its whole cold tier in host
+ * memory, kiv/cold_store.py:92-109). */
+KIV_API kiv_status kiv_host_alloc(size_t bytes, void **ptr);
+KIV_API kiv_status kiv_host_free(void *ptr);
 
 #ifdef __cplusplus
 }

@@ -38,7 +38,9 @@ class StoreDesc(ctypes.Structure):
                 ("page_size", c_i32), ("dtype", c_i32), ("shard_rank", c_i32),
                 ("shard_count", c_i32), ("hot_hint", c_i32), ("cold_capacity", c_i64),
                 ("hot_capacity", c_i64), ("cold_k", c_vp), ("cold_v", c_vp),
-                ("summaries", c_vp), ("hot_k", c_vp), ("hot_v", c_vp), ("state", c_vp)]
+                ("summaries", c_vp), ("hot_k", c_vp), ("hot_v", c_vp), ("state", c_vp),
+                ("host_capacity", c_i64), ("host_k", c_vp), ("host_v", c_vp), ("stage_pages", c_i32),
+                ("reserved", c_i32)]
 
 
 class QueryDesc(ctypes.Structure):
@@ -64,6 +66,8 @@ P = ctypes.POINTER
 # name -> (restype, argtypes)
 SIGNATURES = {
     "kiv_abi_version": (c_i32, []),
+    "kiv_host_alloc": (c_i32, [ctypes.c_size_t, ctypes.POINTER(c_vp)]),
+    "kiv_host_free": (c_i32, [c_vp]),
     "kiv_status_string": (ctypes.c_char_p, [c_i32]),
     "kiv_last_error": (ctypes.c_char_p, []),
     "kiv_workspace_bytes": (c_sz, [P(StoreDesc), P(QueryDesc)]),

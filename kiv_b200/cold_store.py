@@ -23,6 +23,7 @@ shard p % shard_count); the collective steps then go through ``comm``.
 from __future__ import annotations
 
 import ctypes
+import weakref
 import math
 import os
 
@@ -34,6 +35,13 @@ from .model_topology import ModelTopology
 from .telemetry import RetrievalTelemetry
 
 _MIN_COLD = 8192
+
+
+def _free_host(ptr: int) -> None:
+    try:
+        nat.lib().kiv_host_free(ptr)
+    except Exception:  # pragma: no cover - interpreter shutdown
+        pass
 
 
 class ColdKVStore:
@@ -56,6 +64,9 @@ class ColdKVStore:
         self._batch: int | None = None
         self._dtype: torch.dtype | None = None
         self._k = self._v = self._summ = None
+        # pinned host overflow tier (kiv_host_alloc'd, freed with the store)
+        self._host_k = self._host_v = None
+        self._host_tokens = 0
         self._hk = self._hv = None
         self._hot_cap = 0
         self._state: torch.Tensor | None = None
@@ -121,7 +132,10 @@ class ColdKVStore:
         self._batch, self._dtype = batch, dtype
         self._state = torch.zeros(nat.STATE_WORDS, dtype=torch.int64, device=self.device)
         cap = self.kiv_config.cold_capacity or _MIN_COLD
-        self._alloc_cold(self._round_local(cap))
+        if self.kiv_config.host_tokens > 0:
+            self._alloc_tiered(self._round_local(cap), self._round_local(self.kiv_config.host_tokens))
+        else:
+            self._alloc_cold(self._round_local(cap))
 
     def _round_local(self, global_tokens: int) -> int:
         """Local token slots that hold the pages of ``global_tokens`` cold tokens."""
@@ -143,19 +157,68 @@ class ColdKVStore:
         self._ws.clear()
         self._cached_ws_key = None
 
+    def _alloc_tiered(self, ring: int, host: int) -> None:
+        """HBM ring of `ring` local token slots plus the staging pages, summaries
+        for ring + host pages, and the pinned host tier of `host` slots."""
+        B, H, D, S = self._batch, self._num_kv_heads, self._head_dim, self._page_size
+        stage = self.kiv_config.stage_pages
+        if ring // S < 2:
+            raise ValueError("the HBM ring of a tiered store needs at least 2 pages")
+        self._k = torch.empty(B, H, ring + stage * S, D, dtype=self._dtype, device=self.device)
+        self._v = torch.empty_like(self._k)
+        self._summ = torch.empty(B, H, (ring + host) // S, D, dtype=self._dtype, device=self.device)
+        self._ring_pages = ring // S
+        self._host_tokens = host
+        self._host_k = self._host_tensor(B, H, host, D)
+        self._host_v = self._host_tensor(B, H, host, D)
+        self._desc = None
+        self._ws.clear()
+        self._cached_ws_key = None
+
+    def _host_tensor(self, B: int, H: int, n: int, D: int) -> torch.Tensor:
+        """A [B, H, n, D] CPU tensor over pinned, device-mapped memory."""
+        esz = torch.empty((), dtype=self._dtype).element_size()
+        nbytes = B * H * n * D * esz
+        ptr = ctypes.c_void_p()
+        nat.check(nat.lib().kiv_host_alloc(nbytes, ctypes.byref(ptr)), "host_alloc")
+        weakref.finalize(self, _free_host, ptr.value)
+        buf = (ctypes.c_char * nbytes).from_address(ptr.value)
+        return torch.frombuffer(buf, dtype=torch.uint8).view(self._dtype).view(B, H, n, D)
+
+    @property
+    def tiered(self) -> bool:
+        """True when the store has a pinned host overflow tier."""
+        return self._host_tokens > 0
+
+    def _evict_limit(self) -> int | None:
+        """Most cold rows one eviction call may move with a host tier (each
+        call may reach at most the ring's pages), None without one."""
+        if not self.tiered:
+            return None
+        return max(1, (self._ring_pages - 2) * self._page_size)
+
     def reserve(self, cold_tokens: int, hot_rows: int | None = None) -> None:
         """Preallocate room for ``cold_tokens`` cold tokens (and a hot buffer of
         ``hot_rows``) so later steps never reallocate (CUDA-graph capture)."""
         if self._state is None:
             raise RuntimeError("reserve() needs an initialized store (evict or append first)")
         need = self._round_local(cold_tokens)
-        if need > self._k.shape[2]:
+        if self.tiered:
+            if need > self._ring_pages * self._page_size + self._host_tokens:
+                raise nat.KIVNativeError(f"{cold_tokens} cold tokens exceed the HBM ring + host tier")
+        elif need > self._k.shape[2]:
             self._alloc_cold(need)
         if hot_rows is not None and hot_rows > self._hot_cap:
             self._grow_hot(hot_rows)
 
     def _ensure_cold_room(self, new_cold_len: int) -> None:
         need = self._round_local(new_cold_len)
+        if self.tiered:
+            if need > self._ring_pages * self._page_size + self._host_tokens:
+                raise nat.KIVNativeError(
+                    f"cold tier full: {new_cold_len} tokens exceed the HBM ring "
+                    f"({self._ring_pages * self._page_size}) + host tier ({self._host_tokens}) slots")
+            return
         cap = self._k.shape[2]
         if need > cap:
             self._alloc_cold(max(need, self._round_local(2 * self._cold_len)))
@@ -201,7 +264,9 @@ class ColdKVStore:
                 nat.dtype_code(self._dtype), self._shard_rank, self._shard_count, 0,
                 self._k.shape[2], self._hot_cap,
                 self._k.data_ptr(), self._v.data_ptr(), self._summ.data_ptr(),
-                nat.ptr(self._hk), nat.ptr(self._hv), self._state.data_ptr())
+                nat.ptr(self._hk), nat.ptr(self._hv), self._state.data_ptr(),
+                self._host_tokens, nat.ptr(self._host_k), nat.ptr(self._host_v),
+                self.kiv_config.stage_pages if self.tiered else 0, 0)
         return self._desc
 
     def _rows(self, x: torch.Tensor) -> torch.Tensor:
@@ -228,6 +293,11 @@ class ColdKVStore:
         self._ensure_alloc(B, k_evicted.dtype)
         if n == 0:
             return
+        limit = self._evict_limit()
+        if limit is not None and n > limit:
+            for a in range(0, n, limit):
+                self.evict_from_hot(k_evicted[:, :, a:a + limit], v_evicted[:, :, a:a + limit])
+            return
         k, v = self._rows(k_evicted), self._rows(v_evicted)
         self._ensure_cold_room(self._cold_len + n)
         with torch.cuda.device(self.device):
@@ -251,6 +321,17 @@ class ColdKVStore:
         n_ev = 0 if keep < 0 else min(max(self._hot_len + n - keep, 0), self._hot_len + n)
         if n == 0 and n_ev == 0:
             return 0
+        limit = self._evict_limit()
+        if limit is not None and n_ev > limit:
+            # a host tier bounds the pages one call reaches: append, then evict in steps
+            if n > 0:
+                self.append_and_evict(k_new, v_new, -1)
+            done = 0
+            while done < n_ev:
+                c = min(limit, n_ev - done)
+                self.append_and_evict(None, None, self._hot_len - c)
+                done += c
+            return n_ev
         self._ensure_hot_room(n)
         self._ensure_cold_room(self._cold_len + n_ev)
         if n > 0:
@@ -622,9 +703,16 @@ class ColdKVStore:
         local_fin = self._local_pages(self.num_pages) * self._page_size
         part = self._partial_len if (self.num_pages % self._shard_count) == self._shard_rank else 0
         reserved = sum(t.numel() * t.element_size() for t in (self._k, self._v, self._summ))
+        host_k = host_v = 0
+        if self.tiered:
+            # pages older than the HBM ring live in the pinned host tier
+            started = self._local_pages(math.ceil(self._cold_len / self._page_size))
+            on_host = max(0, started - self._ring_pages) * self._page_size
+            host_k = host_v = on_host * row
+            local_fin = max(0, local_fin - on_host)
         return {
-            "k_index_cpu": 0,
-            "v_store_cpu": 0,
+            "k_index_cpu": host_k,
+            "v_store_cpu": host_v,
             "page_summaries_gpu": self._local_pages(self.num_pages) * row,
             "partial_gpu": 2 * part * row,
             "cold_k_gpu": local_fin * row,

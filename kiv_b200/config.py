@@ -32,3 +32,15 @@ class KIVConfig:
     hot_slack: int = 2048
     # Record per-call retrieval telemetry (copied asynchronously, no host sync).
     telemetry: bool = True
+    # Pinned host overflow tier: cold tokens per layer kept in host memory once
+    # the HBM cold tier (cold_capacity tokens, then a ring of the newest pages)
+    # is full.  0: no host tier (the cold tier grows in HBM).  Needs cold_capacity.
+    host_tokens: int = 0
+    # HBM staging pages for the host-resident pages of one retrieval's union.
+    stage_pages: int = 1024
+
+    def __post_init__(self) -> None:
+        if self.host_tokens < 0 or self.stage_pages < 1:
+            raise ValueError("host_tokens must be >= 0 and stage_pages >= 1")
+        if self.host_tokens > 0 and not self.cold_capacity:
+            raise ValueError("a host tier (host_tokens > 0) needs cold_capacity (the HBM ring size)")

@@ -37,7 +37,7 @@ Workspace workspace_layout(const kiv_store *st, const kiv_query *q, void *base) 
   Workspace w = {};
   w.R = (int64_t)st->batch * q->num_query_heads * q->query_len;
   w.K = q->top_pages;
-  w.np_cap = st->cold_capacity / st->page_size;
+  w.np_cap = summary_pages(*st);
   w.u_cap = std::min<int64_t>(w.np_cap, w.R * w.K);
   w.c_cap = w.u_cap * st->page_size + st->page_size;
   w.split_cap = attn_split_cap(st, q);
@@ -58,6 +58,7 @@ Workspace workspace_layout(const kiv_store *st, const kiv_query *q, void *base) 
   w.chist = reinterpret_cast<uint32_t *>(take(prefill_shape(st, q) ? 0 : w.R * 2048 * 4));
   w.cstat = reinterpret_cast<uint64_t *>(take(16));
   w.part = reinterpret_cast<float *>(take(w.R * w.split_cap * partial_stride(st->head_dim) * 4));
+  w.pslot = reinterpret_cast<int32_t *>(take(st->host_capacity > 0 ? w.np_cap * 4 : 0));
   w.bytes = (size_t)off;
   return w;
 }
@@ -97,6 +98,21 @@ static kiv_status check_store(const kiv_store *st) {
   if (st->hot_capacity > 0 && (!st->hot_k || !st->hot_v || !aligned16(st->hot_k) || !aligned16(st->hot_v))) {
     set_error("hot ring missing or not 16-byte aligned");
     return KIV_ERR_ARG;
+  }
+  if (st->host_capacity < 0 || st->host_capacity % st->page_size != 0) {
+    set_error("host_capacity %lld not a multiple of page_size", (long long)st->host_capacity);
+    return KIV_ERR_ARG;
+  }
+  if (st->host_capacity > 0) {
+    if (!st->host_k || !st->host_v || !aligned16(st->host_k) || !aligned16(st->host_v)) {
+      set_error("host tier missing or not 16-byte aligned");
+      return KIV_ERR_ARG;
+    }
+    if (st->stage_pages < 1 || ring_pages(*st) < 2) {
+      set_error("host tier needs stage_pages >= 1 and at least 2 ring pages (cold_capacity %lld, stage %d)",
+                (long long)st->cold_capacity, st->stage_pages);
+      return KIV_ERR_ARG;
+    }
   }
   return KIV_OK;
 }
@@ -352,6 +368,15 @@ kiv_status kiv_peer_open(const void *ipc_handle, void **dev_ptr) {
 kiv_status kiv_peer_close(void *dev_ptr) { return cuda_status(cudaIpcCloseMemHandle(dev_ptr), "peer_close"); }
 
 kiv_status kiv_peer_free(void *dev_ptr) { return cuda_status(cudaFree(dev_ptr), "peer_free"); }
+
+kiv_status kiv_host_alloc(size_t bytes, void **ptr) {
+  if (!ptr || bytes == 0) { set_error("bad host_alloc arguments"); return KIV_ERR_ARG; }
+  *ptr = nullptr;
+  // pinned, mapped into every device's address space (UVA: same pointer)
+  return cuda_status(cudaHostAlloc(ptr, bytes, cudaHostAllocMapped | cudaHostAllocPortable), "host_alloc");
+}
+
+kiv_status kiv_host_free(void *ptr) { return cuda_status(cudaFreeHost(ptr), "host_free"); }
 
 static kiv_status check_exchange(const kiv_store *st, const kiv_query *q, const kiv_exchange *x, int t,
                                  int64_t ctas, kiv::XArgs &a) {

@@ -139,7 +139,7 @@ attend_split_kernel(AttnArgs<T> a) {
     } else {
       const int64_t tok = tok_hint >= 0 ? tok_hint : selb[k - hot_count];
       const int64_t p = tok / S;
-      const int64_t slot = (p / st.shard_count) * S + tok % S;
+      const int64_t slot = page_slot(st, a.w, p / st.shard_count) * S + tok % S;
       pk = cold_k + (bhk * st.cold_capacity + slot) * D;
       pv = cold_v + (bhk * st.cold_capacity + slot) * D;
     }
@@ -482,7 +482,7 @@ attend_mma_kernel(AttnArgs<T> a) {
     } else {
       const int64_t tok = tok_hint >= 0 ? tok_hint : selb[k - hot_count];
       const int64_t p = tok / S;
-      const int64_t slot = (p / st.shard_count) * S + tok % S;
+      const int64_t slot = page_slot(st, a.w, p / st.shard_count) * S + tok % S;
       pk = cold_k + (bhk * st.cold_capacity + slot) * D;
       pv = cold_v + (bhk * st.cold_capacity + slot) * D;
     }
@@ -846,6 +846,8 @@ __global__ void gather_kernel(kiv_store st, const int32_t *sel, int32_t stride, 
   const int D = st.head_dim, H = st.num_kv_heads, S = st.page_size;
   const int nv = D / V;
   const int64_t cold_len = st_ld(st.state, KIV_ST_COLD_LEN);
+  const int64_t ng = (cold_len + S - 1) / S;   // global pages with rows
+  const int64_t started = ng > st.shard_rank ? (ng - st.shard_rank + st.shard_count - 1) / st.shard_count : 0;
   const int64_t total = (int64_t)st.batch * H * P * nv;
   for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
        e += (int64_t)gridDim.x * blockDim.x) {
@@ -857,9 +859,17 @@ __global__ void gather_kernel(kiv_store st, const int32_t *sel, int32_t stride, 
     if (tok < 0 || tok >= cold_len) continue;
     const int64_t p = tok / S;
     if (p % st.shard_count != st.shard_rank) continue;
-    const int64_t slot = (p / st.shard_count) * S + tok % S;
-    const int64_t src = (bh * st.cold_capacity + slot) * D + vi * V;
+    const int64_t lp = p / st.shard_count;
     const int64_t dst = (bh * P + i) * D + vi * V;
+    if (st.host_capacity > 0 && lp < started - ring_pages(st)) {
+      // a page of the host tier: read it there (mapped host memory)
+      const int64_t src = (bh * st.host_capacity + lp * S + tok % S) * D + vi * V;
+      st16(ok + dst, ld16(reinterpret_cast<const T *>(st.host_k) + src));
+      st16(ov + dst, ld16(reinterpret_cast<const T *>(st.host_v) + src));
+      continue;
+    }
+    const int64_t slot = (st.host_capacity > 0 ? lp % ring_pages(st) : lp) * S + tok % S;
+    const int64_t src = (bh * st.cold_capacity + slot) * D + vi * V;
     st16(ok + dst, ld16(reinterpret_cast<const T *>(st.cold_k) + src));
     st16(ov + dst, ld16(reinterpret_cast<const T *>(st.cold_v) + src));
   }
@@ -995,7 +1005,7 @@ attend_prefill_kernel(AttnArgs<T> a, T *out, float *partial_out) {
         const T *bk, *bv;
         if (k < ncold) {
           const int64_t tok = selb[k], p = tok / S;
-          off = (bhk * st.cold_capacity + (p / st.shard_count) * S + tok % S) * D;
+          off = (bhk * st.cold_capacity + page_slot(st, a.w, p / st.shard_count) * S + tok % S) * D;
           bk = cold_k;
           bv = cold_v;
         } else {
@@ -1211,6 +1221,8 @@ static kiv_status attend_t(const kiv_store *st, const kiv_query *q, const kiv_ma
                            const Workspace &w, const int32_t *sel, int32_t sel_stride,
                            int32_t hot_slice, int32_t hot_slices, void *out, float *partial_out,
                            cudaStream_t s) {
+  // host tier: the selected rows of host pages reach their staging pages first
+  KIV_CHECK(launch_stage_selected(st, w, sel, sel_stride, s));
   const int64_t expected_hot = st->hot_hint > 0 ? st->hot_hint : st->hot_capacity;
   AttnArgs<T> a;
   a.st = *st;

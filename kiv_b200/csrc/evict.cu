@@ -45,11 +45,16 @@ append_evict_kernel(kiv_store st, const T *__restrict__ k_new, const T *__restri
   bool ok = direct || (hot_len + n_new <= hcap) || (hcap == 0 && hot_len == 0 && n_ev == n_new);
   ok = ok && (direct || hot_after <= (hcap > 0 ? hcap : 0));
   // the highest page this shard owns among those the evicted rows reach must
-  // fit its local slots
+  // fit its local slots (with a host tier: its ring plus host pages)
+  const bool tiered = st.host_capacity > 0;
+  const int64_t ring = ring_pages(st);
   const int64_t last_page = (cold_len + n_ev + S - 1) / S - 1;  // global page of the last evicted row
   if (n_ev > 0 && last_page >= st.shard_rank &&
-      ((last_page - st.shard_rank) / st.shard_count + 1) * (int64_t)S > st.cold_capacity)
+      ((last_page - st.shard_rank) / st.shard_count + 1) > (tiered ? summary_pages(st) : st.cold_capacity / S))
     ok = false;
+  // with a host tier one call may reach at most `ring` local pages (each ring
+  // slot is spilled once, before this call overwrites it)
+  if (tiered && pages_per_bh > ring) ok = false;
   // the grid covers ceil(n_evict_max / S) + 1 pages per (b, h)
   if (n_ev > n_evict_max) ok = false;
 
@@ -66,8 +71,20 @@ append_evict_kernel(kiv_store st, const T *__restrict__ k_new, const T *__restri
     const bool owned = (p % st.shard_count) == st.shard_rank;
     if (lo < hi && owned) {
       const int64_t lp = p / st.shard_count;
-      T *ck = reinterpret_cast<T *>(st.cold_k) + ((int64_t)bh * st.cold_capacity + lp * S) * D;
-      T *cv = reinterpret_cast<T *>(st.cold_v) + ((int64_t)bh * st.cold_capacity + lp * S) * D;
+      const int64_t slot = tiered ? lp % ring : lp;
+      T *ck = reinterpret_cast<T *>(st.cold_k) + ((int64_t)bh * st.cold_capacity + slot * S) * D;
+      T *cv = reinterpret_cast<T *>(st.cold_v) + ((int64_t)bh * st.cold_capacity + slot * S) * D;
+      if (tiered && lo == p * S && lp >= ring) {
+        // this call starts page lp in ring slot lp % ring: its previous page
+        // lp - ring moves to the host tier first
+        T *hk = reinterpret_cast<T *>(st.host_k) + ((int64_t)bh * st.host_capacity + (lp - ring) * S) * D;
+        T *hv = reinterpret_cast<T *>(st.host_v) + ((int64_t)bh * st.host_capacity + (lp - ring) * S) * D;
+        for (int e = threadIdx.x; e < S * nv; e += EV_THREADS) {
+          st16(hk + (int64_t)e * V, ld16(ck + (int64_t)e * V));
+          st16(hv + (int64_t)e * V, ld16(cv + (int64_t)e * V));
+        }
+        __syncthreads();
+      }
       const int rows = (int)(hi - lo);
       for (int e = threadIdx.x; e < rows * nv; e += EV_THREADS) {
         const int r = e / nv, vi = e % nv;
@@ -90,8 +107,7 @@ append_evict_kernel(kiv_store st, const T *__restrict__ k_new, const T *__restri
       if (hi == (p + 1) * S) {
         // the page is complete: summary = (sum of its rows in token order) / S
         __syncthreads();
-        T *sm = reinterpret_cast<T *>(st.summaries) +
-                ((int64_t)bh * (st.cold_capacity / S) + lp) * D;
+        T *sm = reinterpret_cast<T *>(st.summaries) + ((int64_t)bh * summary_pages(st) + lp) * D;
         for (int c = threadIdx.x; c < D; c += EV_THREADS) {
           float acc = 0.f;
           const T *col = ck + c;

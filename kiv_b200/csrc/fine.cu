@@ -118,7 +118,7 @@ fine_scores_kernel(kiv_store st, kiv_query q, Workspace w, int tr, int stage_q) 
     const uint32_t bytes = (uint32_t)x.rows * D * sizeof(T);
     if (bytes > 0) {
       const int64_t page = x.u < f.U ? (int64_t)w.uni[x.u] : f.np_global;
-      const int64_t lp = page / st.shard_count;
+      const int64_t lp = page_slot(st, w, page / st.shard_count);
       const T *src = cold_k + (((int64_t)x.b * H + kvh) * st.cold_capacity + lp * S + (int64_t)x.rb * tr) * D;
       mbar_arrive_tx(&bars[stage], bytes);
       bulk_g2s(tiles + (size_t)stage * tr * D, src, bytes, &bars[stage]);
@@ -641,6 +641,7 @@ kiv_status launch_fine_score(const kiv_store *st, const kiv_query *q, const Work
   if (fine_tc_eligible(st, q)) return launch_fine_score_tc(st, q, w, s);
   if (prefill_tc_eligible(st, q)) return launch_prefill_fine_scores(st, q, w, s);
   KIV_CHECK(launch_union(st, w, s));
+  KIV_CHECK(launch_stage_union(st, w, s));
   switch (st->dtype) {
     case KIV_DTYPE_F32: return dispatch_fs<float>(st, q, w, s);
     case KIV_DTYPE_BF16: return dispatch_fs<__nv_bfloat16>(st, q, w, s);

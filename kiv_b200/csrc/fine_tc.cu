@@ -196,7 +196,7 @@ scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_que
           y = (int32_t)((bh0 + kvh) * w.np_cap + u * TC_PAGE);
         } else {
           const int64_t page = u < f.U ? (int64_t)pages[u] : f.np_global;
-          const int64_t lp = page / st.shard_count;
+          const int64_t lp = page_slot(st, w, page / st.shard_count);
           y = (int32_t)((bh0 + kvh) * st.cold_capacity + lp * S);
         }
         mbar_arrive_tx(&full[s], tile_bytes);
@@ -406,8 +406,12 @@ static kiv_status launch_scores_tc(const kiv_store *st, const kiv_query *q, cons
   const size_t tile = (size_t)TC_PAGE * D * 2;
   const size_t qbytes = (size_t)st->num_kv_heads * ncols * D * 2;
   // fine pass: the union list is built in shared memory unless it is large
-  const int union_inline = !coarse && w.u_cap <= TC_UNION_INLINE ? 1 : 0;
-  if (!coarse && !union_inline) KIV_CHECK(launch_union(st, w, s));
+  // (with a host tier the union is staged before scoring: built separately)
+  const int union_inline = !coarse && w.u_cap <= TC_UNION_INLINE && st->host_capacity == 0 ? 1 : 0;
+  if (!coarse && !union_inline) {
+    KIV_CHECK(launch_union(st, w, s));
+    KIV_CHECK(launch_stage_union(st, w, s));
+  }
   const size_t fixed = 1024 + qbytes + SEL_BINS * 4 + (union_inline ? (size_t)w.u_cap * 4 : 0);
   const int stages = (int)std::min<size_t>(4, (200 * 1024 - fixed) / tile);
   if (stages < 2) return KIV_ERR_UNSUPPORTED;

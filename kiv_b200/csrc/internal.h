@@ -38,11 +38,31 @@ struct Workspace {
   uint32_t *chist;     // [R, 2048]          histogram of coarse keys >> 21 per query row, self-clearing
   uint64_t *cstat;     // [2]                largest coarse key, sum of coarse scores (double bits)
   float *part;         // [R, split_cap, D+2] attention split partials
+  int32_t *pslot;      // [np_cap]            HBM page slot of each local page this step (host tier only)
   int64_t R, K, np_cap, u_cap, c_cap, split_cap;
   size_t bytes;
 };
 
 Workspace workspace_layout(const kiv_store *st, const kiv_query *q, void *base);
+
+// ---- host overflow tier geometry (host_capacity > 0)
+// ring pages of the HBM cold slots (the newest local pages), staging pages after them
+__host__ __device__ inline int64_t ring_pages(const kiv_store &st) {
+  return st.cold_capacity / st.page_size - (st.host_capacity > 0 ? st.stage_pages : 0);
+}
+// local pages the summaries (and the page slot table) cover
+__host__ __device__ inline int64_t summary_pages(const kiv_store &st) {
+  return st.host_capacity > 0 ? ring_pages(st) + st.host_capacity / st.page_size : st.cold_capacity / st.page_size;
+}
+// HBM page slot to read local page lp from in this step: identity without a host
+// tier; otherwise the slot the staging kernel recorded (ring slot, or a staging
+// page for a host-resident page of the union)
+__device__ __forceinline__ int64_t page_slot(const kiv_store &st, const Workspace &w, int64_t lp) {
+  return st.host_capacity > 0 ? (int64_t)w.pslot[lp] : lp;
+}
+kiv_status launch_stage_union(const kiv_store *st, const Workspace &w, cudaStream_t s);
+kiv_status launch_stage_selected(const kiv_store *st, const Workspace &w, const int32_t *sel, int32_t sel_stride,
+                                 cudaStream_t s);
 
 int sm_count();
 void set_error(const char *fmt, ...);

@@ -160,7 +160,7 @@ prefill_scores_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
             y = (int32_t)(bh * w.np_cap + u * PF_TILE);
           } else {
             const int64_t page = u < U ? (int64_t)w.uni[u] : np_global;
-            y = (int32_t)(bh * st.cold_capacity + (page / st.shard_count) * S);
+            y = (int32_t)(bh * st.cold_capacity + page_slot(st, w, page / st.shard_count) * S);
           }
           mbar_arrive_tx(&full[s], tile_bytes);
           for (int jb = 0; jb < nbox; ++jb)
@@ -497,6 +497,7 @@ kiv_status launch_prefill_coarse_scores(const kiv_store *st, const kiv_query *q,
 kiv_status launch_prefill_fine_scores(const kiv_store *st, const kiv_query *q, const Workspace &w,
                                       cudaStream_t s) {
   KIV_CHECK(launch_union(st, w, s));
+  KIV_CHECK(launch_stage_union(st, w, s));
   const int64_t prep_grid = std::max<int64_t>(1, std::min<int64_t>(ceil_div(w.c_cap, 4 * 256), sm_count() * 4));
   KIV_CHECK(cuda_status(launch_pdl(agg_prep_kernel, dim3((unsigned)prep_grid), dim3(256), 0, s, 1, *st, w),
                         "agg_prep"));

@@ -196,6 +196,47 @@ class TieredKVCache(DynamicCache):
         self._suppress_cold = False
         self._decode_step = 0
 
+    # ------------------------------------------------------------ persistence
+    def save(self, directory: str) -> None:
+        """Write every independent layer's store (``kiv_b200.persist`` format,
+        one file per layer) and the cache counters to `directory`."""
+        import json
+        import os
+
+        from .persist import save_store
+
+        os.makedirs(directory, exist_ok=True)
+        for li, store in self.cold_stores.items():
+            if store.initialized:
+                save_store(store, os.path.join(directory, f"layer_{li}.kivstore"), meta={"layer": li})
+        state = {"prefill_complete": self._prefill_complete, "decode_step": self._decode_step,
+                 "total_tokens": {str(k): v for k, v in self._total_tokens.items()}}
+        with open(os.path.join(directory, "cache.json"), "w") as f:
+            json.dump(state, f)
+
+    def load(self, directory: str) -> None:
+        """Restore a cache written by save() into this empty cache (same
+        topology); the stores may have another HBM / host tier configuration."""
+        import json
+        import os
+
+        from .persist import load_store
+
+        with open(os.path.join(directory, "cache.json")) as f:
+            state = json.load(f)
+        for li, store in self.cold_stores.items():
+            path = os.path.join(directory, f"layer_{li}.kivstore")
+            if not os.path.exists(path):
+                continue
+            load_store(store, path)
+            layer = self.layers[li]
+            if not layer.is_initialized:
+                layer.dtype, layer.device = store._dtype, store.device
+                layer.is_initialized = True
+        self._prefill_complete = bool(state["prefill_complete"])
+        self._decode_step = int(state["decode_step"])
+        self._total_tokens = {int(k): int(v) for k, v in state["total_tokens"].items()}
+
     def truncate_to(self, new_len: int) -> bool:
         """Trim every global layer to ``new_len`` tokens, inside the hot window only.
 

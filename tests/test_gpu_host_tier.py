@@ -1,0 +1,145 @@
+"""Host overflow tier and store persistence on the GPU.
+
+A tiered store keeps only a ring of the newest pages in HBM (here 8 pages),
+the older pages in pinned host memory; retrievals stage the union's host pages
+(K) and the selected host rows (V) into HBM first.  Every read goes through
+copies of the same bytes, so a tiered cache must give BIT-IDENTICAL results to
+an HBM-only cache on the same inputs: page summaries, selected token sets,
+gathered rows and attention outputs, through prefill, decode steps that cross
+page boundaries (ring slots reused, pages spilled), and a prefill-shaped
+chunk.  Persistence: a cache saved to disk and loaded into fresh caches (HBM
+only, or tiered with another ring size) continues the sequence with the same
+outputs as the original.
+"""
+
+import numpy as np
+import pytest
+import torch
+from transformers import PretrainedConfig
+
+from kiv_b200 import KIVConfig, ModelTopology, TieredKVCache
+from kiv_b200 import _native as nat
+from kiv_b200.synthetic import SynthSpec, make_problem
+from tests.gpu_helpers import DEV
+
+pytestmark = pytest.mark.gpu
+
+SPEC = SynthSpec(batch=2, num_query_heads=8, num_kv_heads=2, head_dim=128, cold_tokens=40 * 128 + 126,
+                 hot_budget=256, query_len=1)
+KNOBS = dict(top_pages=4, top_p=128)
+
+
+def _cache(tiered: bool, ring_pages: int = 8, stage_pages: int = 32, host_pages: int = 64, spec=SPEC):
+    extra = {}
+    if tiered:
+        extra = dict(cold_capacity=ring_pages * 128, host_tokens=host_pages * 128, stage_pages=stage_pages)
+    cfg = KIVConfig(hot_budget=spec.hot_budget, page_size=128, telemetry=False, **KNOBS, **extra)
+    topo = ModelTopology.manual(global_layer_indices=(0,), independent_kv_layers=(0,), kv_sharing_map={},
+                                num_query_heads=spec.num_query_heads, num_kv_heads=spec.num_kv_heads,
+                                head_dim=spec.head_dim, num_hidden_layers=1)
+    return cfg, TieredKVCache(PretrainedConfig(num_hidden_layers=1), cfg, topo, DEV)
+
+
+def _steps(n, seed=9, spec=SPEC):
+    g = torch.Generator().manual_seed(seed)
+    B, Hq, Hkv, D = spec.batch, spec.num_query_heads, spec.num_kv_heads, spec.head_dim
+    return [(torch.randn(B, Hq, 1, D, generator=g), 0.3 * torch.randn(B, Hkv, 1, D, generator=g),
+             torch.randn(B, Hkv, 1, D, generator=g)) for _ in range(n)]
+
+
+def _run(cache, cfg, steps, scaling):
+    """Decode steps: update + retrieve_indices + attend; returns the per-step results."""
+    out = []
+    store = cache.get_cold_store(0)
+    bf = lambda x: x.to(DEV, torch.bfloat16)
+    for q, k, v in steps:
+        cache.update(bf(k), bf(v), 0)
+        sel, P = store.retrieve_indices(bf(q), scaling, cfg, step=cache._decode_step)
+        o = store.attend(bf(q), scaling, cfg, step=cache._decode_step)
+        ko, vo = store.retrieve_top_kv(bf(q), scaling, cfg, step=cache._decode_step)
+        torch.cuda.synchronize()
+        out.append((sel[:, :P].cpu().clone(), o.float().cpu(), ko.float().cpu(), vo.float().cpu()))
+    return out
+
+
+def _prefill(cache, prob):
+    bf = lambda x: x.to(DEV, torch.bfloat16)
+    cache.update(bf(prob.prefill_k), bf(prob.prefill_v), 0)
+    cache.mark_prefill_complete()
+
+
+def test_tiered_cache_matches_hbm_only_bitwise():
+    prob = make_problem(SPEC, seed=4, dtype=torch.bfloat16)
+    scaling = SPEC.head_dim ** -0.5
+    steps = _steps(5)
+    cfg_a, plain = _cache(False)
+    cfg_b, tiered = _cache(True)
+    _prefill(plain, prob)
+    _prefill(tiered, prob)
+    sa, sb = plain.get_cold_store(0), tiered.get_cold_store(0)
+    assert sb.tiered and sb.cold_length == sa.cold_length == SPEC.cold_tokens
+    mem = sb.memory_bytes()
+    assert mem["k_index_cpu"] > 0 and mem["v_store_cpu"] == mem["k_index_cpu"]
+    assert torch.equal(sa.page_summaries(), sb.page_summaries())
+    ra, rb = _run(plain, cfg_a, steps, scaling), _run(tiered, cfg_b, steps, scaling)
+    for i, (x, y) in enumerate(zip(ra, rb)):
+        assert torch.equal(x[0], y[0]), f"step {i}: selections differ"
+        assert torch.equal(x[1], y[1]), f"step {i}: attention outputs differ"
+        assert torch.equal(x[2], y[2]) and torch.equal(x[3], y[3]), f"step {i}: gathered rows differ"
+    assert torch.equal(sa.page_summaries(), sb.page_summaries())
+    assert sb.read_state()[nat.ST_ERROR] == 0 and sa.read_state()[nat.ST_ERROR] == 0
+    # the steps crossed a page boundary: a ring slot was reused and its page spilled
+    assert sb.cold_length // 128 > SPEC.cold_tokens // 128
+
+
+def test_tiered_prefill_chunk_matches_hbm_only():
+    spec = SynthSpec(batch=1, num_query_heads=8, num_kv_heads=8, head_dim=96, cold_tokens=30 * 128 + 5,
+                     hot_budget=128, query_len=96)
+    prob = make_problem(spec, seed=6, dtype=torch.bfloat16)
+    bf = lambda x: x.to(DEV, torch.bfloat16)
+    scaling = spec.head_dim ** -0.5
+    outs = []
+    for tiered in (False, True):
+        cfg, cache = _cache(tiered, ring_pages=6, stage_pages=40, spec=spec)
+        _prefill(cache, prob)
+        cache.update(bf(prob.step_k), bf(prob.step_v), 0)
+        store = cache.get_cold_store(0)
+        sel, P = store.retrieve_indices(bf(prob.query), scaling, cfg)
+        o = store.attend(bf(prob.query), scaling, cfg, causal=True)
+        torch.cuda.synchronize()
+        assert store.read_state()[nat.ST_ERROR] == 0
+        outs.append((sel[:, :P].cpu(), o.float().cpu()))
+    assert torch.equal(outs[0][0], outs[1][0])
+    assert torch.equal(outs[0][1], outs[1][1])
+
+
+def test_stage_capacity_is_reported():
+    prob = make_problem(SPEC, seed=4, dtype=torch.bfloat16)
+    cfg, cache = _cache(True, stage_pages=1)
+    _prefill(cache, prob)
+    store = cache.get_cold_store(0)
+    q = torch.randn(SPEC.batch, SPEC.num_query_heads, 1, SPEC.head_dim).to(DEV, torch.bfloat16)
+    store.attend(q, SPEC.head_dim ** -0.5, cfg)
+    torch.cuda.synchronize()
+    assert store.read_state()[nat.ST_ERROR] & 16, "a union with more host pages than staging pages must be flagged"
+
+
+@pytest.mark.parametrize("target", ["hbm", "tiered"])
+def test_save_and_resume(tmp_path, target):
+    prob = make_problem(SPEC, seed=8, dtype=torch.bfloat16)
+    scaling = SPEC.head_dim ** -0.5
+    warm, cont = _steps(2, seed=1), _steps(3, seed=2)
+    cfg, cache = _cache(True)
+    _prefill(cache, prob)
+    _run(cache, cfg, warm, scaling)
+    cache.save(str(tmp_path / "ckpt"))
+    ref = _run(cache, cfg, cont, scaling)
+    cfg2, fresh = _cache(target == "tiered", ring_pages=12, stage_pages=24)
+    fresh.load(str(tmp_path / "ckpt"))
+    s0 = fresh.get_cold_store(0)
+    assert s0.cold_length == cache.get_cold_store(0).cold_length - len(cont)
+    assert fresh._decode_step == 2 and fresh._prefill_complete
+    got = _run(fresh, cfg2, cont, scaling)
+    for i, (x, y) in enumerate(zip(ref, got)):
+        assert torch.equal(x[0], y[0]), f"step {i}: selections differ after resume"
+        assert torch.equal(x[1], y[1]), f"step {i}: outputs differ after resume"
