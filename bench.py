@@ -61,6 +61,10 @@ WORKLOADS = {
     # c3 (Llama-3-8B shape, 64 sequences x 262,144 cold + 4096 hot) one layer: the full
     # model's cold tier (2.2 TB) does not fit one GPU; one layer holds 69 GB
     "c3l": dict(layers=1, hq=32, hkv=8, d=128, cold=262144, hot=4096, top_pages=32, top_p=512, batch=64),
+    # c2 shapes with the pinned host overflow tier: an HBM ring of 131,072 cold tokens per layer
+    # (1/8 of the cold tier), the older pages in host memory, staged per retrieval
+    "c2h": dict(layers=4, hq=8, hkv=1, d=256, cold=1048576, hot=2048, top_pages=64, top_p=1024, ring=131072,
+                stage_pages=1024),
     # c4 (Phi-3.5 MHA chunked prefill, retrieval on every 4096-token chunk) at sampled cold lengths
     "c4": dict(kind="prefill", layers=1, hq=32, hkv=32, d=96, cold=1048576, hot=2048, chunk=4096,
                top_pages=32, top_p=256, segment=2048),
@@ -361,9 +365,14 @@ def main():
     K, W = args.steps, max(3, args.warmup)
     R = max(1, args.roofline_steps)
     n_steps_total = W + 2 * K + R + 8
+    cold_cap = w["cold"] + w["hot"] + n_steps_total + 4 * PAGE
+    tier = {}
+    if "ring" in w:
+        # HBM ring of w["ring"] tokens, everything older in the pinned host tier
+        tier = dict(host_tokens=cold_cap, stage_pages=w["stage_pages"])
+        cold_cap = w["ring"]
     kcfg = KIVConfig(hot_budget=w["hot"], top_p=w["top_p"], page_size=PAGE, top_pages=w["top_pages"],
-                     cold_capacity=w["cold"] + w["hot"] + n_steps_total + 4 * PAGE, hot_slack=4096,
-                     telemetry=False)
+                     cold_capacity=cold_cap, hot_slack=4096, telemetry=False, **tier)
     q_pool, k_pool, v_pool = make_inputs(w, dev, INPUT_POOL)
     t_build = time.perf_counter()
     cache = build_cache(w, dev, kcfg, comm, q_pool[0, :, :, :, 0, :])
@@ -416,6 +425,18 @@ def main():
                 if a in m and b in m:
                     stage_ms[name] = stage_ms.get(name, 0.0) + m[a].elapsed_time(m[b])
             us.setdefault("U", []).append(U)
+            if "ring" in w:
+                # host-tier bytes this layer-step staged: K of the union's host pages
+                # (staged before fine scoring) + V rows of the selected host tokens
+                ws, lay = st._ws[st._cached_ws_key]
+                uni = ws[lay[2]:lay[2] + 4 * lay[8]].view(torch.int32)[:U].cpu()
+                started = -(-st.cold_length // PAGE)
+                thr = started - st._ring_pages
+                sel = st._bufs[("sel", w.get("batch", 1), w["top_p"], torch.int32)][:, :w["top_p"]].cpu()
+                row = w.get("batch", 1) * w["hkv"] * w["d"] * 2
+                host_pages = int((uni < thr).sum())
+                host_rows = int(((sel // PAGE) < thr).sum())
+                us.setdefault("staged", []).append(host_pages * PAGE * row + host_rows * w["hkv"] * w["d"] * 2)
     n_launch = R * L
     fine_avg_ms = fine_ms / n_launch
     fine_bytes_avg = fine_bytes / n_launch
@@ -503,9 +524,9 @@ def main():
                                    f"{w['cold']} cold + {w['hot']} hot tokens per layer, page={PAGE}, "
                                    f"top_pages={w['top_pages']}, top_p={w['top_p']}, batch {w.get('batch', 1)}",
                        "parallelism": f"cold pages sharded over {world} GPU(s)" if world > 1 else "1 GPU",
-                       "l2": "inputs larger than L2 (each step touches 35 layers x ~39 MB)",
-                       "timing": "CUDA graph of one 35-layer step replayed, CUDA events, max over ranks"},
-            "gpu_launches": int(K * L * (7 if world == 1 else 10)),
+                       "l2": f"inputs larger than L2 (each step touches {L} layers x ~39 MB)",
+                       "timing": f"CUDA graph of one {L}-layer step replayed, CUDA events, max over ranks"},
+            "gpu_launches": int(K * L * ((7 if world == 1 else 10) + (3 if "ring" in w else 0))),
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "api": "kiv_b200.decode_graph.DecodeGraph.replay with pinned host inputs/outputs"},
             "roofline": {"bound": "hbm", "kernel": "scores_tc_kernel<bf16, fine> (tcgen05 fine token scoring)",
@@ -522,6 +543,30 @@ def main():
             "clocks": clocks,
             "build_s": t_build,
         }
+    if rank == 0 and "ring" in w:
+        result["config"]["tiers"] = (f"HBM ring of {w['ring']} cold tokens + {w['stage_pages']} staging pages "
+                                     "per layer; older pages in pinned host memory, staged per retrieval")
+        # the step is bound by the host link: staged bytes over the fine stage
+        # (staging kernels + scoring) against a pinned host->device copy measured here
+        hb = torch.empty(256 << 20, dtype=torch.uint8).pin_memory()
+        db = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+        for _ in range(2):
+            db.copy_(hb, non_blocking=True)
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record()
+        for _ in range(5):
+            db.copy_(hb, non_blocking=True)
+        c1.record()
+        torch.cuda.synchronize(dev)
+        link = 5 * (256 << 20) / (c0.elapsed_time(c1) * 1e-3) / 1e9
+        staged = float(np.mean(us["staged"]))
+        ach = staged / (fine_avg_ms * 1e-3) / 1e9
+        result["hbm_roofline_of_fine_kernel"] = result["roofline"]
+        result["roofline"] = {"bound": "host-link", "kernel": "stage_union_kernel + scores_tc_kernel<bf16, fine> "
+                              "(the fine stage of a tiered layer-step)", "achieved": ach, "peak": link, "unit": "GB/s",
+                              "frac": ach / link, "peak_kind": "measured here: pinned host->device copy, 256 MiB",
+                              "traffic": None, "staged_bytes_per_layer_step": staged,
+                              "avg_launch_us": fine_avg_ms * 1e3}
     graph = None
     if world > 1:
         torch.cuda.synchronize(dev)

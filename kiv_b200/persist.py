@@ -66,7 +66,8 @@ def save_store(store, path: str, meta: dict | None = None) -> dict:
         raise NotImplementedError("persistence of page-sharded stores is per rank and not handled here")
     if store._state is None:
         raise RuntimeError("the store holds nothing yet")
-    torch.cuda.synchronize(store.device)
+    if store.device.type == "cuda":
+        torch.cuda.synchronize(store.device)
     ck, cv = _cold_rows(store)
     hk, hv = store.hot_keys().cpu(), store.hot_values().cpu()
     blobs = {"cold_k": ck, "cold_v": cv, "hot_k": hk, "hot_v": hv}
@@ -145,5 +146,6 @@ def load_store(store, path: str, chunk: int = 65536) -> dict:
     if h > 0:
         store.set_hot(_read_block(path, header, "hot_k", (B, H, h, D)).to(store.device),
                       _read_block(path, header, "hot_v", (B, H, h, D)).to(store.device))
-    torch.cuda.synchronize(store.device)
+    if store.device.type == "cuda":
+        torch.cuda.synchronize(store.device)
     return header
