@@ -174,8 +174,8 @@ coarse_topk_kernel(kiv_store st, kiv_query q, Workspace w, float *row_scores, in
   const int row = blockIdx.x;
   const int K = q.top_pages;
   const int rank = st.shard_rank, nsh = st.shard_count;
-  // self_hist: the scorer left no histogram (prefill-shaped scoring); it is
-  // built here from the staged scores
+  // self_hist: the scorer left no histogram (tcgen05 and prefill-shaped
+  // scoring); it is built here from the staged scores
   const uint32_t *pre = self_hist ? nullptr : w.chist + (int64_t)row * SEL_BINS;
   float *src = w.scores + (int64_t)row * w.np_cap;
   float *ls = row_scores ? row_scores + (int64_t)row * K : nullptr;
@@ -206,7 +206,7 @@ coarse_topk_kernel(kiv_store st, kiv_query q, Workspace w, float *row_scores, in
   auto score_at = [&](int64_t i) { return staged ? sscore[i] : __ldcg(src + i); };
   if (!pre && np > 0 && (int64_t)k < np) {
     __syncthreads();
-    for (int64_t i = threadIdx.x; i < np; i += TK_THREADS) hist_add(cs.hist, f2key(score_at(i)) >> 21);
+    for (int64_t i = threadIdx.x; i < np; i += TK_THREADS) atomicAdd(&cs.hist[f2key(score_at(i)) >> 21], 1u);
     __syncthreads();
   }
   if (np > 0 && (int64_t)k >= np) {
@@ -643,15 +643,21 @@ kiv_status launch_coarse(const kiv_store *st, const kiv_query *q, const Workspac
     set_error("prefill-shaped query needs a 16-byte aligned base and strides that are multiples of 8 elements");
     return KIV_ERR_ARG;
   }
+  // the per-row top-k builds its first histogram from the scores it stages,
+  // except after the CUDA-core scorer (which writes the histograms itself)
+  int topk_self_hist = 1;
   if (self_hist) {
     rc = launch_prefill_coarse_scores(st, q, w, s);
   } else if (fine_tc_eligible(st, q)) {
     rc = launch_coarse_score_tc(st, q, w, s);
-  } else switch (st->dtype) {
-    case KIV_DTYPE_F32: rc = dispatch_cs<float>(st, q, w, s); break;
-    case KIV_DTYPE_BF16: rc = dispatch_cs<__nv_bfloat16>(st, q, w, s); break;
-    case KIV_DTYPE_F16: rc = dispatch_cs<__half>(st, q, w, s); break;
-    default: rc = KIV_ERR_UNSUPPORTED;
+  } else {
+    topk_self_hist = 0;
+    switch (st->dtype) {
+      case KIV_DTYPE_F32: rc = dispatch_cs<float>(st, q, w, s); break;
+      case KIV_DTYPE_BF16: rc = dispatch_cs<__nv_bfloat16>(st, q, w, s); break;
+      case KIV_DTYPE_F16: rc = dispatch_cs<__half>(st, q, w, s); break;
+      default: rc = KIV_ERR_UNSUPPORTED;
+    }
   }
   if (rc != KIV_OK) return rc;
   if (q->top_pages > 8192) {
@@ -680,7 +686,7 @@ kiv_status launch_coarse(const kiv_store *st, const kiv_query *q, const Workspac
   const size_t smem = (size_t)cap * 9 + (size_t)fixed;
   cudaFuncSetAttribute(coarse_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   const cudaError_t e = launch_pdl(coarse_topk_kernel, dim3((unsigned)w.R), dim3(TK_THREADS), smem, s, 1, *st, *q,
-                                   w, row_scores, row_pages, cap, scap, self_hist);
+                                   w, row_scores, row_pages, cap, scap, topk_self_hist);
   if (e != cudaSuccess) return cuda_status(e, "coarse_topk");
   return cuda_status(cudaGetLastError(), "coarse");
 }

@@ -39,8 +39,8 @@ struct TcGeom {
 };
 
 // COARSE == false: fine scoring over candidate pages (key per token, max over rows)
-// COARSE == true:  coarse scoring over page summaries (score per row and page,
-//                  plus each row's first radix histogram)
+// COARSE == true:  coarse scoring over page summaries (score per row and page;
+//                  the per-row top-k builds the rows' histograms from them)
 template <bool BF16, bool COARSE>
 __global__ void __launch_bounds__(TC_THREADS, 1)
 scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_query q, Workspace w,
@@ -258,7 +258,6 @@ scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_que
                 const int64_t R_idx = ((int64_t)b * Hq + h) * Q + tq;
                 w.scores[R_idx * w.np_cap + p] = sc;
                 const uint32_t key = f2key(sc);
-                hist_add(w.chist + R_idx * SEL_BINS, key >> 21);
                 kmax = key > kmax ? key : kmax;
                 ksum += sc;
               }
