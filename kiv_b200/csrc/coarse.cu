@@ -206,7 +206,10 @@ coarse_topk_kernel(kiv_store st, kiv_query q, Workspace w, float *row_scores, in
   auto score_at = [&](int64_t i) { return staged ? sscore[i] : __ldcg(src + i); };
   if (!pre && np > 0 && (int64_t)k < np) {
     __syncthreads();
-    for (int64_t i = threadIdx.x; i < np; i += TK_THREADS) atomicAdd(&cs.hist[f2key(score_at(i)) >> 21], 1u);
+    if (staged)
+      for (int64_t i = threadIdx.x; i < np; i += TK_THREADS) atomicAdd(&cs.hist[f2key(sscore[i]) >> 21], 1u);
+    else
+      for (int64_t i = threadIdx.x; i < np; i += TK_THREADS) atomicAdd(&cs.hist[f2key(__ldcg(src + i)) >> 21], 1u);
     __syncthreads();
   }
   if (np > 0 && (int64_t)k >= np) {
@@ -215,9 +218,13 @@ coarse_topk_kernel(kiv_store st, kiv_query q, Workspace w, float *row_scores, in
     find_bin<TK_THREADS>(k, cs, [&](int b) { return cs.hist[b]; });
     const uint32_t b0 = cs.bin, need0 = k - cs.above;
     __syncthreads();
-    const int n = ordered_compact<TK_THREADS>(
-        (int)np, [&](int i) { return f2key(score_at(i)); },
-        [&](uint32_t key) { return (key >> 21) >= b0; }, ckey, cidx, 0, cap, cs);
+    // (one instantiation per source: a load that may come from either memory
+    // is issued as a generic load, slower than a shared-memory one)
+    auto above_bin = [&](uint32_t key) { return (key >> 21) >= b0; };
+    const int n = staged ? ordered_compact<TK_THREADS>((int)np, [&](int i) { return f2key(sscore[i]); }, above_bin,
+                                                       ckey, cidx, 0, cap, cs)
+                         : ordered_compact<TK_THREADS>((int)np, [&](int i) { return f2key(__ldcg(src + i)); },
+                                                       above_bin, ckey, cidx, 0, cap, cs);
     if (n <= cap) {
       select_candidates<TK_THREADS>(ckey, n, b0, need0, bkey, bidx, flag, TK_BND, cs, rs,
                                     [&](int ci, uint32_t pos) {

@@ -331,8 +331,12 @@ fine_select_kernel(kiv_store st, kiv_query q, Workspace w, int32_t *sel, float *
     find_bin<SL_THREADS>((uint32_t)P, cs, [&](int bin) { return cs.hist[bin]; });
     const uint32_t b0 = cs.bin, need0 = (uint32_t)P - cs.above;
     __syncthreads();
-    const int n_r = ordered_compact<SL_THREADS>(
-        n_local, key_at, [&](uint32_t key) { return (key >> 21) >= b0; }, ckey, cidx, 0, cap, cs);
+    // (one instantiation per source: see coarse_topk_kernel)
+    auto above_bin = [&](uint32_t key) { return (key >> 21) >= b0; };
+    const int n_r = kstaged ? ordered_compact<SL_THREADS>(n_local, [&](int i) { return skey[i]; }, above_bin, ckey,
+                                                          cidx, 0, cap, cs)
+                            : ordered_compact<SL_THREADS>(n_local, [&](int i) { return __ldcg(src + i); }, above_bin,
+                                                          ckey, cidx, 0, cap, cs);
     if (threadIdx.x == 0) s_cnt = n_r;
     cl_sync<CL>();
     int total = 0, off = 0;
