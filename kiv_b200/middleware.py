@@ -35,6 +35,47 @@ logger = logging.getLogger(__name__)
 _extend_mask_for_cold = extend_mask_for_cold
 
 
+def invalidate_cold_candidate_caches(cache: Any) -> None:
+    """Drop every cold store's per-step candidate reuse (kiv/server/generation.py:183-197)."""
+    for store in (getattr(cache, "cold_stores", None) or {}).values():
+        store._cached_candidate_k = None
+        store._cached_candidate_v = None
+        store._cached_candidate_idx = None
+        store._cached_step = -1
+
+
+def chunked_reuse_prefill(model: Any, input_ids: torch.Tensor, cache: Any, *, chunk_size: int = 4096) -> torch.Tensor:
+    """Prefill a prompt tail chunk by chunk WITH cold retrieval on every chunk
+    (the reference server's reuse prefill, kiv/server/generation.py:123-180):
+    inside a chunk nothing is evicted (the chunk's later positions still attend
+    to its earlier ones in the hot window) and the per-step candidate caches
+    are dropped first (no decode step advances inside a chunk); between chunks
+    the hot overflow moves to the cold tier.  The attention of every chunk goes
+    through the KIV wrapper, i.e. the prefill-shaped retrieval kernels.
+    Returns the last position's logits ``[B, vocab]``."""
+    total = input_ids.shape[1]
+    last = None
+    prior = getattr(cache, "_prefill_complete", True)
+    try:
+        with torch.no_grad():
+            for a in range(0, total, chunk_size):
+                b = min(a + chunk_size, total)
+                invalidate_cold_candidate_caches(cache)
+                cache._prefill_complete = False
+                out = model(input_ids=input_ids[:, a:b], past_key_values=cache, use_cache=True)
+                if b == total:
+                    last = out.logits[:, -1, :].clone()
+                del out
+                cache._prefill_complete = True
+                if hasattr(cache, "_evict_excess_all_layers"):
+                    cache._evict_excess_all_layers()
+    finally:
+        cache._prefill_complete = prior
+    if last is None:
+        raise RuntimeError("prefill produced no logits")
+    return last
+
+
 def _prefill_logits_kwargs(model: Any, logits_to_keep: int = 1) -> dict[str, int]:
     """``{"logits_to_keep": n}`` when the model's forward accepts it (feature-detected)."""
     try:
@@ -193,6 +234,14 @@ class KIVMiddleware:
             cache._prefill_complete = True
             cache._evict_excess_all_layers()
         return logits
+
+    def chunked_retrieval_prefill(self, input_ids: torch.Tensor, cache: TieredKVCache,
+                                  chunk_size: int = 4096) -> torch.Tensor:
+        """Prefill with cold retrieval on every chunk (see ``chunked_reuse_prefill``);
+        the KIV attention stays installed, so each chunk retrieves from the cold tier."""
+        if not self._installed:
+            raise RuntimeError("Call install() before chunked_retrieval_prefill().")
+        return chunked_reuse_prefill(self.model, input_ids, cache, chunk_size=chunk_size)
 
     def _resolve_attn_impl(self) -> str:
         cfg = self.model.config

@@ -9,7 +9,9 @@ decode the attention hook (``attention_hook.py``) retrieves from those stores.
 
 Same surface and semantics as the reference connector: the KIV knobs come from
 ``vllm_config.extra_config["kiv"]`` (``hot_budget``, ``top_p``, ``page_size``,
-``top_pages``, optional ``topology``); the new rows of a step are the last
+``top_pages``, optional ``topology``; here also ``cold_capacity``,
+``host_tokens``, ``stage_pages`` and ``telemetry`` for the tier placement);
+the new rows of a step are the last
 ``num_prefill_tokens + num_decode_tokens`` token slots of the layer's cache
 tensor, for the ``[2, slots, H, D]`` and ``[2, blocks, block_size, H, D]``
 layouts; the decode step counter advances in ``wait_for_save`` once the first
@@ -85,10 +87,16 @@ class KIVConnector(_connector_base()):
         self._connector_metadata = None
         extra = getattr(vllm_config, "extra_config", None) or {}
         kiv_extra = extra.get("kiv", {}) if isinstance(extra, dict) else {}
+        # the reference's four knobs, plus this build's tier placement (HBM cold
+        # capacity, pinned host overflow tier) for long contexts
         self.kiv_config = KIVConfig(hot_budget=kiv_extra.get("hot_budget", 2048),
                                     top_p=kiv_extra.get("top_p", 256),
                                     page_size=kiv_extra.get("page_size", 128),
-                                    top_pages=kiv_extra.get("top_pages", 32))
+                                    top_pages=kiv_extra.get("top_pages", 32),
+                                    cold_capacity=kiv_extra.get("cold_capacity"),
+                                    host_tokens=kiv_extra.get("host_tokens", 0),
+                                    stage_pages=kiv_extra.get("stage_pages", 1024),
+                                    telemetry=kiv_extra.get("telemetry", True))
         topology_cfg = kiv_extra.get("topology")
         self.topology = (ModelTopology.manual(**topology_cfg) if topology_cfg is not None
                          else detect_topology_from_vllm(vllm_config))

@@ -143,3 +143,39 @@ def test_save_and_resume(tmp_path, target):
     for i, (x, y) in enumerate(zip(ref, got)):
         assert torch.equal(x[0], y[0]), f"step {i}: selections differ after resume"
         assert torch.equal(x[1], y[1]), f"step {i}: outputs differ after resume"
+
+
+def test_tiered_decode_graph_matches_eager():
+    """A captured decode step (spills inside the eviction kernel, staging kernels)
+    replays to the same outputs as the eager steps of an identical cache."""
+    from kiv_b200.decode_graph import DecodeGraph
+
+    prob = make_problem(SPEC, seed=12, dtype=torch.bfloat16)
+    scaling = SPEC.head_dim ** -0.5
+    warm, *steps = _steps(7, seed=3)     # capture runs one real step on the static inputs: `warm`
+    bf = lambda x: x.to(DEV, torch.bfloat16)
+    outs = []
+    for graphed in (False, True):
+        cfg, cache = _cache(True)
+        _prefill(cache, prob)
+        store = cache.get_cold_store(0)
+        if not graphed:
+            for q, k, v in [warm] + steps:
+                cache.update(bf(k), bf(v), 0)
+                outs.append(store.attend(bf(q), scaling, cfg, step=cache._decode_step).float().cpu())
+            outs = outs[1:]
+            continue
+        sq = bf(warm[0])[None].clone()
+        sk = bf(warm[1])[None].clone()
+        sv = bf(warm[2])[None].clone()
+        out = torch.empty(1, SPEC.batch, 1, SPEC.num_query_heads, SPEC.head_dim, dtype=torch.bfloat16, device=DEV)
+        graph = DecodeGraph(cache, [0], scaling, sq, sk, sv, out, max_steps=len(steps) + 2)
+        for i, (q, k, v) in enumerate(steps):
+            sq[0].copy_(bf(q))
+            sk[0].copy_(bf(k))
+            sv[0].copy_(bf(v))
+            graph.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(out[0].float().cpu(), outs[i]), f"graph step {i} differs from eager"
+        assert store.read_state()[nat.ST_ERROR] == 0
+        assert store.cold_length == SPEC.cold_tokens + len(steps) + 1

@@ -235,3 +235,55 @@ def test_key_to_float_roundtrip():
 def test_config_defaults_match_reference():
     c = KIVConfig()
     assert (c.hot_budget, c.top_p, c.page_size, c.top_pages, c.prefetch_stream) == (2048, 256, 128, 32, True)
+
+
+class _Store(SimpleNamespace):
+    pass
+
+
+class _ReuseCache(_FakeCache):
+    def __init__(self):
+        super().__init__()
+        self._prefill_complete = True
+        self.cold_stores = {0: _Store(_cached_candidate_k=1, _cached_candidate_v=1, _cached_candidate_idx=1,
+                                      _cached_step=5)}
+        self.flags_seen, self.excess = [], 0
+
+    def _evict_excess_all_layers(self):
+        self.excess += 1
+
+
+class _ModelSeesFlag(_ModelPlain):
+    def __init__(self, cache):
+        super().__init__()
+        self.cache = cache
+
+    def forward(self, input_ids, past_key_values=None, use_cache=False):
+        st = self.cache.cold_stores[0]
+        self.cache.flags_seen.append((self.cache._prefill_complete, st._cached_step, st._cached_candidate_idx))
+        st._cached_step = 9              # a retrieval inside the chunk sets the reuse key again
+        return super().forward(input_ids, past_key_values, use_cache)
+
+
+def test_chunked_reuse_prefill_semantics():
+    from kiv_b200.middleware import chunked_reuse_prefill
+    cache = _ReuseCache()
+    m = _ModelSeesFlag(cache)
+    logits = chunked_reuse_prefill(m, torch.ones(1, 7, dtype=torch.long), cache, chunk_size=3)
+    assert m.calls == 3 and logits.shape == (1, 3)
+    # every chunk ran without eviction and with the candidate reuse dropped
+    assert cache.flags_seen == [(False, -1, None)] * 3
+    assert cache.excess == 3 and cache._prefill_complete is True
+
+
+def test_chunked_reuse_prefill_restores_flag_on_error():
+    from kiv_b200.middleware import chunked_reuse_prefill
+
+    class Boom(_ModelPlain):
+        def forward(self, *a, **k):
+            raise RuntimeError("boom")
+    cache = _ReuseCache()
+    cache._prefill_complete = False
+    with pytest.raises(RuntimeError):
+        chunked_reuse_prefill(Boom(), torch.ones(1, 4, dtype=torch.long), cache, chunk_size=2)
+    assert cache._prefill_complete is False

@@ -317,3 +317,11 @@ def test_install_merges_hot_and_cold_and_uninstall_restores():
 def test_install_without_layers_is_inert():
     c = KIVConnector(_vllm_config(), role=1)
     assert hook.install_attention_hook(torch.nn.Module(), c) == {}
+
+
+def test_connector_passes_tier_knobs():
+    c = KIVConnector(_vllm_config(cold_capacity=131072, host_tokens=1 << 20, stage_pages=512, telemetry=False), role=1)
+    cfg = c.kiv_config
+    assert (cfg.cold_capacity, cfg.host_tokens, cfg.stage_pages, cfg.telemetry) == (131072, 1 << 20, 512, False)
+    with pytest.raises(ValueError):
+        KIVConnector(_vllm_config(host_tokens=4096), role=1)   # a host tier needs the HBM ring size
