@@ -285,7 +285,9 @@ scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_que
         if (tok < n_tok) {
           const uint32_t key = f2key(m);
           w.agg[(int64_t)b * w.c_cap + u * S + tok] = key;
-          hist_add(hist, key >> 21);
+          // shared-memory atomic: the warp's keys fall in a few bins, which
+          // costs far less here than aggregating the lanes with a match
+          atomicAdd(&hist[key >> 21], 1u);
           kmax = key > kmax ? key : kmax;
           ksum += m;
         }
