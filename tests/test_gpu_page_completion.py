@@ -1,14 +1,13 @@
 """Decode steps that finalize a page, on the tensor-core (tcgen05) scoring path.
 
-The coarse scorer reads the page summaries it can before its dependency on
-the step's eviction is resolved (the summaries of pages finalized earlier do
-not change), and reads again any tile that holds a page the eviction
-finalized meanwhile.  Here the page that completes during the steps is a
-strong match for the query, so a stale or half-written summary of it would
-drop it from the coarse union: at every step the union and the token set must
-equal the oracle's (ties within 1e-6), and the completed page must be
-selected once it is final.  Both the eager steps and the captured decode
-graph are checked.
+The eviction kernel of a decode step writes the summary of a page that the
+step completes, and the coarse scorer launched right after it (programmatic
+dependent launch) must score that page from the new summary.  Here the page
+that completes during the steps is a strong match for the query, so a stale
+or half-written summary of it would drop it from the coarse union: at every
+step the union and the token set must equal the oracle's (ties within 1e-6),
+and the completed page must be selected once it is final.  Both the eager
+steps and the captured decode graph are checked.
 """
 
 import numpy as np
