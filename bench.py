@@ -52,7 +52,10 @@ METRIC = "decode steps/s per layer at 1M cold ctx (1/2/4/8 GPU); % of HBM roofli
 UNIT = "layer-steps/s"
 
 WORKLOADS = {
-    # name: layers, Hq, Hkv, D, cold, hot, top_pages, top_p
+    # name: layers, Hq, Hkv, D, cold, hot, top_pages, top_p (bf16 unless "dtype" says otherwise)
+    # c0 (TinyLlama GQA attention, fp32, the reference's CPU-runnable case): 4 identical
+    # independent layers so that one step (~240 MB) exceeds L2; metric per layer-step
+    "c0": dict(layers=4, hq=32, hkv=4, d=64, cold=65536, hot=2048, top_pages=32, top_p=256, dtype="f32"),
     "c2": dict(layers=35, hq=8, hkv=1, d=256, cold=1048576, hot=2048, top_pages=64, top_p=1024),
     "c1": dict(layers=28, hq=28, hkv=4, d=128, cold=131072, hot=2048, top_pages=32, top_p=512),
     "tiny": dict(layers=3, hq=8, hkv=1, d=256, cold=65536, hot=2048, top_pages=64, top_p=1024),
@@ -175,6 +178,15 @@ class ClockSampler:
                 "samples": len(rows)}
 
 
+def wdtype(w):
+    """Storage dtype of a workload (bf16 unless the workload says fp32)."""
+    return torch.float32 if w.get("dtype") == "f32" else torch.bfloat16
+
+
+def welem(w):
+    return 4 if w.get("dtype") == "f32" else 2
+
+
 def step_algorithmic_bytes(w, U, partial, e=2):
     """Bytes one layer-step must move (each element read or written once)."""
     row = w.get("batch", 1) * w["hkv"] * w["d"] * e
@@ -225,7 +237,7 @@ def build_cache(w, dev, kcfg, comm, queries0):
                 s0, s1 = max(lo, a) - a, min(hi, a + n) - a
                 k[:, :, s0:s1] = 2.0 * qhat[:, :, None, :] + 0.3 * torch.randn(
                     B, w["hkv"], s1 - s0, d, generator=gen, device=dev)
-            cache.update(k.to(torch.bfloat16), v.to(torch.bfloat16), li)
+            cache.update(k.to(wdtype(w)), v.to(wdtype(w)), li)
             cache._evict_to_cap(w["hot"])
         del k, v
     cache._prefill_complete = True
@@ -239,10 +251,11 @@ def make_inputs(w, dev, n, seed=7):
     g.manual_seed(seed)
     L, d = w["layers"], w["d"]
     B = w.get("batch", 1)
-    q = torch.randn(n, L, B, w["hq"], 1, d, generator=g, device=dev).to(torch.bfloat16)
+    dt = wdtype(w)
+    q = torch.randn(n, L, B, w["hq"], 1, d, generator=g, device=dev).to(dt)
     cent = torch.randn(L, B, w["hkv"], 1, d, generator=g, device=dev) / math.sqrt(64.0)
-    k = (cent[None] + 0.3 * torch.randn(n, L, B, w["hkv"], 1, d, generator=g, device=dev)).to(torch.bfloat16)
-    v = torch.randn(n, L, B, w["hkv"], 1, d, generator=g, device=dev).to(torch.bfloat16)
+    k = (cent[None] + 0.3 * torch.randn(n, L, B, w["hkv"], 1, d, generator=g, device=dev)).to(dt)
+    v = torch.randn(n, L, B, w["hkv"], 1, d, generator=g, device=dev).to(dt)
     return q, k, v
 
 
@@ -260,15 +273,16 @@ class StageRecorder:
 
 # ----------------------------------------------------------- CPU baseline
 def cpu_oracle_layer(w):
-    """One full-size layer of the workload in the CPU oracle port (bf16 values)."""
+    """One full-size layer of the workload in the CPU oracle port (the workload's storage values)."""
     from kiv_b200.synthetic import SynthSpec, make_problem
     from oracle.kiv_oracle import OracleLayer, OracleStore
 
     torch.set_num_threads(os.cpu_count() or 1)
     spec = SynthSpec(batch=1, num_query_heads=w["hq"], num_kv_heads=w["hkv"], head_dim=w["d"],
                      cold_tokens=w["cold"], hot_budget=w["hot"], page_size=PAGE, segment=SEGMENT)
-    prob = make_problem(spec, seed=0, dtype=torch.bfloat16)
-    store = OracleStore(1, w["hkv"], w["d"], spec.groups, PAGE, "bf16", compute=np.float32)
+    prob = make_problem(spec, seed=0, dtype=wdtype(w))
+    store = OracleStore(1, w["hkv"], w["d"], spec.groups, PAGE, "f32" if w.get("dtype") == "f32" else "bf16",
+                        compute=np.float32)
     layer = OracleLayer(store, w["hot"])
     layer.update(prob.prefill_k.float().numpy(), prob.prefill_v.float().numpy())
     layer.mark_prefill_complete()
@@ -319,11 +333,12 @@ def run_reference(args, w, rank, world):
     steps = min(args.steps, max(3, int(150.0 * rate_probe)))
     rate, n, el, threads = cpu_oracle_rate(w, layer, max_steps=steps)
     sample = (f"1 of {w['layers']} layers at full size ({w['cold']} cold tokens), {n} layer-steps "
-              f"(numpy oracle port, fp32 math on bf16 values, {threads} threads, {cpu_model()})")
+              f"(numpy oracle port, fp32 math on {w.get('dtype', 'bf16')} values, {threads} threads, "
+              f"{cpu_model()})")
     line = {
         "metric": METRIC, "value": rate, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1000.0 / rate, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "scaling": "strong", "vs_baseline": None, "dtype": w.get("dtype", "bf16"), "data": "synthetic",
         "config": {"workload": f"{args.workload}: {w['layers']} layers, Hq={w['hq']} Hkv={w['hkv']} "
                                f"D={w['d']}, {w['cold']} cold + {w['hot']} hot, top_pages={w['top_pages']}, "
                                f"top_p={w['top_p']}, page={PAGE}", "parallelism": "cpu"},
@@ -416,7 +431,7 @@ def main():
             m = dict(rec[li].marks)
             t_fine = m["fine_score_begin"].elapsed_time(m["fine_score_end"])
             fine_ms += t_fine
-            fine_bytes += w.get("batch", 1) * (U * PAGE + own_partial) * w["hkv"] * w["d"] * 2
+            fine_bytes += w.get("batch", 1) * (U * PAGE + own_partial) * w["hkv"] * w["d"] * welem(w)
             for a, b, name in (("update_begin", "coarse_begin", "update"),
                                ("coarse_begin", "fine_score_begin", "coarse"),
                                ("fine_score_begin", "fine_score_end", "fine_score"),
@@ -448,7 +463,7 @@ def main():
     static_q = torch.empty_like(q_pool[0])
     static_k = torch.empty_like(k_pool[0])
     static_v = torch.empty_like(v_pool[0])
-    out = torch.empty(L, w.get("batch", 1), 1, w["hq"], w["d"], dtype=torch.bfloat16, device=dev)
+    out = torch.empty(L, w.get("batch", 1), 1, w["hq"], w["d"], dtype=wdtype(w), device=dev)
     i0 = (W + R) % INPUT_POOL
     static_q.copy_(q_pool[i0]); static_k.copy_(k_pool[i0]); static_v.copy_(v_pool[i0])
     graph = DecodeGraph(cache, layers, scaling, static_q, static_k, static_v, out, max_steps=2 * K + 4)
@@ -506,30 +521,34 @@ def main():
     barrier()
     ms_e2e = max_over_ranks(e2.elapsed_time(e3))
     e2e = L * K / (ms_e2e * 1e-3)
-    h2d = (static_q.numel() + static_k.numel() + static_v.numel()) * 2
-    d2h = out.numel() * 2
+    h2d = (static_q.numel() + static_k.numel() + static_v.numel()) * welem(w)
+    d2h = out.numel() * welem(w)
     assert torch.isfinite(hout.float()).all(), "non-finite attention output"
     err_words = [st.read_state()[nat.ST_ERROR] for st in stores]
     assert not any(err_words), f"kernel error bits set: {err_words}"
 
     result = None
     if rank == 0:
-        step_bytes = step_algorithmic_bytes(w, U_mean, 1)
+        step_bytes = step_algorithmic_bytes(w, U_mean, 1, e=welem(w))
+        f32 = w.get("dtype") == "f32"
         layer_step_s = ms * 1e-3 / (L * K)
         result = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
             "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "vs_baseline": None, "dtype": w.get("dtype", "bf16"), "data": "synthetic",
             "config": {"workload": f"{args.workload}: {L} layers, Hq={w['hq']} Hkv={w['hkv']} D={w['d']}, "
                                    f"{w['cold']} cold + {w['hot']} hot tokens per layer, page={PAGE}, "
                                    f"top_pages={w['top_pages']}, top_p={w['top_p']}, batch {w.get('batch', 1)}",
                        "parallelism": f"cold pages sharded over {world} GPU(s)" if world > 1 else "1 GPU",
-                       "l2": f"inputs larger than L2 (each step touches {L} layers x ~39 MB)",
+                       "l2": f"inputs larger than L2 (each step touches {L} layers x ~{step_bytes / 1e6:.0f} MB)",
                        "timing": f"CUDA graph of one {L}-layer step replayed, CUDA events, max over ranks"},
-            "gpu_launches": int(K * L * ((7 if world == 1 else 10) + (3 if "ring" in w else 0))),
+            # per layer-step: 7 kernels (8 on the CUDA-core fp32 path, whose union is its own kernel)
+            "gpu_launches": int(K * L * ((7 if world == 1 else 10) + (1 if f32 else 0) + (3 if "ring" in w else 0))),
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "api": "kiv_b200.decode_graph.DecodeGraph.replay with pinned host inputs/outputs"},
-            "roofline": {"bound": "hbm", "kernel": "scores_tc_kernel<bf16, fine> (tcgen05 fine token scoring)",
+            "roofline": {"bound": "hbm",
+                         "kernel": ("fine_scores_kernel<float> (CUDA-core fine token scoring)" if f32 else
+                                    "scores_tc_kernel<bf16, fine> (tcgen05 fine token scoring)"),
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_kind": peak_kind, "traffic": committed_traffic(args.workload, fine_bytes_avg),
                          "algorithmic_bytes_per_launch": fine_bytes_avg,
@@ -577,7 +596,7 @@ def main():
         result["cpu_baseline"] = {
             "value": rate, "unit": UNIT, "cores": threads, "kind": "port",
             "sample": f"1 of {L} layers at full size, {n} layer-steps in {el:.1f} s "
-                      f"(numpy oracle port, fp32 math on bf16 values, {cpu_model()})"}
+                      f"(numpy oracle port, fp32 math on {w.get('dtype', 'bf16')} values, {cpu_model()})"}
     if rank == 0:
         print(json.dumps(result), flush=True)
     if world > 1:
