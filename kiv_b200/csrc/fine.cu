@@ -67,6 +67,7 @@ fine_scores_kernel(kiv_store st, kiv_query q, Workspace w, int tr, int stage_q) 
   extern __shared__ __align__(128) uint8_t fs_smem[];
   __shared__ uint64_t bars[FS_STAGES];
   __shared__ int s_fail;
+  __shared__ uint32_t s_hist[SEL_BINS];   // first-pass histogram of the batch row being processed
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane % LPR, grp = lane / LPR;
   constexpr int GPW = 32 / LPR;
@@ -97,6 +98,7 @@ fine_scores_kernel(kiv_store st, kiv_query q, Workspace w, int tr, int stage_q) 
     s_fail = 0;
   }
   for (int i = threadIdx.x; i < tr; i += FS_THREADS) mx[i] = -INFINITY;
+  for (int i = threadIdx.x; i < SEL_BINS; i += FS_THREADS) s_hist[i] = 0;
   __syncthreads();
 
   struct Unit { int b; int64_t u; int rb; int rows; };
@@ -131,7 +133,10 @@ fine_scores_kernel(kiv_store st, kiv_query q, Workspace w, int tr, int stage_q) 
   }
 
   int staged_b = -1;
-  // running stats of the batch row being processed (flushed when it changes)
+  // running stats and histogram of the batch row being processed (flushed
+  // when it changes and at the end; every thread calls this, at the same
+  // points).  The histogram collects in shared memory with plain atomics
+  // and reaches the row's global histogram once, non-zero bins only.
   int stat_b = -1;
   uint32_t kmax = 0;
   float ksum = 0.f;
@@ -147,6 +152,16 @@ fine_scores_kernel(kiv_store st, kiv_query q, Workspace w, int tr, int stage_q) 
     }
     kmax = 0;
     ksum = 0.f;
+    __syncthreads();
+    uint32_t *hb = w.fhist + (int64_t)stat_b * SEL_BINS;
+    for (int i = threadIdx.x; i < SEL_BINS; i += FS_THREADS) {
+      const uint32_t c = s_hist[i];
+      if (c) {
+        atomicAdd(&hb[i], c);
+        s_hist[i] = 0;
+      }
+    }
+    __syncthreads();
   };
   for (int64_t t = 0; t < my_tiles; ++t) {
     const Unit x = unit_of(t);
@@ -218,12 +233,11 @@ fine_scores_kernel(kiv_store st, kiv_query q, Workspace w, int tr, int stage_q) 
         stat_b = x.b;
       }
       uint32_t *dst = w.agg + (int64_t)x.b * w.c_cap + x.u * S + (int64_t)x.rb * tr;
-      uint32_t *hb = w.fhist + (int64_t)x.b * SEL_BINS;
       for (int i = threadIdx.x; i < tr; i += FS_THREADS) {
         if (i < x.rows) {
           const uint32_t key = f2key(mx[i]);
           dst[i] = key;
-          hist_add(hb, key >> 21);
+          atomicAdd(&s_hist[key >> 21], 1u);
           kmax = key > kmax ? key : kmax;
           ksum += mx[i];
         }
