@@ -726,8 +726,10 @@ combine_kernel(const float *part, int64_t row_stride, int64_t pstride, int n, in
   griddep_wait();
   constexpr int C4 = CB_COLS / 4;              // float4 columns per chunk
   constexpr int NG = CB_THREADS / C4;          // partial groups
-  __shared__ float4 s_acc[NG][C4];
-  __shared__ float s_m[NG][C4], s_l[NG][C4];
+  constexpr int NW = CB_THREADS / 32;          // warps (each merges 32 / C4 groups)
+  static_assert(32 % C4 == 0, "a warp holds whole groups");
+  __shared__ float4 s_acc[NW][C4];
+  __shared__ float s_m[NW][C4], s_l[NW][C4];
   const int nch = (D + CB_COLS - 1) / CB_COLS;
   const int64_t row = blockIdx.x / nch;        // (b*Hq + h)*Q + t
   const int chunk = blockIdx.x % nch;
@@ -788,9 +790,34 @@ combine_kernel(const float *part, int64_t row_stride, int64_t pstride, int n, in
     l = l * a + li * bi;
     m = mn;
   }
-  s_acc[grp][c4] = acc;
-  s_m[grp][c4] = m;
-  s_l[grp][c4] = l;
+  // the warp's groups of this column quad (lanes c4, c4 + C4, ...) merge by
+  // shuffles in a fixed tree; both lanes of a pair compute the same
+  // (commutative) result, so every lane ends with the warp's merge
+#pragma unroll
+  for (int off = C4; off < 32; off <<= 1) {
+    const float mo = __shfl_xor_sync(KIV_FULL_MASK, m, off);
+    const float lo = __shfl_xor_sync(KIV_FULL_MASK, l, off);
+    float4 ao;
+    ao.x = __shfl_xor_sync(KIV_FULL_MASK, acc.x, off);
+    ao.y = __shfl_xor_sync(KIV_FULL_MASK, acc.y, off);
+    ao.z = __shfl_xor_sync(KIV_FULL_MASK, acc.z, off);
+    ao.w = __shfl_xor_sync(KIV_FULL_MASK, acc.w, off);
+    const float mn = fmaxf(m, mo);
+    const float a = m == -INFINITY ? 0.f : __expf(m - mn);
+    const float b = mo == -INFINITY ? 0.f : __expf(mo - mn);
+    acc.x = acc.x * a + ao.x * b;
+    acc.y = acc.y * a + ao.y * b;
+    acc.z = acc.z * a + ao.z * b;
+    acc.w = acc.w * a + ao.w * b;
+    l = l * a + lo * b;
+    m = mn;
+  }
+  const int warp = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) < C4) {
+    s_acc[warp][c4] = acc;
+    s_m[warp][c4] = m;
+    s_l[warp][c4] = l;
+  }
   if (X && !ok)
     atomicOr(reinterpret_cast<unsigned long long *>(state + KIV_ST_ERROR),
              (unsigned long long)KIV_ERRBIT_WAIT_TIMEOUT);
@@ -799,11 +826,11 @@ combine_kernel(const float *part, int64_t row_stride, int64_t pstride, int n, in
   if (grp != 0) return;
   float M = -INFINITY;
 #pragma unroll
-  for (int gi = 0; gi < NG; ++gi) M = fmaxf(M, s_m[gi][c4]);
+  for (int gi = 0; gi < NW; ++gi) M = fmaxf(M, s_m[gi][c4]);
   float L = 0.f;
   float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-  for (int gi = 0; gi < NG; ++gi) {
+  for (int gi = 0; gi < NW; ++gi) {
     const float mg = s_m[gi][c4];
     const float w = mg == -INFINITY ? 0.f : __expf(mg - M);
     const float4 u = s_acc[gi][c4];
