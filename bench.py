@@ -13,8 +13,10 @@ summaries), coarse page scoring + top-k + union, fine token scoring + top-P,
 attention over [selected cold ; hot].  The metric is layer-steps per second
 (= decode steps/s per layer).  With N GPUs the cold pages of every layer are
 sharded over the ranks (page p on rank p % N) and one sequence's step is
-computed by all of them (strong scaling); per layer-step three small NCCL
-all-gathers exchange coarse candidates, fine candidates and attention partials.
+computed by all of them (strong scaling); per layer-step the ranks exchange
+coarse candidates, fine candidates and attention partials through peer memory
+over NVLink (the merge kernels store into every rank's exchange arena and wait
+on flagged words there; no NCCL call is on the decode path).
 
 Lines printed by rank 0 (one JSON object):
 * value: device-resident inputs, the step captured once in a CUDA graph and

@@ -255,9 +255,12 @@ KIV_API kiv_status kiv_retrieve_attend(const kiv_store *st, const kiv_query *q, 
  * that may not allocate device memory while they serve (engines that own all
  * memory through their own pool, plugin hosts without an allocator hook).
  * Shapes needing more scratch are rejected with KIV_ERR_CAPACITY.  All calls
- * on a device share the array: calls that overlap on the GPU race.  The first
- * call on a device looks up the array's address; make it before any stream
- * capture.  No counterpart in the reference (it has no C interface).
+ * on a device share the array, which keeps the last call's contents: every
+ * call first clears, on its stream, the part that must start at zero, so a
+ * call of another shape or a failed call before it does not matter.  Calls
+ * that overlap on the GPU race on the array.  The first call on a device
+ * looks up the array's address; make it before any stream capture.
+ * No counterpart in the reference (it has no C interface).
  */
 #define KIV_NOALLOC_SCRATCH_BYTES (32u << 20)
 KIV_API kiv_status kiv_retrieve_attend_noalloc(const kiv_store *st, const kiv_query *q,
@@ -274,10 +277,11 @@ KIV_API kiv_status kiv_retrieve_attend_noalloc(const kiv_store *st, const kiv_qu
  * KIV_IPC_HANDLE_BYTES), the ranks swap the handles over any host channel,
  * and each rank maps the others' arenas with kiv_peer_open.  The
  * *_exchange_merge calls then store this rank's lists straight into every
- * rank's arena over NVLink, raise a per-source counter there (release
- * ordering at system scope), wait for every rank's lists (acquire; each wait
- * is bounded, a timeout sets KIV_ERRBIT_WAIT_TIMEOUT in the state) and merge,
- * all in one kernel.  Every rank must make the same sequence of these calls
+ * rank's arena over NVLink as 64-bit words that carry the exchange's flag
+ * next to each value (one single-copy atomic store per value), wait for
+ * every rank's words to carry the flag (each wait bounded by wait_cycles; a
+ * timeout sets KIV_ERRBIT_WAIT_TIMEOUT in the state) and merge, all in one
+ * kernel.  Every rank must make the same sequence of these calls
  * with the same shapes.  An arena serves one (store shape, query shape);
  * stores of the same shape may share it when their calls are stream-ordered.
  */
@@ -288,6 +292,12 @@ typedef struct kiv_exchange {
   int32_t rank;                   /* this rank (== kiv_store.shard_rank) */
   void *arena[KIV_MAX_PEERS];     /* every rank's arena as mapped in this process */
   int64_t arena_bytes;            /* size of every arena */
+  int64_t wait_cycles;            /* bound of every wait on a peer, in SM clock cycles;
+                                     0: 2^31 (about 1.1 s at 1965 MHz).  A wait that runs
+                                     out sets KIV_ERRBIT_WAIT_TIMEOUT and the merge writes
+                                     no output (the coarse merge marks no page, the fine
+                                     merge selects nothing, the attention merge leaves
+                                     `out` as it was) */
 } kiv_exchange;
 
 KIV_API size_t kiv_exchange_bytes(const kiv_store *st, const kiv_query *q, int32_t world);

@@ -59,7 +59,8 @@ IPC_HANDLE_BYTES = 64
 
 
 class ExchangeDesc(ctypes.Structure):
-    _fields_ = [("world", c_i32), ("rank", c_i32), ("arena", c_vp * MAX_PEERS), ("arena_bytes", c_i64)]
+    _fields_ = [("world", c_i32), ("rank", c_i32), ("arena", c_vp * MAX_PEERS), ("arena_bytes", c_i64),
+                ("wait_cycles", c_i64)]
 
 
 P = ctypes.POINTER

@@ -410,6 +410,11 @@ static kiv_status check_exchange(const kiv_store *st, const kiv_query *q, const 
   }
   a.off = L.off[t];
   a.par_bytes = L.par[t];
+  if (x->wait_cycles < 0) {
+    set_error("negative exchange wait bound");
+    return KIV_ERR_ARG;
+  }
+  a.budget = x->wait_cycles > 0 ? x->wait_cycles : kiv::X_DEFAULT_WAIT_CYCLES;
   return KIV_OK;
 }
 

@@ -721,9 +721,11 @@ template <typename T, bool X, int CB_COLS>
 __global__ void __launch_bounds__(CB_THREADS)
 combine_kernel(const float *part, int64_t row_stride, int64_t pstride, int n, int D, int Hq, int Q,
                T *final_out, float *merged, XArgs x, const float *mine, int64_t rows, int64_t *state) {
-  // the epoch was advanced by this type's previous exchange, kernels ago
-  const unsigned long long e = X ? x_epoch(x, X_ATTN) : 0ull;
+  // the epoch was advanced by this type's previous exchange; read it after
+  // the dependency wait, which also covers a merge of the same type right
+  // before this one in the stream
   griddep_wait();
+  const unsigned long long e = X ? x_epoch(x, X_ATTN) : 0ull;
   constexpr int C4 = CB_COLS / 4;              // float4 columns per chunk
   constexpr int NG = CB_THREADS / C4;          // partial groups
   constexpr int NW = CB_THREADS / 32;          // warps (each merges 32 / C4 groups)
@@ -768,12 +770,12 @@ combine_kernel(const float *part, int64_t row_stride, int64_t pstride, int n, in
       const unsigned long long w0 = ld_relaxed_sys(wi + colc), w1 = ld_relaxed_sys(wi + colc + 1);
       const unsigned long long w2 = ld_relaxed_sys(wi + colc + 2), w3 = ld_relaxed_sys(wi + colc + 3);
       const unsigned long long wm = ld_relaxed_sys(wi + D), wl = ld_relaxed_sys(wi + D + 1);
-      v.x = __uint_as_float(ll_check(wi + colc, w0, flag, ok));
-      v.y = __uint_as_float(ll_check(wi + colc + 1, w1, flag, ok));
-      v.z = __uint_as_float(ll_check(wi + colc + 2, w2, flag, ok));
-      v.w = __uint_as_float(ll_check(wi + colc + 3, w3, flag, ok));
-      mi = __uint_as_float(ll_check(wi + D, wm, flag, ok));
-      li = __uint_as_float(ll_check(wi + D + 1, wl, flag, ok));
+      v.x = __uint_as_float(ll_check(wi + colc, w0, flag, ok, x.budget));
+      v.y = __uint_as_float(ll_check(wi + colc + 1, w1, flag, ok, x.budget));
+      v.z = __uint_as_float(ll_check(wi + colc + 2, w2, flag, ok, x.budget));
+      v.w = __uint_as_float(ll_check(wi + colc + 3, w3, flag, ok, x.budget));
+      mi = __uint_as_float(ll_check(wi + D, wm, flag, ok, x.budget));
+      li = __uint_as_float(ll_check(wi + D + 1, wl, flag, ok, x.budget));
     } else {
       const float *pi = p + (int64_t)i * pstride * Dp;
       v = __ldcg(reinterpret_cast<const float4 *>(pi + colc));
@@ -821,9 +823,10 @@ combine_kernel(const float *part, int64_t row_stride, int64_t pstride, int n, in
   if (X && !ok)
     atomicOr(reinterpret_cast<unsigned long long *>(state + KIV_ST_ERROR),
              (unsigned long long)KIV_ERRBIT_WAIT_TIMEOUT);
-  __syncthreads();
+  // a wait that gave up leaves some inputs unread: write no output
+  const bool failed = __syncthreads_or(X && !ok) != 0;
   if (X) x_advance(x, X_ATTN, e);   // every CTA has read its inputs from the arena
-  if (grp != 0) return;
+  if (failed || grp != 0) return;
   float M = -INFINITY;
 #pragma unroll
   for (int gi = 0; gi < NW; ++gi) M = fmaxf(M, s_m[gi][c4]);

@@ -500,9 +500,11 @@ template <bool X>
 __global__ void __launch_bounds__(CM_THREADS)
 coarse_merge_kernel(kiv_store st, kiv_query q, Workspace w, const float *ls, const int32_t *lp, int32_t n,
                     XArgs x, const float *mine_s, const int32_t *mine_p) {
-  // the epoch was advanced by this type's previous exchange, kernels ago
-  const unsigned long long e = X ? x_epoch(x, X_COARSE) : 0ull;
+  // the epoch was advanced by this type's previous exchange; read it after
+  // the dependency wait, which also covers a merge of the same type right
+  // before this one in the stream
   griddep_wait();
+  const unsigned long long e = X ? x_epoch(x, X_COARSE) : 0ull;
   extern __shared__ uint4 dyn_smem[];
   __shared__ SelectSmem<CM_THREADS> sm;
   const int S = st.page_size;
@@ -550,8 +552,8 @@ coarse_merge_kernel(kiv_store st, kiv_query q, Workspace w, const float *ls, con
       int32_t pg;
       float sc;
       if (X) {
-        sc = __uint_as_float(ll_check(mine + 2 * offs[k], wv[2 * k], flag, ok));
-        pg = (int32_t)ll_check(mine + 2 * offs[k] + 1, wv[2 * k + 1], flag, ok);
+        sc = __uint_as_float(ll_check(mine + 2 * offs[k], wv[2 * k], flag, ok, x.budget));
+        pg = (int32_t)ll_check(mine + 2 * offs[k] + 1, wv[2 * k + 1], flag, ok, x.budget);
       } else {
         sc = __ldcg(ls + offs[k]);
         pg = __ldcg(lp + offs[k]);
@@ -563,7 +565,11 @@ coarse_merge_kernel(kiv_store st, kiv_query q, Workspace w, const float *ls, con
   if (X && !ok)
     atomicOr(reinterpret_cast<unsigned long long *>(st.state + KIV_ST_ERROR),
              (unsigned long long)KIV_ERRBIT_WAIT_TIMEOUT);
-  __syncthreads();
+  // a wait that gave up leaves some lists unread: mark no page
+  if (__syncthreads_or(X && !ok)) {
+    if (X) x_advance(x, X_COARSE, e);
+    return;
+  }
   const uint32_t k = (uint32_t)(K < np_global ? (int64_t)K : np_global);
   auto mark = [&](int32_t id) {
     if ((id % st.shard_count) == st.shard_rank) {

@@ -30,7 +30,11 @@ struct XArgs {
   char *arena[KIV_MAX_PEERS];
   int64_t off;        // byte offset of this type's region (parity 0)
   int64_t par_bytes;  // bytes of one parity of the region
+  int64_t budget;     // SM clock cycles a wait may spin before it gives up
 };
+
+// default bound of every wait: 2^31 cycles, about 1.1 s at 1965 MHz
+constexpr int64_t X_DEFAULT_WAIT_CYCLES = 1ll << 31;
 
 // byte offsets of the three regions and the arena size for per-rank payloads
 // (bytes of one rank's lists) cb, fb, ab
@@ -72,16 +76,16 @@ __device__ __forceinline__ void ll_store(unsigned long long *p, uint32_t data, u
   asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 // v was loaded from p: if its flag is not `flag` yet, reload until it is (a
-// bounded wait, after which ok turns false and later checks stop waiting);
-// returns the value.  Callers load a batch of words first (independent loads,
-// one round trip) and check them afterwards.
+// wait bounded by `budget` cycles, after which ok turns false and later
+// checks stop waiting); returns the value.  Callers load a batch of words
+// first (independent loads, one round trip) and check them afterwards.
 __device__ __forceinline__ uint32_t ll_check(const unsigned long long *p, unsigned long long v, uint32_t flag,
-                                             bool &ok) {
+                                             bool &ok, int64_t budget) {
   if ((uint32_t)(v >> 32) != flag && ok) {
     const long long t0 = clock64();
     do {
       v = ld_relaxed_sys(p);
-      if (clock64() - t0 > (1ll << 31)) {
+      if (clock64() - t0 > budget) {
         ok = false;
         break;
       }

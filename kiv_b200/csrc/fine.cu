@@ -491,9 +491,11 @@ __global__ void __launch_bounds__(FM_THREADS)
 fine_merge_kernel(kiv_store st, kiv_query q, Workspace w, const float *ls, const int32_t *lt,
                   int32_t n, int32_t *sel, int32_t *sel_local, XArgs x, const float *mine_s,
                   const int32_t *mine_t) {
-  // the epoch was advanced by this type's previous exchange, kernels ago
-  const unsigned long long e = X ? x_epoch(x, X_FINE) : 0ull;
+  // the epoch was advanced by this type's previous exchange; read it after
+  // the dependency wait, which also covers a merge of the same type right
+  // before this one in the stream
   griddep_wait();
+  const unsigned long long e = X ? x_epoch(x, X_FINE) : 0ull;
   extern __shared__ uint4 fm_dyn[];
   __shared__ SelectSmem<FM_THREADS> sm;
   __shared__ typename cub::BlockScan<int, FM_THREADS>::TempStorage fm_scan;
@@ -544,8 +546,8 @@ fine_merge_kernel(kiv_store st, kiv_query q, Workspace w, const float *ls, const
       int32_t id;
       float sc;
       if (X) {
-        id = (int32_t)ll_check(mine + 2 * offs[k], wv[2 * k], flag, ok);
-        sc = __uint_as_float(ll_check(mine + 2 * offs[k] + 1, wv[2 * k + 1], flag, ok));
+        id = (int32_t)ll_check(mine + 2 * offs[k], wv[2 * k], flag, ok, x.budget);
+        sc = __uint_as_float(ll_check(mine + 2 * offs[k] + 1, wv[2 * k + 1], flag, ok, x.budget));
       } else {
         id = __ldcg(lt + offs[k]);
         sc = __ldcg(ls + offs[k]);
@@ -558,7 +560,18 @@ fine_merge_kernel(kiv_store st, kiv_query q, Workspace w, const float *ls, const
     atomicOr(reinterpret_cast<unsigned long long *>(st.state + KIV_ST_ERROR),
              (unsigned long long)KIV_ERRBIT_WAIT_TIMEOUT);
   if (threadIdx.x < 64) s_valid[threadIdx.x] = 0;
-  __syncthreads();
+  // a wait that gave up leaves some lists unread: select nothing
+  if (__syncthreads_or(X && !ok)) {
+    if (threadIdx.x == 0) {
+      w.selcnt[b] = 0;
+      if (b == 0) {
+        st.state[KIV_ST_SEL] = 0;
+        st.state[KIV_ST_SEL_LOCAL] = 0;
+      }
+    }
+    if (X) x_advance(x, X_FINE, e);
+    return;
+  }
   // valid entries per list, one shared atomic per warp and list
   for (int i0 = threadIdx.x & ~31; i0 < m; i0 += FM_THREADS) {
     const int i = i0 + (threadIdx.x & 31);

@@ -114,11 +114,10 @@ scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_que
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = s_tmem;
-  // fine pass: the cold length was published by the eviction, kernels back
-  int64_t cold = COARSE ? 0 : st_ld(st.state, KIV_ST_COLD_LEN);
-  // ---- the previous kernel's results (state, union) are needed from here on
+  // ---- the previous kernel's results (state, union) are needed from here on;
+  // the cold length too (an eviction may be the kernel right before this one)
   griddep_wait();
-  if (COARSE) cold = st_ld(st.state, KIV_ST_COLD_LEN);
+  const int64_t cold = st_ld(st.state, KIV_ST_COLD_LEN);
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     st.state[COARSE ? KIV_ST_COARSE_MAX : KIV_ST_FINE_MAX] = 0;
     st.state[COARSE ? KIV_ST_COARSE_SUM : KIV_ST_FINE_SUM] = 0;

@@ -14,13 +14,15 @@
 // * the scratch is KIV_NOALLOC_SCRATCH_BYTES (32 MiB) per GPU, reserved in
 //   every GPU that loads the library until the process exits; a store/query
 //   shape whose workspace exceeds it is rejected with KIV_ERR_CAPACITY;
-// * every call on a device uses the same array and leaves its contents there;
-//   the regions that must start at zero (page marks, select histograms and
-//   stats) are left at zero by every completed call, and the whole span that
-//   holds them is cleared whenever the workspace layout changes (a call with
-//   another shape); two calls whose work overlaps on the GPU (different
-//   streams, no ordering between them) race on the array and give wrong
-//   results;
+// * every call on a device uses the same array, which keeps the last call's
+//   contents.  Each call therefore first clears, on its stream, the span of
+//   the scratch that must start at zero (page marks through the select
+//   histograms and statistics) -- whatever shape, failure or interruption the
+//   previous call left behind.  The clear is part of every call, so it is
+//   also recorded when the call is captured into a CUDA graph;
+// * two calls whose work overlaps on the GPU (different streams with no
+//   ordering between them, or graph replays running beside eager calls) race
+//   on the array and give wrong results;
 // * the first call on a device looks up the array's device address
 //   (cudaGetSymbolAddress, with that device current); make that first call
 //   before any stream capture.
@@ -34,7 +36,6 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[KIV_NOALLOC_SCR
 
 static constexpr int kMaxDevices = 64;
 static void *g_scratch_addr[kMaxDevices] = {};
-static int64_t g_layout_sig[kMaxDevices][3] = {};   // workspace bytes, marks offset, partials offset
 static std::mutex g_scratch_mu;
 
 // Device address of the scratch array for the current device (host-side
@@ -81,24 +82,11 @@ extern "C" kiv_status kiv_retrieve_attend_noalloc(const kiv_store *st, const kiv
   int64_t lay[10];
   rc = kiv_workspace_layout(st, q, lay);
   if (rc != KIV_OK) return rc;
-  // a new layout may find another layout's data where its zero-start
-  // regions lie: clear the span from the page marks to the partials
-  int dev = 0;
-  cudaGetDevice(&dev);
-  bool changed;
-  {
-    std::lock_guard<std::mutex> lock(g_scratch_mu);
-    int64_t *sig = g_layout_sig[dev];
-    changed = sig[0] != (int64_t)need || sig[1] != lay[1] || sig[2] != lay[5];
-    sig[0] = (int64_t)need;
-    sig[1] = lay[1];
-    sig[2] = lay[5];
-  }
-  if (changed) {
-    rc = cuda_status(cudaMemsetAsync(static_cast<unsigned char *>(scratch) + lay[1], 0, (size_t)(lay[5] - lay[1]),
-                                     (cudaStream_t)stream),
-                     "noalloc: clear zero-start regions");
-    if (rc != KIV_OK) return rc;
-  }
+  // the regions that must start at zero lie between the page marks and the
+  // attention partials: clear that span on every call
+  rc = cuda_status(cudaMemsetAsync(static_cast<unsigned char *>(scratch) + lay[1], 0, (size_t)(lay[5] - lay[1]),
+                                   (cudaStream_t)stream),
+                   "noalloc: clear zero-start regions");
+  if (rc != KIV_OK) return rc;
   return kiv_retrieve_attend(st, q, mask, scratch, KIV_NOALLOC_SCRATCH_BYTES, 0, sel, out, stream);
 }

@@ -11,8 +11,8 @@ merged output.
 On CUDA the exchanges go through peer memory: every rank allocates an
 exchange arena, the ranks swap CUDA IPC handles once over the process group,
 and the merge kernels store their lists straight into the peers' arenas over
-NVLink and wait on per-source counters (``kiv_*_exchange_merge`` in the C
-ABI).  ``all_gather`` / ``all_reduce_sum`` (the process group's collectives)
+NVLink as words that carry the exchange's flag, and wait (bounded) until every
+rank's words carry it (``kiv_*_exchange_merge`` in the C ABI).  ``all_gather`` / ``all_reduce_sum`` (the process group's collectives)
 remain for the API paths that return tensors and for CPU process groups.
 """
 
