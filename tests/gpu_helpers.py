@@ -102,6 +102,20 @@ def check_selection(store, ol, query, scaling, cfg, sel, P, storage="f32", rtol=
 
 
 def rel_err(a, b):
+    """Normwise relative error: the largest absolute difference over the whole
+    output divided by the largest absolute reference value (see also
+    ``rel_err_rows`` for the same ratio per query row)."""
     a = np.asarray(a, np.float64)
     b = np.asarray(b, np.float64)
     return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+def rel_err_rows(a, b):
+    """Largest per-row relative error: for every query row (the last axis holds
+    its D values), the largest absolute difference divided by that row's
+    largest absolute reference value; the maximum over rows."""
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    num = np.abs(a - b).max(axis=-1)
+    den = np.maximum(np.abs(b).max(axis=-1), 1e-30)
+    return float((num / den).max())
