@@ -14,7 +14,9 @@ What differs is where the data lives and who computes:
   and length are kept in device memory next to the cold length, so the decode
   step launches the same kernels with the same arguments every time;
 * every step of the retrieval runs in ``libkiv_b200.so`` (C ABI, ``include/
-  kiv_b200.h``); there is no CPU or PyTorch fallback, a missing library raises.
+  kiv_b200.h``), called through its PyTorch operators ``torch.ops.kiv.*``
+  (``kiv_b200.ops``); there is no CPU or PyTorch fallback, a missing library
+  raises.
 
 The store can be one shard of a cold tier partitioned over GPUs (page p on
 shard p % shard_count); the collective steps then go through ``comm``.
@@ -30,6 +32,7 @@ import os
 import torch
 
 from . import _native as nat
+from . import ops
 from .config import KIVConfig
 from .model_topology import ModelTopology
 from .telemetry import RetrievalTelemetry
@@ -75,6 +78,7 @@ class ColdKVStore:
         self._hot_start = 0
         self._hot_len = 0
         self._desc: nat.StoreDesc | None = None
+        self._op_tensors: list | None = None
         self._ws: dict[tuple, tuple] = {}
         self._bufs: dict[tuple, torch.Tensor] = {}
         # shared-layer candidate reuse (attribute names of the reference)
@@ -128,7 +132,7 @@ class ColdKVStore:
                 f"ColdKVStore runs on CUDA devices only (got {self.device}); the B200 kernels "
                 "are the only implementation")
         nat.dtype_code(dtype)
-        nat.load_library()
+        ops.load()
         self._batch, self._dtype = batch, dtype
         self._state = torch.zeros(nat.STATE_WORDS, dtype=torch.int64, device=self.device)
         cap = self.kiv_config.cold_capacity or _MIN_COLD
@@ -154,6 +158,7 @@ class ColdKVStore:
             s[:, :, :old // S].copy_(self._summ)
         self._k, self._v, self._summ = k, v, s
         self._desc = None
+        self._op_tensors = None
         self._ws.clear()
         self._cached_ws_key = None
 
@@ -172,6 +177,7 @@ class ColdKVStore:
         self._host_k = self._host_tensor(B, H, host, D)
         self._host_v = self._host_tensor(B, H, host, D)
         self._desc = None
+        self._op_tensors = None
         self._ws.clear()
         self._cached_ws_key = None
 
@@ -234,6 +240,7 @@ class ColdKVStore:
         self._hk, self._hv, self._hot_cap = hk, hv, cap
         self._set_hot_start(0)
         self._desc = None
+        self._op_tensors = None
         self._ws.clear()
         self._cached_ws_key = None
 
@@ -269,6 +276,22 @@ class ColdKVStore:
                 self.kiv_config.stage_pages if self.tiered else 0, 0)
         return self._desc
 
+    def _op_store(self, hot_hint: int = 0):
+        """The store as the operators take it: (8 tensors, 5 ints)."""
+        if self._op_tensors is None:
+            empty = self._empty()
+            self._op_tensors = [self._k, self._v, self._summ,
+                                self._hk if self._hk is not None else empty,
+                                self._hv if self._hv is not None else empty, self._state,
+                                self._host_k if self._host_k is not None else empty,
+                                self._host_v if self._host_v is not None else empty]
+        geom = [self._page_size, self._shard_rank, self._shard_count, int(hot_hint),
+                self.kiv_config.stage_pages if self.tiered else 0]
+        return self._op_tensors, geom
+
+    def _empty(self) -> torch.Tensor:
+        return torch.empty(0, dtype=self._dtype, device=self.device)
+
     def _rows(self, x: torch.Tensor) -> torch.Tensor:
         """New K/V rows as the kernels want them: store dtype/device, 16-byte aligned rows."""
         if x.device != self.device or x.dtype != self._dtype:
@@ -301,9 +324,7 @@ class ColdKVStore:
         k, v = self._rows(k_evicted), self._rows(v_evicted)
         self._ensure_cold_room(self._cold_len + n)
         with torch.cuda.device(self.device):
-            nat.check(nat.lib().kiv_append_evict(
-                ctypes.byref(self.descriptor()), k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1),
-                k.stride(2), n, nat.KEEP_DIRECT, n, nat.stream_ptr(self.device)), "evict_from_hot")
+            ops.call(ops.kiv().append_evict, *self._op_store(), k, v, nat.KEEP_DIRECT, n)
         self._cold_len += n
 
     def append_and_evict(self, k_new: torch.Tensor | None, v_new: torch.Tensor | None,
@@ -334,16 +355,13 @@ class ColdKVStore:
             return n_ev
         self._ensure_hot_room(n)
         self._ensure_cold_room(self._cold_len + n_ev)
+        k = v = None
         if n > 0:
             k, v = self._rows(k_new), self._rows(v_new)
-            kp, vp, sb, sh, st = k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1), k.stride(2)
-        else:
-            kp = vp = None
-            sb = sh = st = 0
+            if k.stride() != v.stride():
+                k, v = k.contiguous(), v.contiguous()
         with torch.cuda.device(self.device):
-            nat.check(nat.lib().kiv_append_evict(
-                ctypes.byref(self.descriptor()), kp, vp, sb, sh, st, n, keep, n_ev,
-                nat.stream_ptr(self.device)), "append_evict")
+            ops.call(ops.kiv().append_evict, *self._op_store(), k, v, keep, n_ev)
         self._cold_len += n_ev
         self._hot_start += n_ev
         self._hot_len += n - n_ev
@@ -391,22 +409,20 @@ class ColdKVStore:
             query = query.contiguous()
         return query
 
-    def _workspace(self, qd: nat.QueryDesc, B: int, Hq: int, Q: int, top_pages: int, top_p: int):
+    def _workspace(self, qa: tuple, B: int, Hq: int, Q: int, top_pages: int, top_p: int):
+        """(key, (workspace tensor, layout words)) for this query shape."""
         key = (B, Hq, Q, top_pages, top_p)
         ws = self._ws.get(key)
         if ws is None:
-            desc = self.descriptor()
-            nbytes = nat.lib().kiv_workspace_bytes(ctypes.byref(desc), ctypes.byref(qd))
+            lay = ops.call(ops.kiv().workspace_layout, *self._op_store(), qa[0], top_pages, top_p)
+            nbytes = lay[10]
             if nbytes == 0:
-                nat.check(nat.KIV_OK + 1, "workspace size")
+                raise nat.KIVNativeError("workspace size: the store/query shape was rejected")
             # zeroed once: the page-flag array must start clear (kernels keep it clear)
             buf = torch.zeros(nbytes + 256, dtype=torch.uint8, device=self.device)
             off = (-buf.data_ptr()) % 256
             buf = buf[off:off + nbytes]
-            lay = (ctypes.c_int64 * 10)()
-            nat.check(nat.lib().kiv_workspace_layout(ctypes.byref(desc), ctypes.byref(qd), lay),
-                      "workspace layout")
-            ws = (buf, tuple(lay))
+            ws = (buf, tuple(lay[:10]))
             self._ws[key] = ws
         return key, ws
 
@@ -429,11 +445,10 @@ class ColdKVStore:
         """Coarse (or reuse) + fine.  Returns (sel [B, top_p] int32, ws key, ws, qdesc)."""
         B, Hq, Q, _ = query.shape
         top_pages, top_p = kiv_config.top_pages, kiv_config.top_p
-        qd = nat.query_desc(query, scaling, top_pages, top_p, softcap)
-        wkey, (ws, lay) = self._workspace(qd, B, Hq, Q, top_pages, top_p)
-        desc = self.descriptor()
-        L = nat.lib()
-        s = nat.stream_ptr(self.device)
+        qa = (query, float(scaling), int(top_pages), int(top_p), float(softcap or 0.0))
+        wkey, (ws, lay) = self._workspace(qa, B, Hq, Q, top_pages, top_p)
+        K = ops.kiv()
+        so = self._op_store()
         reuse = (step >= 0 and step == self._cached_step and self._cached_candidate_k is not None
                  and self._cached_candidate_k.shape[0] == B and self._cached_ws_key == wkey)
         if reuse:
@@ -442,10 +457,9 @@ class ColdKVStore:
             if self._profile is not None:
                 self._profile.record("coarse_begin")
             if self._shard_count == 1:
-                nat.check(L.kiv_coarse_select(ctypes.byref(desc), ctypes.byref(qd), ws.data_ptr(),
-                                              ws.numel(), None, None, s), "coarse_select")
+                ops.call(K.coarse_select, *so, *qa, ws, None, None)
             else:
-                self._sharded_coarse(desc, qd, ws, B * Hq * Q, top_pages, s)
+                self._sharded_coarse(qa, ws, B * Hq * Q, top_pages)
             marker = self._buffer("marker", (B, 0), torch.int8)
             self._cached_candidate_k = marker
             self._cached_candidate_v = marker
@@ -458,17 +472,15 @@ class ColdKVStore:
             prof = self._profile
             if prof is not None:
                 prof.record("fine_score_begin")
-            nat.check(L.kiv_fine_score(ctypes.byref(desc), ctypes.byref(qd), ws.data_ptr(), ws.numel(), s),
-                      "fine_score")
+            ops.call(K.fine_score, *so, *qa, ws)
             if prof is not None:
                 prof.record("fine_score_end")
-            nat.check(L.kiv_fine_topk(ctypes.byref(desc), ctypes.byref(qd), ws.data_ptr(), ws.numel(),
-                                      sel.data_ptr(), None, s), "fine_topk")
+            ops.call(K.fine_topk, *so, *qa, ws, sel, None)
             if prof is not None:
                 prof.record("fine_topk_end")
             sel_local = sel
         else:
-            sel_local = self._sharded_fine(desc, qd, ws, B, top_p, sel if global_sel else None, s)
+            sel_local = self._sharded_fine(qa, ws, B, top_p, sel if global_sel else None)
         if not reuse:
             # the fine scorer materializes the page union the coarse pass marked
             if self.num_pages > 0:
@@ -478,7 +490,7 @@ class ColdKVStore:
                                               n_scores=B * Hq * Q * self._local_pages(self.num_pages))
             else:
                 self._telemetry.record_coarse_skipped(cold_length=self._cold_len)
-        return sel, sel_local, ws, qd
+        return sel, sel_local, ws, qa
 
     def _record_fine(self, sel: torch.Tensor, P: int | None, top_p: int) -> None:
         if self._telemetry.enabled:
@@ -521,9 +533,7 @@ class ColdKVStore:
             out_k.zero_()
             out_v.zero_()
         with torch.cuda.device(self.device):
-            nat.check(nat.lib().kiv_gather_rows(ctypes.byref(self.descriptor()), sel.data_ptr(),
-                                                sel.shape[1], P, out_k.data_ptr(), out_v.data_ptr(),
-                                                nat.stream_ptr(self.device)), "gather_rows")
+            ops.call(ops.kiv().gather_rows, *self._op_store(), sel, P, out_k, out_v)
         if self._shard_count > 1:
             self._comm.all_reduce_sum(out_k)
             self._comm.all_reduce_sum(out_v)
@@ -545,110 +555,94 @@ class ColdKVStore:
         elif (out.shape != (B, Q, Hq, D) or out.dtype != self._dtype or not out.is_contiguous()
               or out.device != self.device):
             raise ValueError("out must be a contiguous [B, Q, Hq, D] tensor of the store dtype")
-        md = nat.mask_desc(mask_add, causal)
+        if mask_add is not None and (mask_add.dtype != torch.float32 or mask_add.stride(-1) != 1):
+            raise nat.KIVNativeError("mask must be float32 with a contiguous last dim")
         with torch.cuda.device(self.device):
-            s = nat.stream_ptr(self.device)
             if self._cold_len > 0:
-                sel, sel_local, ws, qd = self._select(query, scaling, kiv_config, step, softcap,
+                sel, sel_local, ws, qa = self._select(query, scaling, kiv_config, step, softcap,
                                                       global_sel=self._telemetry.enabled)
                 if self._telemetry.enabled:
                     self._record_fine(sel, self._expected_P(kiv_config.top_pages, kiv_config.top_p),
                                       kiv_config.top_p)
             else:
-                qd = nat.query_desc(query, scaling, kiv_config.top_pages, kiv_config.top_p, softcap)
-                _, (ws, _) = self._workspace(qd, B, Hq, Q, kiv_config.top_pages, kiv_config.top_p)
+                qa = (query, float(scaling), int(kiv_config.top_pages), int(kiv_config.top_p),
+                      float(softcap or 0.0))
+                _, (ws, lay) = self._workspace(qa, B, Hq, Q, kiv_config.top_pages, kiv_config.top_p)
                 sel_local = self._buffer("sel", (B, kiv_config.top_p), torch.int32)
-                self._zero_selcounts(ws, qd)
-            L = nat.lib()
-            desc = self.descriptor()
-            desc.hot_hint = self._hot_len
+                ws[lay[4]:lay[4] + 4 * self._batch].zero_()
+            K = ops.kiv()
+            so = self._op_store(hot_hint=self._hot_len)
             if self._shard_count == 1:
-                nat.check(L.kiv_attend(ctypes.byref(desc), ctypes.byref(qd), ctypes.byref(md),
-                                       ws.data_ptr(), ws.numel(), sel_local.data_ptr(),
-                                       sel_local.shape[1], 0, 1, out.data_ptr(), None, s), "attend")
+                ops.call(K.attend, *so, *qa, ws, sel_local, mask_add, bool(causal), 0, 1, out, None)
                 if self._profile is not None:
                     self._profile.record("attend_end")
             else:
                 R = B * Hq * Q
                 part = self._buffer("apart", (R, D + 4), torch.float32)
-                nat.check(L.kiv_attend(ctypes.byref(desc), ctypes.byref(qd), ctypes.byref(md),
-                                       ws.data_ptr(), ws.numel(), sel_local.data_ptr(),
-                                       sel_local.shape[1], self._shard_rank, self._shard_count,
-                                       None, part.data_ptr(), s), "attend")
-                x = self._exchange(desc, qd)
+                ops.call(K.attend, *so, *qa, ws, sel_local, mask_add, bool(causal), self._shard_rank,
+                         self._shard_count, None, part)
+                x = self._exchange(qa)
                 if x is not None:
-                    nat.check(L.kiv_attend_exchange_merge(ctypes.byref(desc), ctypes.byref(qd), part.data_ptr(),
-                                                          ctypes.byref(x), out.data_ptr(), s),
-                              "attend_exchange_merge")
+                    ops.call(K.attend_exchange_merge, *so, *qa, part, *x, out)
                 else:
                     gathered = self._buffer("apart_all", (self._shard_count, R, D + 4), torch.float32)
                     self._comm.all_gather(gathered, part)
-                    nat.check(L.kiv_attend_merge(ctypes.byref(desc), ctypes.byref(qd), gathered.data_ptr(),
-                                                 self._shard_count, out.data_ptr(), s), "attend_merge")
+                    ops.call(K.attend_merge, *so, *qa, gathered, out)
                 if self._profile is not None:
                     self._profile.record("attend_end")
         return out
 
-    def _zero_selcounts(self, ws: torch.Tensor, qd: nat.QueryDesc) -> None:
-        lay = (ctypes.c_int64 * 10)()
-        nat.check(nat.lib().kiv_workspace_layout(ctypes.byref(self.descriptor()), ctypes.byref(qd), lay),
-                  "workspace layout")
-        ws[lay[4]:lay[4] + 4 * self._batch].zero_()
-
     # ---------------------------------------------------------- sharded steps
-    def _exchange(self, desc, qd):
-        """Peer-memory exchange descriptor for this query shape, or None when the
-        process group's collectives are used (``KIV_SHARD_EXCHANGE=collective``)."""
+    def _exchange(self, qa: tuple):
+        """Peer-memory exchange arguments ``(arenas, arena_bytes, wait_cycles)`` for
+        this query shape, or None when the process group's collectives are used
+        (``KIV_SHARD_EXCHANGE=collective``)."""
         if os.environ.get("KIV_SHARD_EXCHANGE", "peer") == "collective":
             return None
-        nbytes = nat.lib().kiv_exchange_bytes(ctypes.byref(desc), ctypes.byref(qd), self._shard_count)
+        qd = nat.query_desc(qa[0], qa[1], qa[2], qa[3], qa[4])
+        nbytes = nat.lib().kiv_exchange_bytes(ctypes.byref(self.descriptor()), ctypes.byref(qd),
+                                              self._shard_count)
         if nbytes == 0:
             raise nat.KIVNativeError("kiv_exchange_bytes rejected the store/query shape")
-        return self._comm.exchange(nbytes, self.device)
+        x = self._comm.exchange(nbytes, self.device)
+        return [int(x.arena[i]) for i in range(x.world)], int(x.arena_bytes), int(x.wait_cycles)
 
-    def _sharded_coarse(self, desc, qd, ws, R: int, K: int, s: int) -> None:
-        L = nat.lib()
+    def _sharded_coarse(self, qa: tuple, ws, R: int, K: int) -> None:
+        kv = ops.kiv()
+        so = self._op_store()
         sc = self._buffer("crow_s", (R, K), torch.float32)
         pg = self._buffer("crow_p", (R, K), torch.int32)
-        nat.check(L.kiv_coarse_select(ctypes.byref(desc), ctypes.byref(qd), ws.data_ptr(), ws.numel(),
-                                      sc.data_ptr(), pg.data_ptr(), s), "coarse_select")
-        x = self._exchange(desc, qd)
+        ops.call(kv.coarse_select, *so, *qa, ws, sc, pg)
+        x = self._exchange(qa)
         if x is not None:
-            nat.check(L.kiv_coarse_exchange_merge(ctypes.byref(desc), ctypes.byref(qd), ws.data_ptr(), ws.numel(),
-                                                  sc.data_ptr(), pg.data_ptr(), ctypes.byref(x), s),
-                      "coarse_exchange_merge")
+            ops.call(kv.coarse_exchange_merge, *so, *qa, ws, sc, pg, *x)
             return
         n = self._shard_count
         all_s = self._buffer("crow_s_all", (n, R, K), torch.float32)
         all_p = self._buffer("crow_p_all", (n, R, K), torch.int32)
         self._comm.all_gather(all_s, sc)
         self._comm.all_gather(all_p, pg)
-        nat.check(L.kiv_coarse_merge(ctypes.byref(desc), ctypes.byref(qd), ws.data_ptr(), ws.numel(),
-                                     all_s.data_ptr(), all_p.data_ptr(), n, s), "coarse_merge")
+        ops.call(kv.coarse_merge, *so, *qa, ws, all_s, all_p)
 
-    def _sharded_fine(self, desc, qd, ws, B: int, top_p: int, sel: torch.Tensor | None, s: int) -> torch.Tensor:
+    def _sharded_fine(self, qa: tuple, ws, B: int, top_p: int, sel: torch.Tensor | None) -> torch.Tensor:
         """Local fine pass + exchange + merge; fills ``sel`` (the global list) when given."""
-        L = nat.lib()
+        kv = ops.kiv()
+        so = self._op_store()
         lt = self._buffer("fl_t", (B, top_p), torch.int32)
         ls = self._buffer("fl_s", (B, top_p), torch.float32)
         prof = self._profile
         if prof is not None:
             prof.record("fine_score_begin")
-        nat.check(L.kiv_fine_score(ctypes.byref(desc), ctypes.byref(qd), ws.data_ptr(), ws.numel(), s),
-                  "fine_score")
+        ops.call(kv.fine_score, *so, *qa, ws)
         if prof is not None:
             prof.record("fine_score_end")
-        nat.check(L.kiv_fine_topk(ctypes.byref(desc), ctypes.byref(qd), ws.data_ptr(), ws.numel(),
-                                  lt.data_ptr(), ls.data_ptr(), s), "fine_topk")
+        ops.call(kv.fine_topk, *so, *qa, ws, lt, ls)
         if prof is not None:
             prof.record("fine_topk_end")
         sel_local = self._buffer("sel_local", (B, top_p), torch.int32)
-        x = self._exchange(desc, qd)
+        x = self._exchange(qa)
         if x is not None:
-            nat.check(L.kiv_fine_exchange_merge(ctypes.byref(desc), ctypes.byref(qd), ws.data_ptr(), ws.numel(),
-                                                ls.data_ptr(), lt.data_ptr(), ctypes.byref(x),
-                                                None if sel is None else sel.data_ptr(),
-                                                sel_local.data_ptr(), s), "fine_exchange_merge")
+            ops.call(kv.fine_exchange_merge, *so, *qa, ws, ls, lt, *x, sel, sel_local)
             return sel_local
         n = self._shard_count
         all_t = self._buffer("fl_t_all", (n, B, top_p), torch.int32)
@@ -657,19 +651,14 @@ class ColdKVStore:
         self._comm.all_gather(all_s, ls)
         if sel is None:
             sel = self._buffer("sel_global_scratch", (B, top_p), torch.int32)
-        nat.check(L.kiv_fine_merge(ctypes.byref(desc), ctypes.byref(qd), ws.data_ptr(), ws.numel(),
-                                   all_s.data_ptr(), all_t.data_ptr(), n, sel.data_ptr(),
-                                   sel_local.data_ptr(), s), "fine_merge")
+        ops.call(kv.fine_merge, *so, *qa, ws, all_s, all_t, sel, sel_local)
         return sel_local
 
     # --------------------------------------------------------------- misc API
     def read_state(self) -> list[int]:
-        """Device state words (syncs); for tests and debugging."""
-        words = (ctypes.c_int64 * nat.STATE_WORDS)()
+        """Device state words (syncs the current stream); for tests and debugging."""
         with torch.cuda.device(self.device):
-            nat.check(nat.lib().kiv_read_state(ctypes.byref(self.descriptor()), words,
-                                               nat.stream_ptr(self.device)), "read_state")
-        return list(words)
+            return [int(x) for x in self._state.cpu().tolist()]
 
     def page_summaries(self) -> torch.Tensor | None:
         """Summaries of this shard's finalized pages ``[B, Hkv, local pages, D]``."""
