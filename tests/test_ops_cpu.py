@@ -81,3 +81,13 @@ def test_workspace_layout_matches_the_c_abi():
         nat.check(L.kiv_workspace_layout(ctypes.byref(sd), ctypes.byref(qd), want), "layout")
         assert list(lay[:10]) == list(want)
         assert lay[10] == L.kiv_workspace_bytes(ctypes.byref(sd), ctypes.byref(qd))
+
+
+def test_operator_errors_raise_not_crash():
+    """A shape the library rejects comes back as KIVNativeError with its message."""
+    import pytest
+
+    store, geom = _fake_store(torch.device("meta"), D=6, dtype=torch.float32)
+    q = torch.empty(1, 4, 1, 6, device="meta")
+    with pytest.raises(nat.KIVNativeError, match="multiple of 16 bytes"):
+        ops.call(ops.kiv().workspace_layout, store, geom, q, 4, 16)
