@@ -25,11 +25,16 @@ Lines printed by rank 0 (one JSON object):
   step copies its inputs from pinned host memory and reads the outputs back;
 * roofline: the dominant kernel (fine token scoring) timed alone with CUDA
   events in an eager pass, algorithmic bytes = candidate K rows read;
-* cpu_baseline: the oracle port (numpy) on one layer, on this box's host cores.
+* cpu_baseline: the oracle port (numpy) on layer 0 of the bench's own cache
+  (after checking one replayed step of that layer against it: "parity"), and
+  beside it the reference package's own CPU path when ``baseline/_ref`` holds
+  it, both on this box's host cores.
 
-``--impl reference`` times the CPU oracle port of the reference's algorithm
-(the reference is pure Python/PyTorch; its own package is not shipped to the
-GPU box) on the same workload, one layer-step per step.
+``--impl reference`` times the reference's own CPU path -- its package from
+``baseline/_ref`` (``TieredKVCache.update`` + ``ColdKVStore.retrieve_top_kv`` +
+HF eager attention, device cpu, every host thread) -- on one layer of the
+same workload, with the oracle port timed beside it; without the package the
+port is the reference arm.
 """
 
 from __future__ import annotations
@@ -209,7 +214,10 @@ def keys_for(gen, n, d, centroid_rows, t0, dev):
     return centroid_rows[seg] + 0.3 * torch.randn(n, d, generator=gen, device=dev)
 
 
-def build_cache(w, dev, kcfg, comm, queries0):
+def build_cache(w, dev, kcfg, comm, queries0, seq_shard=False, seed_offset=0):
+    """The bench cache, prefilled.  ``comm``: page sharding (one sequence over
+    the ranks), or with ``seq_shard`` sequence sharding (this rank's sequences,
+    union taken over the ranks)."""
     from transformers import PretrainedConfig
 
     from kiv_b200 import ModelTopology, TieredKVCache
@@ -217,13 +225,14 @@ def build_cache(w, dev, kcfg, comm, queries0):
     L, d = w["layers"], w["d"]
     topo = ModelTopology.manual(global_layer_indices=tuple(range(L)), num_query_heads=w["hq"],
                                 num_kv_heads=w["hkv"], head_dim=d, num_hidden_layers=L)
-    cache = TieredKVCache(PretrainedConfig(num_hidden_layers=L), kcfg, topo, dev, shard_group=comm)
+    groups = dict(batch_group=comm) if seq_shard else dict(shard_group=comm)
+    cache = TieredKVCache(PretrainedConfig(num_hidden_layers=L), kcfg, topo, dev, **groups)
     T = w["cold"] + w["hot"]
     B = w.get("batch", 1)
     chunk = max(4096, 65536 // B)
     for li in range(L):
         gen = torch.Generator(device=dev)
-        gen.manual_seed(1000 + li)
+        gen.manual_seed(1000 + li + seed_offset)
         n_seg = (T + w["hot"] + SEGMENT) // SEGMENT + 2
         cent = torch.randn(B, w["hkv"], n_seg, d, generator=gen, device=dev) / math.sqrt(64.0)
         needle = int(torch.randint(0, w["cold"] // PAGE, (1,), generator=gen, device=dev).item())
@@ -391,6 +400,75 @@ def cpu_oracle_rate(w, layer, seconds=12.0, max_steps=None, min_steps=3):
     return n / el, n, el, threads
 
 
+REF_PKG = os.path.join(ROOT, "baseline", "_ref")
+
+
+def reference_package_available():
+    return os.path.isdir(os.path.join(REF_PKG, "kiv"))
+
+
+def reference_package_rate(w, seconds=20.0, max_steps=None):
+    """Layer-steps/s of the reference package's own CPU path on one layer of
+    the workload: ``TieredKVCache.update`` (append + evict), ``ColdKVStore.
+    retrieve_top_kv`` and HF eager attention over ``[selected cold ; hot]``,
+    as its attention wrapper runs them (kiv/middleware.py:308-354), with
+    ``device="cpu"``, ``prefetch_stream=False`` and every host thread.  The
+    cold tier is built through ``update`` in chunks of 8 pages, each followed
+    by ``_evict_to_cap`` (one call with the whole prefill would re-slice its
+    partial buffer once per page, quadratic in the prefill).  Returns (rate, steps, seconds, threads)."""
+    if REF_PKG not in sys.path:
+        sys.path.insert(0, REF_PKG)
+    from kiv import KIVConfig as RefConfig
+    from kiv import ModelTopology as RefTopology
+    from kiv import TieredKVCache as RefCache
+    from transformers import PretrainedConfig
+    from transformers.models.llama.modeling_llama import eager_attention_forward
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    dt = torch.float32 if w.get("dtype") == "f32" else torch.bfloat16
+    hq, hkv, d = w["hq"], w["hkv"], w["d"]
+    cfg = RefConfig(hot_budget=w["hot"], top_p=w["top_p"], page_size=PAGE, top_pages=w["top_pages"],
+                    prefetch_stream=False)
+    topo = RefTopology.manual(global_layer_indices=(0,), num_query_heads=hq, num_kv_heads=hkv, head_dim=d,
+                              num_hidden_layers=1)
+    cache = RefCache(PretrainedConfig(num_hidden_layers=1), cfg, topo, torch.device("cpu"))
+    gen = torch.Generator().manual_seed(0)
+    T = w["cold"] + w["hot"]
+    cent = torch.randn(1, hkv, T // SEGMENT + 2, d, generator=gen) / math.sqrt(64.0)
+    chunk = 8 * PAGE
+    for a in range(0, T, chunk):
+        n = min(chunk, T - a)
+        seg = torch.arange(a, a + n) // SEGMENT
+        k = cent[:, :, seg] + 0.3 * torch.randn(1, hkv, n, d, generator=gen)
+        v = torch.randn(1, hkv, n, d, generator=gen)
+        cache.update(k.to(dt), v.to(dt), 0)
+        cache._evict_to_cap(w["hot"])
+    cache.mark_prefill_complete()
+    store = cache.get_cold_store(0)
+
+    class _Attn:        # what eager_attention_forward reads from the attention module
+        num_key_value_groups = hq // hkv
+        training = False
+
+    scaling = d ** -0.5
+    n, t0 = 0, time.perf_counter()
+    while True:
+        q = torch.randn(1, hq, 1, d, generator=gen).to(dt)
+        k = (0.3 * torch.randn(1, hkv, 1, d, generator=gen)).to(dt)
+        v = torch.randn(1, hkv, 1, d, generator=gen).to(dt)
+        hot_k, hot_v = cache.update(k, v, 0)
+        ck, cv = store.retrieve_top_kv(q, scaling, cfg, step=-1)
+        if ck is not None:
+            hot_k, hot_v = torch.cat([ck, hot_k], dim=2), torch.cat([cv, hot_v], dim=2)
+        eager_attention_forward(_Attn(), q, hot_k, hot_v, None, scaling=scaling)
+        n += 1
+        el = time.perf_counter() - t0
+        if (max_steps is not None and n >= max_steps) or (max_steps is None and n >= 3 and el >= seconds):
+            break
+    return n / el, n, el, threads
+
+
 def cpu_model():
     try:
         with open("/proc/cpuinfo") as f:
@@ -403,30 +481,50 @@ def cpu_model():
 
 
 # ------------------------------------------------------------------- main
+def workload_string(name, w):
+    """The config.workload string both arms print (one format for both)."""
+    return (f"{name}: {w['layers']} layers, Hq={w['hq']} Hkv={w['hkv']} D={w['d']}, {w['cold']} cold + "
+            f"{w['hot']} hot tokens per layer, page={PAGE}, top_pages={w['top_pages']}, top_p={w['top_p']}, "
+            f"batch {w.get('batch', 1)}")
+
+
 def run_reference(args, w, rank, world):
+    """The reference's own CPU path (its package from baseline/_ref) on one
+    layer of the workload, every host thread; the oracle port is timed beside
+    it.  Without the package the port is the reference arm."""
     if rank != 0:
         return 0
-    layer = cpu_oracle_layer(w)
-    # warm-up doubles as a rate probe; the timed steps stay within ~2.5 minutes
-    rate_probe, _, _, threads = cpu_oracle_rate(w, layer, max_steps=max(args.warmup, 1))
-    steps = min(args.steps, max(3, int(150.0 * rate_probe)))
-    rate, n, el, threads = cpu_oracle_rate(w, layer, max_steps=steps)
-    sample = (f"1 of {w['layers']} layers at full size ({w['cold']} cold tokens), {n} layer-steps "
-              f"(numpy oracle port, fp32 math on {w.get('dtype', 'bf16')} values, {threads} threads, "
-              f"{cpu_model()})")
+    budget = 150.0
+    port_layer = cpu_oracle_layer(w)
+    probe, _, _, threads = cpu_oracle_rate(w, port_layer, max_steps=max(args.warmup, 1))
+    steps = min(args.steps, max(3, int(60.0 * probe)))
+    p_rate, p_n, p_el, threads = cpu_oracle_rate(w, port_layer, max_steps=steps)
+    del port_layer
+    port = {"value": p_rate, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"1 of {w['layers']} layers at full size, {p_n} layer-steps (numpy oracle port, fp32 math "
+                      f"on {w.get('dtype', 'bf16')} values, {cpu_model()})"}
+    note = None
+    if reference_package_available() and w.get("batch", 1) == 1:
+        rate, n, el, threads = reference_package_rate(w, seconds=min(budget, 10.0 * max(1, args.steps)))
+        kind = "reference"
+        sample = (f"1 of {w['layers']} layers at full size ({w['cold']} cold tokens), {n} layer-steps in {el:.1f} s: "
+                  f"the reference package's TieredKVCache.update + ColdKVStore.retrieve_top_kv + HF eager "
+                  f"attention on device cpu, {threads} threads, {cpu_model()}")
+    else:
+        rate, n, kind, sample = p_rate, p_n, "port", port["sample"]
+        note = "the reference package (baseline/_ref) is not on this box: the oracle port is the reference arm"
     line = {
         "metric": METRIC, "value": rate, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1000.0 / rate, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": w.get("dtype", "bf16"), "data": "synthetic",
-        "config": {"workload": f"{args.workload}: {w['layers']} layers, Hq={w['hq']} Hkv={w['hkv']} "
-                               f"D={w['d']}, {w['cold']} cold + {w['hot']} hot, top_pages={w['top_pages']}, "
-                               f"top_p={w['top_p']}, page={PAGE}", "parallelism": "cpu"},
+        "config": {"workload": workload_string(args.workload, w), "parallelism": "cpu"},
         "impl": "reference",
-        "cpu_baseline": {"value": rate, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "cpu_baseline": {"value": rate, "unit": UNIT, "cores": threads, "kind": kind, "sample": sample},
         "e2e": {"value": rate, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "port": port,
     }
-    if steps < args.steps:
-        line["note"] = f"ran {steps} of {args.steps} requested steps to stay within the time budget"
+    if note:
+        line["note"] = note
     print(json.dumps(line), flush=True)
     return 0
 
@@ -469,9 +567,18 @@ def main():
         cold_cap = w["ring"]
     kcfg = KIVConfig(hot_budget=w["hot"], top_p=w["top_p"], page_size=PAGE, top_pages=w["top_pages"],
                      cold_capacity=cold_cap, hot_slack=4096, telemetry=False, **tier)
-    q_pool, k_pool, v_pool = make_inputs(w, dev, INPUT_POOL)
+    # sequence sharding (batched workloads over N GPUs): each rank holds
+    # batch / N of the sequences, drawn from its own seeds
+    w_total = dict(w)
+    seq_shard = world > 1 and w.get("batch", 1) > 1
+    if seq_shard:
+        if w["batch"] % world:
+            raise SystemExit(f"batch {w['batch']} does not split over {world} GPUs")
+        w["batch"] //= world
+    q_pool, k_pool, v_pool = make_inputs(w, dev, INPUT_POOL, seed=7 + (rank if seq_shard else 0))
     t_build = time.perf_counter()
-    cache = build_cache(w, dev, kcfg, comm, q_pool[0, :, :, :, 0, :])
+    cache = build_cache(w, dev, kcfg, comm, q_pool[0, :, :, :, 0, :], seq_shard=seq_shard,
+                        seed_offset=100003 * rank if seq_shard else 0)
     t_build = time.perf_counter() - t_build
     scaling = w["d"] ** -0.5
     layers = list(range(L))
@@ -642,17 +749,19 @@ def main():
 
     result = None
     if rank == 0:
-        step_bytes = step_algorithmic_bytes(w, U_mean, 1, e=welem(w))
+        # (sequence sharding: every rank moves its own sequences' bytes)
+        step_bytes = step_algorithmic_bytes(w, U_mean, 1, e=welem(w)) * (world if seq_shard else 1)
         f32 = w.get("dtype") == "f32"
         layer_step_s = ms * 1e-3 / (L * K)
         result = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
             "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": w.get("dtype", "bf16"), "data": "synthetic",
-            "config": {"workload": f"{args.workload}: {L} layers, Hq={w['hq']} Hkv={w['hkv']} D={w['d']}, "
-                                   f"{w['cold']} cold + {w['hot']} hot tokens per layer, page={PAGE}, "
-                                   f"top_pages={w['top_pages']}, top_p={w['top_p']}, batch {w.get('batch', 1)}",
-                       "parallelism": f"cold pages sharded over {world} GPU(s)" if world > 1 else "1 GPU",
+            "config": {"workload": workload_string(args.workload, w_total),
+                       "parallelism": ("1 GPU" if world == 1 else
+                                       f"sequences sharded over {world} GPUs ({w['batch']} per GPU), page union "
+                                       "OR-reduced over the ranks" if seq_shard else
+                                       f"cold pages sharded over {world} GPU(s)"),
                        "l2": f"inputs larger than L2 (each step touches {L} layers x ~{step_bytes / 1e6:.0f} MB)",
                        "timing": f"CUDA graph of one {L}-layer step replayed, CUDA events, max over ranks"},
             # per layer-step: 7 kernels (8 on the CUDA-core fp32 path, whose union is its own kernel)
@@ -718,6 +827,14 @@ def main():
             "value": rate, "unit": UNIT, "cores": threads, "kind": "port",
             "sample": f"{what}, {n} layer-steps in {el:.1f} s "
                       f"(numpy oracle port, fp32 math on {w.get('dtype', 'bf16')} values, {cpu_model()})"}
+        del layer
+        if reference_package_available() and w.get("batch", 1) == 1:
+            r_rate, r_n, r_el, r_threads = reference_package_rate(w, seconds=12.0)
+            result["cpu_baseline"]["reference_package"] = {
+                "value": r_rate, "unit": UNIT, "cores": r_threads, "kind": "reference",
+                "sample": f"1 of {L} layers at full size, {r_n} layer-steps in {r_el:.1f} s: the reference "
+                          "package's TieredKVCache.update + ColdKVStore.retrieve_top_kv + HF eager attention "
+                          "on device cpu"}
     if rank == 0:
         print(json.dumps(result), flush=True)
     if world > 1:

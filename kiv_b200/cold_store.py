@@ -51,7 +51,7 @@ class ColdKVStore:
     """Cold tier (and hot window buffer) of one independent KV layer."""
 
     def __init__(self, kiv_config: KIVConfig, topology: ModelTopology, device: torch.device,
-                 *, shard_rank: int = 0, shard_count: int = 1, comm=None) -> None:
+                 *, shard_rank: int = 0, shard_count: int = 1, comm=None, batch_comm=None) -> None:
         self.kiv_config = kiv_config
         self.device = torch.device(device)
         self._num_kv_groups = topology.num_query_heads // topology.num_kv_heads
@@ -62,6 +62,11 @@ class ColdKVStore:
         self._shard_rank = shard_rank
         self._shard_count = shard_count
         self._comm = comm
+        # sequence sharding: this store holds the calling rank's sequences;
+        # the page union is OR-reduced over batch_comm's ranks
+        self._batch_comm = batch_comm
+        if shard_count > 1 and batch_comm is not None:
+            raise ValueError("a store is either page-sharded or sequence-sharded, not both")
         if shard_count > 1 and comm is None:
             raise ValueError("a sharded ColdKVStore needs a comm")
         self._batch: int | None = None
@@ -322,6 +327,8 @@ class ColdKVStore:
                 self.evict_from_hot(k_evicted[:, :, a:a + limit], v_evicted[:, :, a:a + limit])
             return
         k, v = self._rows(k_evicted), self._rows(v_evicted)
+        if any(m > 1 and a != b for m, a, b in zip(k.shape, k.stride(), v.stride())):
+            k, v = k.contiguous(), v.contiguous()
         self._ensure_cold_room(self._cold_len + n)
         with torch.cuda.device(self.device):
             ops.call(ops.kiv().append_evict, *self._op_store(), k, v, nat.KEEP_DIRECT, n)
@@ -358,7 +365,7 @@ class ColdKVStore:
         k = v = None
         if n > 0:
             k, v = self._rows(k_new), self._rows(v_new)
-            if k.stride() != v.stride():
+            if any(n > 1 and a != b for n, a, b in zip(k.shape, k.stride(), v.stride())):
                 k, v = k.contiguous(), v.contiguous()
         with torch.cuda.device(self.device):
             ops.call(ops.kiv().append_evict, *self._op_store(), k, v, keep, n_ev)
@@ -458,6 +465,10 @@ class ColdKVStore:
                 self._profile.record("coarse_begin")
             if self._shard_count == 1:
                 ops.call(K.coarse_select, *so, *qa, ws, None, None)
+                if self._batch_comm is not None and self._batch_comm.size > 1:
+                    # the union spans the whole batch, held by all ranks
+                    words = (lay[7] + 31) // 32
+                    self._batch_comm.all_or_bits(ws[lay[1]:lay[1] + 4 * words].view(torch.int32))
             else:
                 self._sharded_coarse(qa, ws, B * Hq * Q, top_pages)
             marker = self._buffer("marker", (B, 0), torch.int8)

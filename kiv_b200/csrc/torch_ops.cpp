@@ -137,8 +137,10 @@ void append_evict(at::TensorList store, at::IntArrayRef geom, const c10::optiona
   int32_t n_new = 0;
   if (k_new.has_value() && k_new->defined()) {
     const Tensor &k = *k_new, &v = *v_new;
-    TORCH_CHECK(k.dim() == 4 && v.sizes() == k.sizes() && v.strides() == k.strides(),
-                "kiv: new K/V rows must be [B, Hkv, n, D] with the same strides");
+    TORCH_CHECK(k.dim() == 4 && v.sizes() == k.sizes(), "kiv: new K/V rows must both be [B, Hkv, n, D]");
+    // one set of strides serves both (a dimension of size 1 is never stepped)
+    for (int d = 0; d < 4; ++d)
+      TORCH_CHECK(k.size(d) == 1 || k.stride(d) == v.stride(d), "kiv: new K and V rows need the same strides");
     TORCH_CHECK(k.scalar_type() == store[0].scalar_type(), "kiv: new rows must have the store dtype");
     kp = k.data_ptr();
     vp = v.data_ptr();

@@ -175,13 +175,18 @@ class KIVMiddleware:
         self._kiv_key = None
         logger.info("KIV middleware uninstalled.")
 
-    def create_cache(self, device: torch.device | None = None, *, shard_group=None) -> TieredKVCache:
+    def create_cache(self, device: torch.device | None = None, *, shard_group=None,
+                     batch_group=None) -> TieredKVCache:
+        """``shard_group``: split every layer's cold pages over the group's ranks
+        (one sequence, strong scaling); ``batch_group``: this rank holds its own
+        sequences of the batch and the page union is taken over the group."""
         if self.topology is None:
             raise RuntimeError("Call install() before create_cache().")
         if device is None:
             device = next(self.model.parameters()).device
         cache = TieredKVCache(config=self.model.config, kiv_config=self.config,
-                              topology=self.topology, device=device, shard_group=shard_group)
+                              topology=self.topology, device=device, shard_group=shard_group,
+                              batch_group=batch_group)
         self.activate_cache(cache)
         return cache
 

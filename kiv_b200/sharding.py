@@ -1,4 +1,11 @@
-"""Exchanges of the page-sharded cold tier (one process per GPU of one box).
+"""Exchanges of the sharded cold tier (one process per GPU of one box).
+
+Two partitions exist.  Sequence sharding (``batch_group``): each rank holds
+its own sequences of the batch; the only exchange is the page union, which
+the reference takes across the whole batch (kiv/cold_store.py:224) -- the
+ranks OR their coarse page marks (``all_or_bits``) before the fine pass, and
+everything after it is per sequence.  Page sharding (``shard_group``) splits
+one sequence's cold pages:
 
 The cold tier of a layer is partitioned by page over the GPUs of one box (page
 p lives on rank p % world).  A decode layer-step then needs three small
@@ -89,6 +96,16 @@ class ShardComm:
 
     def all_reduce_sum(self, t: torch.Tensor) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
+
+    def all_or_bits(self, words: torch.Tensor) -> None:
+        """Bitwise OR of an int32 bitmap over the ranks, in place (every rank
+        ends with the union of all ranks' bits).  The bits travel as bytes
+        reduced with MAX, which every backend supports for uint8."""
+        shifts = torch.arange(32, device=words.device, dtype=torch.int32)
+        flags = ((words[:, None] >> shifts) & 1).to(torch.uint8)
+        dist.all_reduce(flags, op=dist.ReduceOp.MAX, group=self.group)
+        packed = (flags.to(torch.int64) << shifts.to(torch.int64)).sum(dim=1)
+        words.copy_(packed.to(torch.int32))
 
 
 def shard_of_page(page: int, world: int) -> int:

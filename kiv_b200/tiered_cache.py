@@ -83,7 +83,7 @@ class TieredKVCache(DynamicCache):
     """Hot window + HBM cold tier per independent global layer."""
 
     def __init__(self, config, kiv_config: KIVConfig, topology: ModelTopology,
-                 device: torch.device | None = None, *, shard_group=None) -> None:
+                 device: torch.device | None = None, *, shard_group=None, batch_group=None) -> None:
         super().__init__(config=config)
         self.kiv_config = kiv_config
         self.topology = topology
@@ -96,10 +96,20 @@ class TieredKVCache(DynamicCache):
             comm = shard_group if isinstance(shard_group, ShardComm) else ShardComm(shard_group)
             rank, count = comm.rank, comm.size
         self.shard_comm = comm
+        # sequence sharding: this rank's cache holds its own sequences of the
+        # batch; the page union is taken across the ranks (the reference's
+        # union spans the batch, kiv/cold_store.py:224)
+        bcomm = None
+        if batch_group is not None:
+            if shard_group is not None:
+                raise ValueError("pass shard_group (pages) or batch_group (sequences), not both")
+            from .sharding import ShardComm
+            bcomm = batch_group if isinstance(batch_group, ShardComm) else ShardComm(batch_group)
+        self.batch_comm = bcomm
         self.cold_stores: dict[int, ColdKVStore] = {}
         for li in topology.independent_kv_layers:
             self.cold_stores[li] = ColdKVStore(kiv_config, topology, self.device,
-                                               shard_rank=rank, shard_count=count, comm=comm)
+                                               shard_rank=rank, shard_count=count, comm=comm, batch_comm=bcomm)
         need = max(topology.independent_kv_layers, default=-1) + 1
         while len(self.layers) < need:
             self.layers.append(DynamicLayer())

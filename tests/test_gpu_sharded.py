@@ -167,3 +167,87 @@ def test_sharded_step_matches_single_gpu(shape, exchange):
                         p.kill()
                 pytest.fail("sharded ranks did not finish in 300 s")
         assert os.path.exists(os.path.join(d, "ok"))
+
+
+SEQ_SHAPE = dict(batch=4, num_query_heads=32, num_kv_heads=8, head_dim=128, cold_tokens=8192 + 37,
+                 hot_budget=512)
+
+
+def _seq_worker(rank, port, out_dir):
+    """Sequence sharding: rank r holds sequences [2r, 2r + 2) of a batch of 4;
+    its selection and attention must match the unsharded oracle's for them
+    (the page union spans all four sequences, OR-reduced over the ranks)."""
+    import datetime
+
+    import torch.distributed as dist
+    from transformers import PretrainedConfig
+
+    from kiv_b200 import KIVConfig, ModelTopology, TieredKVCache
+    from kiv_b200.synthetic import SynthSpec, make_problem
+    from oracle.kiv_oracle import eager_attention, topk_set_mismatch
+    from tests.gpu_helpers import oracle_decode, rel_err, rel_err_rows
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=WORLD, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        spec = SynthSpec(**SEQ_SHAPE)
+        top_pages, top_p = 8, 256
+        prob = make_problem(spec, seed=13, dtype=torch.bfloat16)
+        lo, hi = 2 * rank, 2 * rank + 2
+        cfg = KIVConfig(hot_budget=spec.hot_budget, page_size=spec.page_size, top_pages=top_pages, top_p=top_p,
+                        telemetry=False)
+        topo = ModelTopology.manual(global_layer_indices=(0,), num_query_heads=spec.num_query_heads,
+                                    num_kv_heads=spec.num_kv_heads, head_dim=spec.head_dim, num_hidden_layers=1)
+        cache = TieredKVCache(PretrainedConfig(num_hidden_layers=1), cfg, topo, dev, batch_group=dist.group.WORLD)
+        t = lambda x: x[lo:hi].to(dev)
+        cache.update(t(prob.prefill_k), t(prob.prefill_v), 0)
+        cache.mark_prefill_complete()
+        cache.update(t(prob.step_k), t(prob.step_v), 0)
+        store = cache.get_cold_store(0)
+        q = t(prob.query)
+        scaling = spec.head_dim ** -0.5
+        sel, P = store.retrieve_indices(q, scaling, cfg)
+        out = store.attend(q, scaling, cfg).float().cpu().numpy()
+        assert store.read_state()[7] == 0
+        f32 = lambda x: x.float().numpy()
+        ol = oracle_decode(spec, f32(prob.prefill_k), f32(prob.prefill_v), f32(prob.step_k), f32(prob.step_v),
+                           storage="bf16")
+        res = ol.store.retrieve_top_kv(f32(prob.query), scaling, top_pages, top_p)
+        got = sel[:, :P].cpu().numpy()
+        assert P == res.selected.shape[1]
+        pos = {int(c): i for i, c in enumerate(res.cand_idx)}
+        for j, b in enumerate(range(lo, hi)):
+            bad = topk_set_mismatch(got[j], res.selected[b], lambda c: res.agg_scores[b, pos[c]], P,
+                                    res.agg_scores[b])
+            assert bad == [], f"sequence {b}: selection differs beyond ties: {bad[:4]}"
+        ko, vo = ol.store.gather(np.concatenate([np.zeros((lo, P), np.int64), got,
+                                                 np.zeros((spec.batch - hi, P), np.int64)]))
+        ref = eager_attention(f32(prob.query), ko, vo, ol.hot_k, ol.hot_v, scaling)[lo:hi]
+        assert rel_err(out, ref) <= 2e-2 and rel_err_rows(out, ref) <= 2e-2
+        with open(os.path.join(out_dir, f"ok{rank}"), "w") as f:
+            f.write("ok")
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sequence_sharded_step_matches_oracle():
+    if torch.cuda.device_count() < WORLD:
+        pytest.skip(f"needs {WORLD} GPUs")
+    import torch.multiprocessing as mp
+
+    with tempfile.TemporaryDirectory() as d:
+        ctx = mp.start_processes(_seq_worker, args=(_free_port(), d), nprocs=WORLD, join=False,
+                                 start_method="spawn")
+        deadline = time.time() + 300
+        while not ctx.join(timeout=5):
+            if time.time() > deadline:
+                for p in ctx.processes:
+                    if p.is_alive():
+                        p.kill()
+                pytest.fail("sequence-sharded ranks did not finish in 300 s")
+        assert all(os.path.exists(os.path.join(d, f"ok{r}")) for r in range(WORLD))
