@@ -18,6 +18,7 @@
  * Layouts (all innermost-contiguous, element type = store dtype):
  *   cold_k, cold_v  [B, Hkv, cold_capacity, D]   token slots of this shard
  *   summaries       [B, Hkv, cold_capacity / S, D] mean-K of each finalized page
+ *                   (shard_count * (cold_capacity / S + 1) pages with replicated summaries)
  *   hot_k, hot_v    [B, Hkv, hot_capacity, D]    ring: logical hot row j lives
  *                                                 at slot (hot_start + j) % hot_capacity
  * Sharding: global page p lives on shard p % shard_count at local page
@@ -102,8 +103,22 @@ typedef struct kiv_store {
   int64_t host_capacity;    /* token slots of the pinned host tier (multiple of page_size) */
   void *host_k, *host_v;    /* pinned, device-mapped host memory [B, Hkv, host_capacity, D] */
   int32_t stage_pages;      /* staging pages at the end of the HBM cold slots */
-  int32_t reserved;
+  int32_t flags;            /* KIV_STORE_* */
+  /* replicated summaries (KIV_STORE_REPL_SUMMARIES): fp32 running sums of the
+   * rows of the page being filled, [B, Hkv, D] */
+  float *page_sums;
 } kiv_store;
+
+/* kiv_store.flags */
+#define KIV_STORE_REPL_SUMMARIES 1
+/* With shard_count > 1: every shard keeps the summary of EVERY global page
+ * (summaries [B, Hkv, shard_count * (cold_capacity / S + 1), D], indexed by
+ * global page), updated by each eviction from the rows it moves (all shards see them:
+ * the hot window is replicated) and the running sums in page_sums.  The
+ * coarse pass then scores every page on every shard and finds the exact
+ * global per-row top pages locally: kiv_coarse_select marks this shard's
+ * pages of the global union for the fine pass and no coarse exchange is
+ * needed.  Not combined with a host tier. */
 
 typedef struct kiv_query {
   const void *q;            /* [B, Hq, Q, D] store dtype, innermost contiguous */
@@ -168,7 +183,9 @@ KIV_API kiv_status kiv_append_evict(const kiv_store *st, const void *k_new, cons
  *   workspace for kiv_fine_select, and row_scores/row_pages may be NULL.
  * shard_count > 1: each row's local top list is written to row_scores /
  *   row_pages [R, top_pages] (R = B*Hq*Q; unused tail entries have page -1)
- *   for an all-gather, followed by kiv_coarse_merge.
+ *   for an all-gather, followed by kiv_coarse_merge -- or, with replicated
+ *   summaries, the global union's pages of this shard are marked directly
+ *   (row_scores / row_pages may be NULL; no merge follows).
  * Replaces: kiv/cold_store.py:203-230 (_repeat_kv + matmul, topk, unique).
  */
 KIV_API kiv_status kiv_coarse_select(const kiv_store *st, const kiv_query *q, void *ws, size_t ws_bytes,

@@ -25,6 +25,7 @@ KEEP_DIRECT = -2
 STATE_WORDS = 32
 ST_COLD_LEN, ST_HOT_START, ST_HOT_LEN, ST_UNION, ST_CAND, ST_SEL, ST_SEL_LOCAL, ST_ERROR = range(8)
 ST_COARSE_MAX, ST_COARSE_SUM, ST_FINE_MAX, ST_FINE_SUM = 8, 9, 10, 11
+ST_PAGESUM_SLOT = 21   # replicated summaries: which page_sums slot holds the carried sum
 
 c_i32, c_i64, c_f32, c_vp, c_sz = ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p, ctypes.c_size_t
 
@@ -40,7 +41,10 @@ class StoreDesc(ctypes.Structure):
                 ("hot_capacity", c_i64), ("cold_k", c_vp), ("cold_v", c_vp),
                 ("summaries", c_vp), ("hot_k", c_vp), ("hot_v", c_vp), ("state", c_vp),
                 ("host_capacity", c_i64), ("host_k", c_vp), ("host_v", c_vp), ("stage_pages", c_i32),
-                ("reserved", c_i32)]
+                ("flags", c_i32), ("page_sums", c_vp)]
+
+
+STORE_REPL_SUMMARIES = 1
 
 
 class QueryDesc(ctypes.Structure):

@@ -75,6 +75,7 @@ class ColdKVStore:
         # pinned host overflow tier (kiv_host_alloc'd, freed with the store)
         self._host_k = self._host_v = None
         self._host_tokens = 0
+        self._page_sums: torch.Tensor | None = None
         self._hk = self._hv = None
         self._hot_cap = 0
         self._state: torch.Tensor | None = None
@@ -151,16 +152,28 @@ class ColdKVStore:
         pages = math.ceil(global_tokens / self._page_size)
         return max(1, self._local_pages(pages)) * self._page_size
 
+    @property
+    def replicated_summaries(self) -> bool:
+        """Page-sharded stores keep every global page's summary on every shard:
+        the coarse pass is then exact on each shard with no exchange."""
+        return self._shard_count > 1 and self.kiv_config.host_tokens == 0
+
     def _alloc_cold(self, cap: int) -> None:
         B, H, D, S = self._batch, self._num_kv_heads, self._head_dim, self._page_size
         k = torch.empty(B, H, cap, D, dtype=self._dtype, device=self.device)
         v = torch.empty_like(k)
-        s = torch.empty(B, H, cap // S, D, dtype=self._dtype, device=self.device)
+        # summaries: this shard's pages, or every global page the shards hold
+        # (their local page counts differ by at most one)
+        n_summ = (cap // S + 1) * self._shard_count if self.replicated_summaries else cap // S
+        s = torch.empty(B, H, n_summ, D, dtype=self._dtype, device=self.device)
+        if self.replicated_summaries and self._page_sums is None:
+            # running fp32 sums of the page being filled (two slots: read one, write the other)
+            self._page_sums = torch.zeros(2, B, H, D, dtype=torch.float32, device=self.device)
         if self._k is not None:
             old = self._k.shape[2]
             k[:, :, :old].copy_(self._k)
             v[:, :, :old].copy_(self._v)
-            s[:, :, :old // S].copy_(self._summ)
+            s[:, :, :self._summ.shape[2]].copy_(self._summ)
         self._k, self._v, self._summ = k, v, s
         self._desc = None
         self._op_tensors = None
@@ -278,8 +291,11 @@ class ColdKVStore:
                 self._k.data_ptr(), self._v.data_ptr(), self._summ.data_ptr(),
                 nat.ptr(self._hk), nat.ptr(self._hv), self._state.data_ptr(),
                 self._host_tokens, nat.ptr(self._host_k), nat.ptr(self._host_v),
-                self.kiv_config.stage_pages if self.tiered else 0, 0)
+                self.kiv_config.stage_pages if self.tiered else 0, self._store_flags(), nat.ptr(self._page_sums))
         return self._desc
+
+    def _store_flags(self) -> int:
+        return nat.STORE_REPL_SUMMARIES if self.replicated_summaries else 0
 
     def _op_store(self, hot_hint: int = 0):
         """The store as the operators take it: (8 tensors, 5 ints)."""
@@ -289,9 +305,10 @@ class ColdKVStore:
                                 self._hk if self._hk is not None else empty,
                                 self._hv if self._hv is not None else empty, self._state,
                                 self._host_k if self._host_k is not None else empty,
-                                self._host_v if self._host_v is not None else empty]
+                                self._host_v if self._host_v is not None else empty,
+                                self._page_sums if self._page_sums is not None else empty]
         geom = [self._page_size, self._shard_rank, self._shard_count, int(hot_hint),
-                self.kiv_config.stage_pages if self.tiered else 0]
+                self.kiv_config.stage_pages if self.tiered else 0, self._store_flags()]
         return self._op_tensors, geom
 
     def _empty(self) -> torch.Tensor:
@@ -621,6 +638,11 @@ class ColdKVStore:
     def _sharded_coarse(self, qa: tuple, ws, R: int, K: int) -> None:
         kv = ops.kiv()
         so = self._op_store()
+        if self.replicated_summaries:
+            # every shard scores every page: the exact global union, this shard's
+            # pages of it marked for the fine pass, no exchange
+            ops.call(kv.coarse_select, *so, *qa, ws, None, None)
+            return
         sc = self._buffer("crow_s", (R, K), torch.float32)
         pg = self._buffer("crow_p", (R, K), torch.int32)
         ops.call(kv.coarse_select, *so, *qa, ws, sc, pg)
@@ -672,10 +694,13 @@ class ColdKVStore:
             return [int(x) for x in self._state.cpu().tolist()]
 
     def page_summaries(self) -> torch.Tensor | None:
-        """Summaries of this shard's finalized pages ``[B, Hkv, local pages, D]``."""
+        """Summaries of the finalized pages this shard holds: ``[B, Hkv, pages, D]``
+        -- every global page with replicated summaries (page-sharded stores),
+        else this shard's pages in local order."""
         if self._summ is None:
             return None
-        return self._summ[:, :, :self._local_pages(self.num_pages)]
+        n = self.num_pages if self.replicated_summaries else self._local_pages(self.num_pages)
+        return self._summ[:, :, :n]
 
     def reset(self) -> None:
         """Clear all cold storage and the hot window (buffers are kept for reuse)."""
@@ -713,7 +738,8 @@ class ColdKVStore:
         return {
             "k_index_cpu": host_k,
             "v_store_cpu": host_v,
-            "page_summaries_gpu": self._local_pages(self.num_pages) * row,
+            "page_summaries_gpu": (self.num_pages if self.replicated_summaries
+                                   else self._local_pages(self.num_pages)) * row,
             "partial_gpu": 2 * part * row,
             "cold_k_gpu": local_fin * row,
             "cold_v_gpu": local_fin * row,

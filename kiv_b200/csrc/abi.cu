@@ -103,6 +103,17 @@ static kiv_status check_store(const kiv_store *st) {
     set_error("host_capacity %lld not a multiple of page_size", (long long)st->host_capacity);
     return KIV_ERR_ARG;
   }
+  if (st->flags & ~KIV_STORE_REPL_SUMMARIES) { set_error("unknown store flags 0x%x", st->flags); return KIV_ERR_ARG; }
+  if (repl_summaries(*st)) {
+    if (st->host_capacity > 0) {
+      set_error("replicated summaries are not combined with a host tier");
+      return KIV_ERR_UNSUPPORTED;
+    }
+    if (!st->page_sums || !aligned16(st->page_sums)) {
+      set_error("replicated summaries need page_sums (fp32 [B, Hkv, D], 16-byte aligned)");
+      return KIV_ERR_ARG;
+    }
+  }
   if (st->host_capacity > 0) {
     if (!st->host_k || !st->host_v || !aligned16(st->host_k) || !aligned16(st->host_v)) {
       set_error("host tier missing or not 16-byte aligned");
@@ -222,8 +233,8 @@ kiv_status kiv_coarse_select(const kiv_store *st, const kiv_query *q, void *ws, 
   KIV_TRY(check_query(st, q));
   Workspace w;
   KIV_TRY(check_ws(st, q, ws, ws_bytes, w));
-  if (st->shard_count > 1 && (!row_scores || !row_pages)) {
-    set_error("sharded coarse_select needs row_scores/row_pages");
+  if (st->shard_count > 1 && !repl_summaries(*st) && (!row_scores || !row_pages)) {
+    set_error("sharded coarse_select needs row_scores/row_pages (or replicated summaries)");
     return KIV_ERR_ARG;
   }
   return launch_coarse(st, q, w, row_scores, row_pages, (cudaStream_t)stream);

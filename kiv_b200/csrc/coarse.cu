@@ -53,7 +53,7 @@ coarse_scores_kernel(kiv_store st, kiv_query q, Workspace w) {
   const int rows_kv = G * Q;
   const int nchunks = (rows_kv + RCH - 1) / RCH;
   const int64_t np_global = st_ld(st.state, KIV_ST_COLD_LEN) / S;
-  const int64_t np = local_pages(np_global, st.shard_rank, st.shard_count);
+  const int64_t np = coarse_pages(st, np_global);
   clear_stale_marks(st, w, np);
   const int64_t nblk = (np + CS_PAGES - 1) / CS_PAGES;
   const int64_t items = (int64_t)st.batch * H * nchunks * nblk;
@@ -168,7 +168,7 @@ coarse_topk_kernel(kiv_store st, kiv_query q, Workspace w, float *row_scores, in
   // the cold length was published by the eviction, two kernels back
   const int S = st.page_size;
   const int64_t np_global = st_ld(st.state, KIV_ST_COLD_LEN) / S;
-  const int64_t np = local_pages(np_global, st.shard_rank, st.shard_count);
+  const int64_t np = coarse_pages(st, np_global);
   __syncthreads();
   griddep_wait();
   const int row = blockIdx.x;
@@ -180,9 +180,16 @@ coarse_topk_kernel(kiv_store st, kiv_query q, Workspace w, float *row_scores, in
   float *src = w.scores + (int64_t)row * w.np_cap;
   float *ls = row_scores ? row_scores + (int64_t)row * K : nullptr;
   int32_t *lpg = row_pages ? row_pages + (int64_t)row * K : nullptr;
+  const bool repl = repl_summaries(st);
   auto emit_page = [&](int64_t lp, uint32_t pos, uint32_t key) {
     if (nsh == 1) {
       atomicOr(&w.pbits[lp >> 5], 1u << (lp & 31));
+    } else if (repl) {
+      // lp is a global page: mark it (by its local index) when this shard owns it
+      if (lp % nsh == rank) {
+        const int64_t l = lp / nsh;
+        atomicOr(&w.pbits[l >> 5], 1u << (l & 31));
+      }
     } else if (pos < (uint32_t)K) {
       ls[pos] = key2f(key);
       lpg[pos] = (int32_t)(lp * nsh + rank);
@@ -247,7 +254,7 @@ coarse_topk_kernel(kiv_store st, kiv_query q, Workspace w, float *row_scores, in
                                   [&](int i, uint32_t pos) { emit_page(i, pos, gk[i]); });
     }
   }
-  if (nsh > 1) {
+  if (nsh > 1 && !repl) {
     for (int j = (int)k + threadIdx.x; j < K; j += TK_THREADS) {
       ls[j] = 0.f;
       lpg[j] = -1;
@@ -258,7 +265,7 @@ coarse_topk_kernel(kiv_store st, kiv_query q, Workspace w, float *row_scores, in
   if (pre)
     for (int i = threadIdx.x; i < SEL_BINS; i += TK_THREADS) w.chist[(int64_t)row * SEL_BINS + i] = 0;
   if (row == 0 && threadIdx.x == 0) {
-    if (nsh == 1) st.state[KIV_ST_UNION_PENDING] = 1;
+    if (nsh == 1 || repl) st.state[KIV_ST_UNION_PENDING] = 1;
     const unsigned long long mk = w.cstat[0], sb = w.cstat[1];
     if (mk) atomicMax(reinterpret_cast<unsigned long long *>(st.state + KIV_ST_COARSE_MAX), mk);
     atomicAdd(reinterpret_cast<double *>(st.state + KIV_ST_COARSE_SUM), __longlong_as_double((long long)sb));
@@ -302,12 +309,19 @@ coarse_rows_topk_kernel(kiv_store st, kiv_query q, Workspace w, float *row_score
   const int nsh = st.shard_count, rank = st.shard_rank;
   griddep_wait();
   const int64_t np_global = st_ld(st.state, KIV_ST_COLD_LEN) / S;
-  const int64_t np = local_pages(np_global, rank, nsh);
+  const int64_t np = coarse_pages(st, np_global);
+  const bool repl = repl_summaries(st);
+  const bool marks = nsh == 1 || repl;
   const int K = q.top_pages;
   const uint32_t k = (uint32_t)(K < np ? (int64_t)K : np);
   const unsigned lt = (1u << lane) - 1u;
   __syncthreads();
   auto mark = [&](int64_t i) {
+    if (repl) {
+      // i is a global page: marked by its local index when this shard owns it
+      if (i % nsh != rank) return;
+      i /= nsh;
+    }
     if (nwords > 0) atomicOr(&bits[i >> 5], 1u << (i & 31));
     else atomicOr(&w.pbits[i >> 5], 1u << (i & 31));
   };
@@ -394,7 +408,7 @@ coarse_rows_topk_kernel(kiv_store st, kiv_query q, Workspace w, float *row_score
         const bool in = i < np;
         const bool up = in && (all || (key & mask) > prefix);
         const bool bnd = in && !all && (key & mask) == prefix;
-        if (up && nsh == 1) mark(i);
+        if (up && marks) mark(i);
         const unsigned bb = __ballot_sync(KIV_FULL_MASK, bnd);
         if (bnd) {
           const int pos = nb + __popc(bb & lt);
@@ -423,10 +437,10 @@ coarse_rows_topk_kernel(kiv_store st, kiv_query q, Workspace w, float *row_score
         take = r < remaining;
       }
       cflag[j] = take ? 1 : 0;
-      if (take && nsh == 1) mark(cidx[j]);
+      if (take && marks) mark(cidx[j]);
     }
     __syncwarp();
-    if (nsh > 1) {
+    if (!marks) {
       // this rank's list of the row, (score, global page) in page order
       int pos = 0, bi = 0;
       for (int64_t base = 0; base < np; base += 32) {
@@ -462,7 +476,7 @@ coarse_rows_topk_kernel(kiv_store st, kiv_query q, Workspace w, float *row_score
     for (int i = threadIdx.x; i < nwords; i += RT_THREADS)
       if (bits[i]) atomicOr(&w.pbits[i], bits[i]);
   if (blockIdx.x == 0 && threadIdx.x == 0) {
-    if (nsh == 1) st.state[KIV_ST_UNION_PENDING] = 1;
+    if (marks) st.state[KIV_ST_UNION_PENDING] = 1;
     const unsigned long long mk = w.cstat[0], sb = w.cstat[1];
     if (mk) atomicMax(reinterpret_cast<unsigned long long *>(st.state + KIV_ST_COARSE_MAX), mk);
     atomicAdd(reinterpret_cast<double *>(st.state + KIV_ST_COARSE_SUM), __longlong_as_double((long long)sb));

@@ -52,6 +52,12 @@ append_evict_kernel(kiv_store st, const T *__restrict__ k_new, const T *__restri
   if (n_ev > 0 && last_page >= st.shard_rank &&
       ((last_page - st.shard_rank) / st.shard_count + 1) > (tiered ? summary_pages(st) : st.cold_capacity / S))
     ok = false;
+  // replicated summaries: every global page the rows reach needs a summary row
+  const bool repl = repl_summaries(st);
+  if (repl && n_ev > 0 && last_page >= summary_pages(st)) ok = false;
+  // the running sum of a page that spans calls: read from one slot, written to
+  // the other (a call may read the first page's sum and write the last page's)
+  const int64_t ps_in = repl ? st_ld(st.state, ST_PAGESUM_SLOT) & 1 : 0;
   // with a host tier one call may reach at most `ring` local pages (each ring
   // slot is spilled once, before this call overwrites it)
   if (tiered && pages_per_bh > ring) ok = false;
@@ -69,6 +75,33 @@ append_evict_kernel(kiv_store st, const T *__restrict__ k_new, const T *__restri
     const int64_t hi_all = cold_len + n_ev;
     const int64_t hi = hi_all < (p + 1) * S ? hi_all : (p + 1) * S;
     const bool owned = (p % st.shard_count) == st.shard_rank;
+    if (repl && lo < hi) {
+      // every shard: summary of a page completed here, or the running sum of
+      // the page left incomplete -- fp32 adds of the page's rows in token
+      // order from 0 (the sum carried in from earlier calls first), the same
+      // operations as the summary over the cold slots below
+      const int64_t nsl = (int64_t)st.batch * H * D;
+      const float *sum_in = st.page_sums + ps_in * nsl + (int64_t)bh * D;
+      float *sum_out = st.page_sums + (1 - ps_in) * nsl + (int64_t)bh * D;
+      for (int c = threadIdx.x; c < D; c += EV_THREADS) {
+        float acc = lo > p * S ? sum_in[c] : 0.f;
+        for (int64_t g = lo; g < hi; ++g) {
+          const int64_t j = g - cold_len;
+          const T *src;
+          if (!direct && j < hot_len) {
+            src = reinterpret_cast<const T *>(st.hot_k) + ((int64_t)bh * hcap + (hot_start + j) % hcap) * D;
+          } else {
+            src = k_new + b * sb + h * sh + (direct ? j : j - hot_len) * stt;
+          }
+          acc += Elem<T>::to_f(src[c]);
+        }
+        if (hi == (p + 1) * S)
+          reinterpret_cast<T *>(st.summaries)[((int64_t)bh * summary_pages(st) + p) * D + c] =
+              Elem<T>::from_f(acc / (float)S);
+        else
+          sum_out[c] = acc;
+      }
+    }
     if (lo < hi && owned) {
       const int64_t lp = p / st.shard_count;
       const int64_t slot = tiered ? lp % ring : lp;
@@ -104,7 +137,7 @@ append_evict_kernel(kiv_store st, const T *__restrict__ k_new, const T *__restri
         st16(ck + off, ld16(sk + vi * V));
         st16(cv + off, ld16(sv + vi * V));
       }
-      if (hi == (p + 1) * S) {
+      if (hi == (p + 1) * S && !repl) {
         // the page is complete: summary = (sum of its rows in token order) / S
         __syncthreads();
         T *sm = reinterpret_cast<T *>(st.summaries) + ((int64_t)bh * summary_pages(st) + lp) * D;
@@ -141,6 +174,7 @@ append_evict_kernel(kiv_store st, const T *__restrict__ k_new, const T *__restri
     if (threadIdx.x == 0) {
       if (ok) {
         st.state[KIV_ST_COLD_LEN] = cold_len + n_ev;
+        if (repl && n_ev > 0) st.state[ST_PAGESUM_SLOT] = 1 - ps_in;
         if (!direct) {
           st.state[KIV_ST_HOT_START] = hcap > 0 ? (hot_start + n_ev) % hcap : 0;
           st.state[KIV_ST_HOT_LEN] = hot_after;

@@ -174,7 +174,9 @@ scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_que
   // per batch row b.  FINE: one unit per candidate page (tiles = its KV
   // heads); COARSE: one unit per block of 128 finalized local pages (tiles =
   // KV heads).  CTA cj of the row's cpb takes units cj, cj + cpb, ...
-  const int64_t units = COARSE ? (np_local + TC_PAGE - 1) / TC_PAGE : f.per_b;
+  // coarse: the pages this shard scores (all of them with replicated summaries)
+  const int64_t np_scored = COARSE ? coarse_pages(st, f.np_global) : np_local;
+  const int64_t units = COARSE ? (np_scored + TC_PAGE - 1) / TC_PAGE : f.per_b;
   const int64_t my_units = units > cj ? (units - cj + cpb - 1) / cpb : 0;
   const int64_t my_tiles = my_units * H;
   const int64_t bh0 = (int64_t)b * H;
@@ -247,7 +249,7 @@ scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_que
         for (int c0 = 0; c0 < ncols; c0 += 16) {
           tc::ld_32x16(taddr + c0, r);
           tc::wait_ld();
-          if (p < np_local) {
+          if (p < np_scored) {
 #pragma unroll
             for (int c = 0; c < 16; ++c) {
               const int rr = c0 + c;

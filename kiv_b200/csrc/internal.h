@@ -20,6 +20,7 @@ enum : int {
   CTR_MERGE = 18,
   CTR_FINE = 19,
   CTR_SEL = 20,
+  ST_PAGESUM_SLOT = 21,   // replicated summaries: which page_sums slot holds the carried sum
 };
 
 constexpr int ATT_TILE = 32;     // keys per attention tile
@@ -50,9 +51,28 @@ Workspace workspace_layout(const kiv_store *st, const kiv_query *q, void *base);
 __host__ __device__ inline int64_t ring_pages(const kiv_store &st) {
   return st.cold_capacity / st.page_size - (st.host_capacity > 0 ? st.stage_pages : 0);
 }
-// local pages the summaries (and the page slot table) cover
+// every shard keeps the summaries of all global pages (and scores them all)
+__host__ __device__ inline bool repl_summaries(const kiv_store &st) {
+  return st.shard_count > 1 && (st.flags & KIV_STORE_REPL_SUMMARIES) != 0;
+}
+// pages the summaries (and the page slot table) cover: local pages, or every
+// global page the shards' slots can hold when summaries are replicated (the
+// shards of one store hold local page counts that differ by at most one)
 __host__ __device__ inline int64_t summary_pages(const kiv_store &st) {
+  if (repl_summaries(st)) return (st.cold_capacity / st.page_size + 1) * st.shard_count;
   return st.host_capacity > 0 ? ring_pages(st) + st.host_capacity / st.page_size : st.cold_capacity / st.page_size;
+}
+// pages of this shard among the first np_global global pages (p % count == rank)
+__host__ __device__ inline int64_t shard_local_pages(int64_t np_global, int rank, int count) {
+  return np_global > rank ? (np_global - rank + count - 1) / count : 0;
+}
+// pages the coarse pass scores: all of them with replicated summaries, else this shard's
+__host__ __device__ inline int64_t coarse_pages(const kiv_store &st, int64_t np_global) {
+  return repl_summaries(st) ? np_global : shard_local_pages(np_global, st.shard_rank, st.shard_count);
+}
+// global page id of the i-th scored page
+__host__ __device__ inline int64_t coarse_page_id(const kiv_store &st, int64_t i) {
+  return repl_summaries(st) ? i : i * st.shard_count + st.shard_rank;
 }
 // HBM page slot to read local page lp from in this step: identity without a host
 // tier; otherwise the slot the staging kernel recorded (ring slot, or a staging

@@ -128,7 +128,9 @@ prefill_scores_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
   }
   // units of one (batch row, KV head): coarse -- blocks of 128 local pages;
   // fine -- the union pages plus the partial page
-  const int64_t units = COARSE ? (np_local + PF_TILE - 1) / PF_TILE : U + (part_owned ? 1 : 0);
+  // coarse: the pages this shard scores (all of them with replicated summaries)
+  const int64_t np_scored = coarse_pages(st, np_global);
+  const int64_t units = COARSE ? (np_scored + PF_TILE - 1) / PF_TILE : U + (part_owned ? 1 : 0);
   const int64_t my_units = (nb > 0 && units > j) ? (units - j + g.nj - 1) / g.nj : 0;
   const int64_t BH = (int64_t)st.batch * H;
 
@@ -230,7 +232,7 @@ prefill_scores_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
           const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(a * g.nt);
           if (COARSE) {
             const int64_t p = u * PF_TILE + row;
-            const bool live = p < np_local;
+            const bool live = p < np_scored;
             float *dst = w.scores + (((int64_t)b * Hq + kvh * G + gi) * Q + t0) * w.np_cap + p;
             for (int c0 = 16 * half; c0 < g.nt; c0 += 32) {
               uint32_t r[16];

@@ -9,9 +9,10 @@
 // (shape-only, no work) for tracing with fake tensors.
 //
 // A store is passed as two lists:
-//   store = [cold_k, cold_v, summaries, hot_k, hot_v, state, host_k, host_v]
-//           (hot_* and host_* may be empty tensors: no hot ring / no host tier)
-//   geom  = [page_size, shard_rank, shard_count, hot_hint, stage_pages]
+//   store = [cold_k, cold_v, summaries, hot_k, hot_v, state, host_k, host_v, page_sums]
+//           (hot_*, host_* and page_sums may be empty tensors: no hot ring,
+//           no host tier, no replicated summaries)
+//   geom  = [page_size, shard_rank, shard_count, hot_hint, stage_pages, flags]
 // and a query as (q [B, Hq, Q, D], scaling, top_pages, top_p, softcap).
 // The operators that write return nothing and declare what they mutate in
 // their schema.  Failures raise RuntimeError with the library's message.
@@ -41,10 +42,10 @@ int32_t dtype_code(const Tensor &t) {
 }
 
 kiv_store make_store(at::TensorList s, at::IntArrayRef g) {
-  TORCH_CHECK(s.size() == 8, "kiv: store list must hold 8 tensors (cold_k, cold_v, summaries, hot_k, hot_v, "
-                             "state, host_k, host_v), got ", s.size());
-  TORCH_CHECK(g.size() == 5, "kiv: geom must hold 5 ints (page_size, shard_rank, shard_count, hot_hint, "
-                             "stage_pages), got ", g.size());
+  TORCH_CHECK(s.size() == 9, "kiv: store list must hold 9 tensors (cold_k, cold_v, summaries, hot_k, hot_v, "
+                             "state, host_k, host_v, page_sums), got ", s.size());
+  TORCH_CHECK(g.size() == 6, "kiv: geom must hold 6 ints (page_size, shard_rank, shard_count, hot_hint, "
+                             "stage_pages, flags), got ", g.size());
   const Tensor &ck = s[0], &hk = s[3], &st = s[5], &hok = s[6];
   TORCH_CHECK(ck.dim() == 4, "kiv: cold_k must be [B, Hkv, slots, D]");
   TORCH_CHECK(st.scalar_type() == at::kLong && st.numel() >= KIV_STATE_WORDS, "kiv: state must be int64[32]");
@@ -69,6 +70,8 @@ kiv_store make_store(at::TensorList s, at::IntArrayRef g) {
   d.host_k = ptr_or_null(s[6]);
   d.host_v = ptr_or_null(s[7]);
   d.stage_pages = (int32_t)g[4];
+  d.flags = (int32_t)g[5];
+  d.page_sums = static_cast<float *>(ptr_or_null(s[8]));
   return d;
 }
 
@@ -305,7 +308,7 @@ void attend_exchange_merge(at::TensorList store, at::IntArrayRef geom, const Ten
 // pointers are stand-ins), so the same kernel serves real and fake tensors.
 std::vector<int64_t> workspace_layout(at::TensorList store, at::IntArrayRef geom, const Tensor &q,
                                       int64_t top_pages, int64_t top_p) {
-  TORCH_CHECK(store.size() == 8 && geom.size() == 5, "kiv: bad store descriptor lists");
+  TORCH_CHECK(store.size() == 9 && geom.size() == 6, "kiv: bad store descriptor lists");
   const Tensor &ck = store[0], &hk = store[3], &hok = store[6];
   TORCH_CHECK(ck.dim() == 4 && q.dim() == 4, "kiv: bad store or query rank");
   char *fake = reinterpret_cast<char *>(uintptr_t(1) << 20);
@@ -326,6 +329,8 @@ std::vector<int64_t> workspace_layout(at::TensorList store, at::IntArrayRef geom
   st.host_capacity = hok.numel() > 0 ? hok.size(2) : 0;
   st.host_k = st.host_v = st.host_capacity > 0 ? fake : nullptr;
   st.stage_pages = (int32_t)geom[4];
+  st.flags = (int32_t)geom[5];
+  st.page_sums = store[8].numel() > 0 ? reinterpret_cast<float *>(fake) : nullptr;
   kiv_query qd = {};
   qd.q = fake;
   // strides of a contiguous query (only their 16-byte alignment is checked)

@@ -8,11 +8,11 @@ cold store calls the kernels through these operators; ``_native`` (ctypes)
 remains for the host-only calls (peer and pinned-host allocation, exchange
 sizing) and for tests of the raw ABI.
 
-A store crosses as ``(store, geom)``: eight tensors ``[cold_k, cold_v,
-summaries, hot_k, hot_v, state, host_k, host_v]`` (empty tensors for a missing
-hot ring or host tier) and five ints ``[page_size, shard_rank, shard_count,
-hot_hint, stage_pages]``.  There is no fallback: a missing operator library
-raises.
+A store crosses as ``(store, geom)``: nine tensors ``[cold_k, cold_v,
+summaries, hot_k, hot_v, state, host_k, host_v, page_sums]`` (empty tensors
+for a missing hot ring, host tier or running page sums) and six ints
+``[page_size, shard_rank, shard_count, hot_hint, stage_pages, flags]``.
+There is no fallback: a missing operator library raises.
 """
 
 from __future__ import annotations

@@ -16,8 +16,16 @@ cold_len, hot_len, blocks ({name: [offset, nbytes]}) and an optional "meta"
 dict of the caller.  Page summaries are not stored: loading replays the cold
 rows through the eviction kernel, which rebuilds them bit for bit, and the
 rows land in whichever tier (HBM ring or pinned host memory) the loading
-store's configuration puts them.  Stores sharded over GPUs are saved rank by
-rank by their owner and are not handled here.
+store's configuration puts them.
+
+A page-sharded store (one process per GPU) is saved rank by rank: each rank's
+file holds the rows of its own pages in local page order (``cold_k``,
+``cold_v`` [B, Hkv, local_rows, D]), the replicated hot window, every global
+page's summary (``summaries`` [B, Hkv, pages, D]) and the running sums of the
+page being filled (``page_sums`` fp32 [2, B, Hkv, D]); the header adds a
+``shard`` entry {rank, count, local_rows, page_sum_slot}.  Such a file loads
+into an empty store of the same rank and shard count by plain copies (the
+other ranks' rows, which rebuilt summaries would need, are not on this rank).
 """
 
 from __future__ import annotations
@@ -28,6 +36,8 @@ import os
 import struct
 
 import torch
+
+from . import _native as nat
 
 MAGIC = b"KIVSTOR1"
 VERSION = 1
@@ -60,21 +70,38 @@ def _cold_rows(store) -> tuple[torch.Tensor, torch.Tensor]:
     return torch.cat(parts_k, dim=2), torch.cat(parts_v, dim=2)
 
 
+def _local_rows(store) -> int:
+    """Rows of a page-sharded store's own pages (a prefix of its token slots)."""
+    S, N, r = store._page_size, store._shard_count, store._shard_rank
+    full = store._local_pages(store.num_pages) * S
+    part = store._partial_len if store.num_pages % N == r else 0
+    return full + part
+
+
 def save_store(store, path: str, meta: dict | None = None) -> dict:
     """Write one store to `path`; returns the header."""
-    if store._shard_count != 1:
-        raise NotImplementedError("persistence of page-sharded stores is per rank and not handled here")
     if store._state is None:
         raise RuntimeError("the store holds nothing yet")
     if store.device.type == "cuda":
         torch.cuda.synchronize(store.device)
-    ck, cv = _cold_rows(store)
     hk, hv = store.hot_keys().cpu(), store.hot_values().cpu()
-    blobs = {"cold_k": ck, "cold_v": cv, "hot_k": hk, "hot_v": hv}
     header = {"format": "kiv_b200 cold store", "version": VERSION, "batch": store._batch,
               "num_kv_heads": store._num_kv_heads, "head_dim": store._head_dim,
               "page_size": store._page_size, "dtype": _DTYPES[store._dtype],
               "cold_len": store.cold_length, "hot_len": store.hot_length, "meta": meta or {}}
+    if store._shard_count == 1:
+        ck, cv = _cold_rows(store)
+        blobs = {"cold_k": ck, "cold_v": cv, "hot_k": hk, "hot_v": hv}
+    else:
+        if not store.replicated_summaries:
+            raise NotImplementedError("page-sharded stores with a host tier are not saved")
+        n = _local_rows(store)
+        words = store.read_state()
+        blobs = {"cold_k": store._k[:, :, :n].cpu(), "cold_v": store._v[:, :, :n].cpu(), "hot_k": hk,
+                 "hot_v": hv, "summaries": store.page_summaries().cpu(),
+                 "page_sums": store._page_sums.cpu()}
+        header["shard"] = {"rank": store._shard_rank, "count": store._shard_count, "local_rows": n,
+                           "page_sum_slot": int(words[nat.ST_PAGESUM_SLOT]) & 1}
     # offsets depend on the header length: fix the block table with a first pass
     blocks = {name: [0, t.numel() * t.element_size()] for name, t in blobs.items()}
     prev = None
@@ -116,7 +143,7 @@ def read_header(path: str) -> dict:
 
 def _read_block(path: str, header: dict, name: str, shape: tuple) -> torch.Tensor:
     off, nbytes = header["blocks"][name]
-    dt = _FROM_NAME[header["dtype"]]
+    dt = torch.float32 if name == "page_sums" else _FROM_NAME[header["dtype"]]
     with open(path, "rb") as f:
         f.seek(off)
         raw = bytearray(f.read(nbytes))
@@ -129,16 +156,27 @@ def load_store(store, path: str, chunk: int = 65536) -> dict:
     """Fill an empty store from `path`: cold rows through the eviction kernel
     (summaries rebuilt), then the hot window.  Returns the header."""
     header = read_header(path)
-    if store._shard_count != 1:
-        raise NotImplementedError("persistence of page-sharded stores is per rank and not handled here")
     if store._state is not None and (store.cold_length or store.hot_length):
         raise RuntimeError("load_store needs an empty store")
+    shard = header.get("shard")
+    mine = (getattr(store, "_shard_rank", 0), store._shard_count)
+    if (shard is None) != (mine[1] == 1) or (shard is not None and (shard["rank"], shard["count"]) != mine):
+        raise ValueError(f"{path}: saved for shard {shard and (shard['rank'], shard['count'])}, the store is "
+                         f"shard {mine}")
     geo = (store._num_kv_heads, store._head_dim, store._page_size)
     if (header["num_kv_heads"], header["head_dim"], header["page_size"]) != geo:
         raise ValueError(f"{path}: store geometry {header['num_kv_heads'], header['head_dim'], header['page_size']}"
                          f" does not match {geo}")
     B, H, D = header["batch"], header["num_kv_heads"], header["head_dim"]
     n, h = header["cold_len"], header["hot_len"]
+    if shard is not None:
+        _load_shard(store, path, header, B, H, D)
+        if h > 0:
+            store.set_hot(_read_block(path, header, "hot_k", (B, H, h, D)).to(store.device),
+                          _read_block(path, header, "hot_v", (B, H, h, D)).to(store.device))
+        if store.device.type == "cuda":
+            torch.cuda.synchronize(store.device)
+        return header
     ck = _read_block(path, header, "cold_k", (B, H, n, D))
     cv = _read_block(path, header, "cold_v", (B, H, n, D))
     for a in range(0, n, chunk):
@@ -149,3 +187,23 @@ def load_store(store, path: str, chunk: int = 65536) -> dict:
     if store.device.type == "cuda":
         torch.cuda.synchronize(store.device)
     return header
+
+
+def _load_shard(store, path: str, header: dict, B: int, H: int, D: int) -> None:
+    """A page-sharded store's own rows, every page's summary and the running page
+    sums, copied into place; the device state gets the global cold length."""
+    sh = header["shard"]
+    n, local = header["cold_len"], sh["local_rows"]
+    dt = _FROM_NAME[header["dtype"]]
+    store._ensure_alloc(B, dt)
+    store.reserve(n)
+    pages = n // store._page_size
+    if local:
+        store._k[:, :, :local].copy_(_read_block(path, header, "cold_k", (B, H, local, D)).to(store.device))
+        store._v[:, :, :local].copy_(_read_block(path, header, "cold_v", (B, H, local, D)).to(store.device))
+    if pages:
+        store._summ[:, :, :pages].copy_(_read_block(path, header, "summaries", (B, H, pages, D)).to(store.device))
+    store._page_sums.copy_(_read_block(path, header, "page_sums", (2, B, H, D)).to(store.device))
+    store._state[nat.ST_COLD_LEN].fill_(n)
+    store._state[nat.ST_PAGESUM_SLOT].fill_(sh["page_sum_slot"])
+    store._cold_len = n

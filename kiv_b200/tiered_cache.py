@@ -207,9 +207,17 @@ class TieredKVCache(DynamicCache):
         self._decode_step = 0
 
     # ------------------------------------------------------------ persistence
+    def _store_file(self, li: int) -> str:
+        """File of layer li's store: one per layer, and per rank when the cold
+        pages are sharded over GPUs (each rank saves and loads its own)."""
+        if self.shard_comm is not None and self.shard_comm.size > 1:
+            return f"layer_{li}.rank{self.shard_comm.rank}of{self.shard_comm.size}.kivstore"
+        return f"layer_{li}.kivstore"
+
     def save(self, directory: str) -> None:
         """Write every independent layer's store (``kiv_b200.persist`` format,
-        one file per layer) and the cache counters to `directory`."""
+        one file per layer, per rank for page-sharded caches) and the cache
+        counters to `directory`."""
         import json
         import os
 
@@ -218,7 +226,7 @@ class TieredKVCache(DynamicCache):
         os.makedirs(directory, exist_ok=True)
         for li, store in self.cold_stores.items():
             if store.initialized:
-                save_store(store, os.path.join(directory, f"layer_{li}.kivstore"), meta={"layer": li})
+                save_store(store, os.path.join(directory, self._store_file(li)), meta={"layer": li})
         state = {"prefill_complete": self._prefill_complete, "decode_step": self._decode_step,
                  "total_tokens": {str(k): v for k, v in self._total_tokens.items()}}
         with open(os.path.join(directory, "cache.json"), "w") as f:
@@ -235,7 +243,7 @@ class TieredKVCache(DynamicCache):
         with open(os.path.join(directory, "cache.json")) as f:
             state = json.load(f)
         for li, store in self.cold_stores.items():
-            path = os.path.join(directory, f"layer_{li}.kivstore")
+            path = os.path.join(directory, self._store_file(li))
             if not os.path.exists(path):
                 continue
             load_store(store, path)

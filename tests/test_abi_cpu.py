@@ -44,6 +44,7 @@ int main(void) {{
   printf("kiv_mask %zu\\n", sizeof(kiv_mask));
   printf("kiv_exchange %zu\\n", sizeof(kiv_exchange));
   F(kiv_store, cold_capacity) F(kiv_store, hot_capacity) F(kiv_store, cold_k) F(kiv_store, state)
+  F(kiv_store, flags) F(kiv_store, page_sums)
   F(kiv_query, stride_t) F(kiv_query, scaling) F(kiv_query, top_p)
   F(kiv_mask, stride_t) F(kiv_mask, causal)
   F(kiv_exchange, arena) F(kiv_exchange, arena_bytes)

@@ -179,3 +179,64 @@ def test_tiered_decode_graph_matches_eager():
             assert torch.equal(out[0].float().cpu(), outs[i]), f"graph step {i} differs from eager"
         assert store.read_state()[nat.ST_ERROR] == 0
         assert store.cold_length == SPEC.cold_tokens + len(steps) + 1
+
+
+def test_tiered_steps_and_prefill_chunk_match_oracle():
+    """A tiered store (HBM ring of 6 pages, about 1/7 of the cold tier; the rest
+    in pinned host memory) against the oracle itself: at each decode step --
+    steps that complete a page, so a ring slot is spilled and reused -- the
+    page union and token selection equal the oracle's except for ties within
+    1e-6 of the k-th score, and the attention is within 2e-2 of the float64
+    oracle over the same selection; then a prefill-shaped chunk of 64
+    positions (causal over the hot window, union of 1024 query rows staged from
+    the host tier) is checked the same way."""
+    from oracle.kiv_oracle import OracleLayer, OracleStore, causal_hot_mask, eager_attention
+    from tests.gpu_helpers import check_selection, rel_err, rel_err_rows
+
+    prob = make_problem(SPEC, seed=17, dtype=torch.bfloat16)
+    cfg, cache = _cache(tiered=True, ring_pages=6, stage_pages=48, host_pages=64)
+    _prefill(cache, prob)
+    store = cache.get_cold_store(0)
+    assert store.tiered
+    f32 = lambda t: t.float().numpy()
+    ol = OracleLayer(OracleStore(SPEC.batch, SPEC.num_kv_heads, SPEC.head_dim, SPEC.groups, 128, "bf16"),
+                     SPEC.hot_budget)
+    ol.update(f32(prob.prefill_k), f32(prob.prefill_v))
+    ol.mark_prefill_complete()
+    scaling = SPEC.head_dim ** -0.5
+    bf = lambda x: x.to(DEV, torch.bfloat16)
+    pages0 = store.num_pages
+    for i, (q, k, v) in enumerate(_steps(4, seed=31)):
+        cache.update(bf(k), bf(v), 0)
+        ol.update(f32(bf(k).cpu()), f32(bf(v).cpu()))
+        qb = bf(q)
+        sel, P = store.retrieve_indices(qb, scaling, cfg)
+        check_selection(store, ol, f32(qb.cpu()), scaling, cfg, sel, P, storage="bf16")
+        out = store.attend(qb, scaling, cfg)
+        assert store.read_state()[nat.ST_ERROR] == 0, f"step {i}: kernel error bits"
+        ko, vo = ol.store.gather(sel[:, :P].cpu().numpy())
+        ref = eager_attention(f32(qb.cpu()), ko, vo, ol.hot_k, ol.hot_v, scaling)
+        o = out.float().cpu().numpy()
+        assert rel_err(o, ref) <= 2e-2 and rel_err_rows(o, ref) <= 2e-2, f"step {i}"
+    assert store.num_pages > pages0, "no page completed during the steps"
+    # a prefill-shaped chunk: 64 new positions appended to the hot window (no eviction)
+    g = torch.Generator().manual_seed(5)
+    Qn = 64
+    qc = torch.randn(SPEC.batch, SPEC.num_query_heads, Qn, SPEC.head_dim, generator=g)
+    kc = 0.3 * torch.randn(SPEC.batch, SPEC.num_kv_heads, Qn, SPEC.head_dim, generator=g)
+    vc = torch.randn(SPEC.batch, SPEC.num_kv_heads, Qn, SPEC.head_dim, generator=g)
+    cache._prefill_complete = False
+    cache.update(bf(kc), bf(vc), 0)
+    ol.prefill_complete = False
+    ol.update(f32(bf(kc).cpu()), f32(bf(vc).cpu()))
+    qb = bf(qc)
+    sel, P = store.retrieve_indices(qb, scaling, cfg)
+    check_selection(store, ol, f32(qb.cpu()), scaling, cfg, sel, P, storage="bf16")
+    out = store.attend(qb, scaling, cfg, causal=True)
+    assert store.read_state()[nat.ST_ERROR] == 0, "prefill chunk: kernel error bits"
+    ko, vo = ol.store.gather(sel[:, :P].cpu().numpy())
+    hot = ol.hot_k.shape[2]
+    ref = eager_attention(f32(qb.cpu()), ko, vo, ol.hot_k, ol.hot_v, scaling,
+                          hot_mask=causal_hot_mask(SPEC.batch, Qn, hot))
+    o = out.float().cpu().numpy()
+    assert rel_err(o, ref) <= 2e-2 and rel_err_rows(o, ref) <= 2e-2, "prefill chunk"

@@ -7,6 +7,8 @@ through peer memory (``KIV_SHARD_EXCHANGE=peer``, the default) or the process
 group's collectives.  Rank 0 also runs the step unsharded on its GPU and the
 CPU oracle on the same bf16-valued inputs.  Checked on rank 0:
 
+* every shard's page summaries cover all global pages (replicated, so the
+  coarse pass needs no exchange) and equal the oracle's bit for bit;
 * the sharded selection equals the oracle's except for ties within 1e-6
   relative of the top-P boundary score (fine scores of every cold token in
   float64), and the sharded attention is within 2e-2 of the float64 oracle
@@ -67,10 +69,32 @@ def _run_step(shape, dev, shard_group):
     q = prob.query.to(dev)
     scaling = spec.head_dim ** -0.5
     sel, P = store.retrieve_indices(q, scaling, cfg)
+    from tests.gpu_helpers import kernel_union
+    union = kernel_union(store, 1, spec.num_query_heads, 1, cfg)     # this shard's pages of the union
     out = store.attend(q, scaling, cfg)
     torch.cuda.synchronize(dev)
     err = store.read_state()[7]
-    return sel[:, :P].cpu().numpy(), out.float().cpu().numpy(), int(err), (spec, prob, top_pages, top_p)
+    summ = store.page_summaries().float().cpu().numpy()
+    return (sel[:, :P].cpu().numpy(), out.float().cpu().numpy(), int(err),
+            (spec, prob, top_pages, top_p, summ, union))
+
+
+def _union_check(problem, rank):
+    """This shard's pages of the coarse union against the oracle's union
+    (pages p % WORLD == rank), ties within 1e-6 of a row's k-th score aside."""
+    from tests.gpu_helpers import coarse_union_mismatch, oracle_decode
+
+    spec, prob, top_pages, top_p, summ, union = problem
+    f32 = lambda t: t.float().numpy()
+    ol = oracle_decode(spec, f32(prob.prefill_k), f32(prob.prefill_v), f32(prob.step_k), f32(prob.step_v),
+                       storage="bf16")
+    np.testing.assert_array_equal(summ, ol.store.summaries)
+    ref, _, sc = ol.store.coarse(f32(prob.query), spec.head_dim ** -0.5, top_pages)
+    mine = np.array([p for p in ref.tolist() if p % WORLD == rank], np.int64)
+    k = min(top_pages, ol.store.num_pages)
+    bad = coarse_union_mismatch(union, mine, sc, k)
+    assert bad == [], f"rank {rank}: union pages differ from the oracle's beyond ties: {bad[:6]} " \
+                      f"(kernel {len(union)} pages, oracle {len(mine)})"
 
 
 def _oracle_check(sel, out, problem):
@@ -78,12 +102,14 @@ def _oracle_check(sel, out, problem):
     from oracle.kiv_oracle import _group_rows, eager_attention, topk_set_mismatch
     from tests.gpu_helpers import oracle_decode, rel_err, rel_err_rows
 
-    spec, prob, top_pages, top_p = problem
+    spec, prob, top_pages, top_p, summ, _ = problem
     f32 = lambda t: t.float().numpy()
     ol = oracle_decode(spec, f32(prob.prefill_k), f32(prob.prefill_v), f32(prob.step_k), f32(prob.step_v),
                        storage="bf16")
     scaling = spec.head_dim ** -0.5
     q = f32(prob.query)
+    # every shard holds the summary of every page (its own and the other shard's)
+    np.testing.assert_array_equal(summ, ol.store.summaries)
     res = ol.store.retrieve_top_kv(q, scaling, top_pages, top_p)
     # fine scores of every cold token (max over heads and positions), float64
     rows = _group_rows(q.astype(np.float64), spec.num_kv_heads)
@@ -127,14 +153,18 @@ def _worker(rank, port, out_dir, shape, exchange):
     try:
         sel_sh, out_sh, err_sh, problem = _run_step(shape, dev, comm)
         log("sharded step done")
-        if rank == 0:
+        try:
+            _union_check(problem, rank)
+        except AssertionError as e:
+            failure = e
+        if rank == 0 and failure is None:
             sel_1, out_1, err_1, _ = ref
             try:
                 assert err_sh == 0 and err_1 == 0, (err_sh, err_1)
-                _oracle_check(sel_sh, out_sh, problem)
-                log("oracle check done")
                 assert sel_sh.shape == sel_1.shape, (sel_sh.shape, sel_1.shape)
                 assert np.array_equal(sel_sh, sel_1), "sharded selection differs from the single-GPU selection"
+                _oracle_check(sel_sh, out_sh, problem)
+                log("oracle check done")
                 rel = np.abs(out_sh - out_1).max() / max(np.abs(out_1).max(), 1e-30)
                 assert rel <= 1e-2, rel
                 with open(os.path.join(out_dir, "ok"), "w") as f:
@@ -250,4 +280,86 @@ def test_sequence_sharded_step_matches_oracle():
                     if p.is_alive():
                         p.kill()
                 pytest.fail("sequence-sharded ranks did not finish in 300 s")
+        assert all(os.path.exists(os.path.join(d, f"ok{r}")) for r in range(WORLD))
+
+
+def _persist_worker(rank, port, out_dir):
+    """Page-sharded save and resume: every rank saves its store, a fresh sharded
+    cache loads the files, and the next decode step gives the same selection
+    and output on both caches."""
+    import datetime
+
+    import torch.distributed as dist
+    from transformers import PretrainedConfig
+
+    from kiv_b200 import KIVConfig, ModelTopology, TieredKVCache
+    from kiv_b200.sharding import ShardComm
+    from kiv_b200.synthetic import SynthSpec, make_problem
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=WORLD, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    comm = ShardComm()
+    try:
+        spec = SynthSpec(batch=1, num_query_heads=8, num_kv_heads=1, head_dim=256, cold_tokens=20480 + 45,
+                         hot_budget=512)
+        prob = make_problem(spec, seed=23, dtype=torch.bfloat16)
+        cfg = KIVConfig(hot_budget=spec.hot_budget, page_size=128, top_pages=16, top_p=256, telemetry=False)
+        topo = ModelTopology.manual(global_layer_indices=(0,), num_query_heads=8, num_kv_heads=1, head_dim=256,
+                                    num_hidden_layers=1)
+        mk = lambda: TieredKVCache(PretrainedConfig(num_hidden_layers=1), cfg, topo, dev, shard_group=comm)
+        a = mk()
+        a.update(prob.prefill_k.to(dev), prob.prefill_v.to(dev), 0)
+        a.mark_prefill_complete()
+        a.update(prob.step_k.to(dev), prob.step_v.to(dev), 0)
+        d = os.path.join(out_dir, "ckpt")
+        if rank == 0:
+            os.makedirs(d, exist_ok=True)
+        dist.barrier()
+        a.save(d)
+        dist.barrier()
+        b = mk()
+        b.load(d)
+        g = torch.Generator().manual_seed(3)
+        q = torch.randn(1, 8, 1, 256, generator=g).to(dev, torch.bfloat16)
+        k = (0.3 * torch.randn(1, 1, 1, 256, generator=g)).to(dev, torch.bfloat16)
+        v = torch.randn(1, 1, 1, 256, generator=g).to(dev, torch.bfloat16)
+        res = []
+        for c in (a, b):
+            c.update(k, v, 0)
+            st = c.get_cold_store(0)
+            sel, P = st.retrieve_indices(q, 256 ** -0.5, cfg)
+            out = st.attend(q, 256 ** -0.5, cfg)
+            torch.cuda.synchronize(dev)
+            assert st.read_state()[7] == 0
+            res.append((sel[:, :P].cpu(), out.float().cpu(), st.page_summaries().cpu()))
+        assert torch.equal(res[0][0], res[1][0]), "selection differs after resume"
+        assert torch.equal(res[0][1], res[1][1]), "output differs after resume"
+        assert torch.equal(res[0][2], res[1][2]), "summaries differ after resume"
+        with open(os.path.join(out_dir, f"ok{rank}"), "w") as f:
+            f.write("ok")
+        dist.barrier()
+        comm.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_page_sharded_save_and_resume():
+    if torch.cuda.device_count() < WORLD:
+        pytest.skip(f"needs {WORLD} GPUs")
+    import torch.multiprocessing as mp
+
+    with tempfile.TemporaryDirectory() as d:
+        ctx = mp.start_processes(_persist_worker, args=(_free_port(), d), nprocs=WORLD, join=False,
+                                 start_method="spawn")
+        deadline = time.time() + 300
+        while not ctx.join(timeout=5):
+            if time.time() > deadline:
+                for p in ctx.processes:
+                    if p.is_alive():
+                        p.kill()
+                pytest.fail("ranks did not finish in 300 s")
         assert all(os.path.exists(os.path.join(d, f"ok{r}")) for r in range(WORLD))

@@ -36,14 +36,14 @@ def _fake_store(dev, D=64, H=2, cold=4096, hot=512, dtype=torch.bfloat16):
     hv = torch.empty_like(hk)
     st = torch.zeros(32, dtype=torch.int64, device=dev)
     e = torch.empty(0, dtype=dtype, device=dev)
-    return [ck, cv, sm, hk, hv, st, e, e], [128, 0, 1, hot, 0]
+    return [ck, cv, sm, hk, hv, st, e, e, torch.empty(0, device=dev)], [128, 0, 1, hot, 0, 0]
 
 
 def test_decode_step_traces_with_fake_tensors():
     dev = torch.device("cuda")
 
     def step(store, q, ws, sel, out, knew, vnew):
-        geom = [128, 0, 1, 512, 0]
+        geom = [128, 0, 1, 512, 0, 0]
         torch.ops.kiv.append_evict(store, geom, knew, vnew, 512, 1)
         torch.ops.kiv.coarse_select(store, geom, q, 0.125, 8, 128, 0.0, ws, None, None)
         torch.ops.kiv.fine_select(store, geom, q, 0.125, 8, 128, 0.0, ws, sel, None)
