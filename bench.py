@@ -306,8 +306,10 @@ def fine_back_to_back(cache, stores, layers, q_pool, k_pool, v_pool, i, scaling,
     back: every layer's update and coarse pass first, then the fine scorers
     (timed with CUDA events on the launching stream; each reads its own
     layer's candidate pages, so nothing is reused from L2 across launches),
-    then every layer's top-P select and attention.  Returns the average launch
-    duration and algorithmic bytes."""
+    then every layer's top-P select and attention.  On a page-sharded cache
+    every rank runs this (no exchange is involved) and its scorers read its
+    pages of the union.  Returns the average launch duration and algorithmic
+    bytes."""
     from kiv_b200 import _native as nat
     from kiv_b200 import ops
 
@@ -339,7 +341,8 @@ def fine_back_to_back(cache, stores, layers, q_pool, k_pool, v_pool, i, scaling,
     torch.cuda.synchronize()
     for st, so, qa, ws in args:
         words = st.read_state()
-        partial = st.cold_length % PAGE
+        # (page-sharded: this shard's union pages, and the partial page on its owner)
+        partial = st.cold_length % PAGE if (st.num_pages % st._shard_count) == st._shard_rank else 0
         nbytes += qa[0].shape[0] * (words[nat.ST_UNION] * PAGE + partial) * w["hkv"] * w["d"] * welem(w)
     ms = e0.elapsed_time(e1)
     n = len(args)
@@ -630,6 +633,11 @@ def main():
     layers = list(range(L))
     stores = [cache.get_cold_store(li) for li in layers]
 
+    def cand_x(st):
+        # page-sharded store whose fine pass is the candidate exchange (one call:
+        # scorer + select over every shard's candidates)
+        return world > 1 and not seq_shard and any(st._fx_ok.values())
+
     def eager_step(i):
         for li in layers:
             cache.update(k_pool[i, li], v_pool[i, li], li)
@@ -662,10 +670,16 @@ def main():
             U = words[nat.ST_UNION]
             partial = st.cold_length % PAGE
             own_partial = partial if (st.num_pages % st._shard_count) == st._shard_rank else 0
+            # the candidate exchange builds the whole union; this shard scores its pages of it
+            U_scored = U
+            if cand_x(st):
+                ws, lay = st._ws[st._cached_ws_key]
+                uni = ws[lay[2]:lay[2] + 4 * lay[8]].view(torch.int32)[:U]
+                U_scored = int((uni % world == rank).sum())
             m = dict(rec[li].marks)
             t_fine = m["fine_score_begin"].elapsed_time(m["fine_score_end"])
             fine_ms += t_fine
-            fine_bytes += w.get("batch", 1) * (U * PAGE + own_partial) * w["hkv"] * w["d"] * welem(w)
+            fine_bytes += w.get("batch", 1) * (U_scored * PAGE + own_partial) * w["hkv"] * w["d"] * welem(w)
             for a, b, name in (("update_begin", "coarse_begin", "update"),
                                ("coarse_begin", "fine_score_begin", "coarse"),
                                ("fine_score_begin", "fine_score_end", "fine_score"),
@@ -694,7 +708,8 @@ def main():
     U_mean = float(np.mean(us["U"]))
     single = {"achieved": achieved, "avg_launch_us": fine_avg_ms * 1e3, "launches_timed": n_launch}
     b2b = None
-    if world == 1 and "ring" not in w and L >= 8:
+    # (page-sharded: every rank times its own scorers on its pages; no exchange runs)
+    if (world == 1 or cand_x(stores[0])) and "ring" not in w and L >= 8:
         b2b = fine_back_to_back(cache, stores, layers, q_pool, k_pool, v_pool, (W + R) % INPUT_POOL, scaling,
                                 kcfg, w)
 
@@ -812,11 +827,16 @@ def main():
                        "parallelism": ("1 GPU" if world == 1 else
                                        f"sequences sharded over {world} GPUs ({w['batch']} per GPU), page union "
                                        "OR-reduced over the ranks" if seq_shard else
-                                       f"cold pages sharded over {world} GPU(s)"),
+                                       f"cold pages sharded over {world} GPU(s)" +
+                                       (": candidates exchanged through peer memory, every GPU selects the "
+                                        "global top-P and attends the selected rows over NVLink"
+                                        if cand_x(stores[0]) else "")),
                        "l2": f"inputs larger than L2 (each step touches {L} layers x ~{step_bytes / 1e6:.0f} MB)",
                        "timing": f"CUDA graph of one {L}-layer step replayed, CUDA events, max over ranks"},
-            # per layer-step: 7 kernels (8 on the CUDA-core fp32 path, whose union is its own kernel)
-            "gpu_launches": int(K * L * ((7 if world == 1 else 10) + (1 if f32 else 0) + (3 if "ring" in w else 0))),
+            # per layer-step: 7 kernels (8 on the CUDA-core fp32 path, whose union is its own kernel);
+            # page-sharded with list exchanges: + the partials' exchange merge
+            "gpu_launches": int(K * L * ((7 if world == 1 or seq_shard or cand_x(stores[0]) else 8) +
+                                         (1 if f32 else 0) + (3 if "ring" in w else 0))),
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "api": "kiv_b200.decode_graph.DecodeGraph.replay with pinned host inputs/outputs"},
             "roofline": ({"bound": "hbm",
@@ -828,10 +848,16 @@ def main():
                           "algorithmic_bytes_per_launch": b2b["bytes_per_launch"],
                           "avg_launch_us": b2b["avg_launch_us"], "launches_timed": b2b["launches"],
                           "timing": "the fine scorers of all layers of one decode step launched back to back "
-                                    "(each on its own layer's pages, no L2 reuse), CUDA events around them",
+                                    "(each on its own layer's pages, no L2 reuse), CUDA events around them" +
+                                    (f"; rank 0 of {world}, scoring its pages of the union (the decode step's "
+                                     "form of the kernel also stores each key into every shard's arena)"
+                                     if world > 1 else ""),
                           "single_launch": single, "mean_union_pages": U_mean} if b2b is not None else
                          {"bound": "hbm",
                           "kernel": ("fine_scores_kernel<float> (CUDA-core fine token scoring)" if f32 else
+                                     "scores_tc_kernel<bf16, fine, candidate exchange> + fine_select_kernel "
+                                     "(one call, timed together; bytes = this shard's union pages)"
+                                     if cand_x(stores[0]) else
                                      "scores_tc_kernel<bf16, fine> (tcgen05 fine token scoring)"),
                           "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                           "peak_kind": peak_kind, "traffic": committed_traffic(args.workload, fine_bytes_avg),

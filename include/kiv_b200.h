@@ -184,8 +184,8 @@ KIV_API kiv_status kiv_append_evict(const kiv_store *st, const void *k_new, cons
  * shard_count > 1: each row's local top list is written to row_scores /
  *   row_pages [R, top_pages] (R = B*Hq*Q; unused tail entries have page -1)
  *   for an all-gather, followed by kiv_coarse_merge -- or, with replicated
- *   summaries, the global union's pages of this shard are marked directly
- *   (row_scores / row_pages may be NULL; no merge follows).
+ *   summaries, the pages of the global union are marked directly (one bit per
+ *   global page; row_scores / row_pages may be NULL; no merge follows).
  * Replaces: kiv/cold_store.py:203-230 (_repeat_kv + matmul, topk, unique).
  */
 KIV_API kiv_status kiv_coarse_select(const kiv_store *st, const kiv_query *q, void *ws, size_t ws_bytes,
@@ -322,6 +322,19 @@ KIV_API kiv_status kiv_peer_alloc(size_t bytes, void **dev_ptr, void *ipc_handle
 KIV_API kiv_status kiv_peer_open(const void *ipc_handle, void **dev_ptr);
 KIV_API kiv_status kiv_peer_close(void *dev_ptr);
 KIV_API kiv_status kiv_peer_free(void *dev_ptr);
+/* IPC handle of the device allocation that contains dev_ptr (any cudaMalloc'd
+ * buffer, e.g. a store's cold_k) and dev_ptr's byte offset in it: a peer maps
+ * the handle with kiv_peer_open and adds the offset (one open per allocation
+ * and process; kiv_peer_close unmaps it). */
+KIV_API kiv_status kiv_peer_export(const void *dev_ptr, void *ipc_handle, int64_t *offset);
+
+/* Every shard's cold rows as mapped in this process (index = shard rank; the
+ * own entry is the store's cold_k / cold_v).  All shards' stores must have
+ * the same cold_capacity. */
+typedef struct kiv_peer_rows {
+  const void *cold_k[KIV_MAX_PEERS];
+  const void *cold_v[KIV_MAX_PEERS];
+} kiv_peer_rows;
 
 /* kiv_coarse_merge with the lists exchanged through the arenas: row_scores /
  * row_pages are this rank's lists from kiv_coarse_select. */
@@ -334,6 +347,45 @@ KIV_API kiv_status kiv_coarse_exchange_merge(const kiv_store *st, const kiv_quer
 KIV_API kiv_status kiv_fine_exchange_merge(const kiv_store *st, const kiv_query *q, void *ws, size_t ws_bytes,
                                            const float *scores, const int32_t *tokens, const kiv_exchange *x,
                                            int32_t *sel, int32_t *sel_local, void *stream);
+/*
+ * Candidate exchange: the fine pass of a page-sharded store with replicated
+ * summaries (KIV_STORE_REPL_SUMMARIES) in one scorer and one select, with no
+ * list merge.  After kiv_coarse_select every shard holds the whole page union;
+ * the scorer scores the union pages this shard owns and stores each key at its
+ * global candidate position into every rank's arena, and every rank's select
+ * takes the exact global top-P over all candidates (score descending, token id
+ * ascending; the same order as kiv_fine_select on one GPU).  sel [B, top_p]
+ * gets the global selection on every rank (ascending ids, tail -1).  With
+ * sel_local, this shard's rows of it go there (ascending) for kiv_attend +
+ * kiv_attend_exchange_merge; with sel_local NULL, kiv_attend_peers reads sel
+ * itself.  (The workspace's per-row selected counts follow the list the
+ * attention reads.)  A wait that runs out sets KIV_ERRBIT_WAIT_TIMEOUT and
+ * selects nothing.
+ * Every rank's store must have the same cold_capacity (the candidate
+ * positions and the arena layout follow it).
+ * kiv_fine_exchange_supported returns 1 when the store and query shapes can use
+ * it (16-bit rows, page_size 128, head_dim a multiple of 64 up to 256, at most
+ * 16 query rows per KV head, a union of at most 8192 pages, no host tier);
+ * otherwise use kiv_fine_score + kiv_fine_topk + kiv_fine_exchange_merge.
+ * Replaces, for sharded stores, the reference's fine pass
+ * (kiv/cold_store.py:283-371 retrieve_top_kv, steps 2-3).
+ */
+KIV_API int32_t kiv_fine_exchange_supported(const kiv_store *st, const kiv_query *q);
+KIV_API kiv_status kiv_fine_exchange_select(const kiv_store *st, const kiv_query *q, void *ws, size_t ws_bytes,
+                                            const kiv_exchange *x, int32_t *sel, int32_t *sel_local,
+                                            void *stream);
+/* Attention of a page-sharded store over the global selection sel [B,
+ * sel_stride] (from kiv_fine_exchange_select with sel_local NULL) and the
+ * whole (replicated) hot window: every selected row is read from the cold
+ * tier of the shard that owns its page, over NVLink for the other shards'
+ * pages, so every rank computes the full output `out` ([B, Q, Hq, D]) with no
+ * exchange of partials.  Same arithmetic as kiv_attend on one GPU.  16-bit
+ * stores with at most 16 query rows per KV head, head_dim a multiple of 64
+ * (<= 256), no host tier.  Replaces, for sharded stores: kiv/middleware.py:
+ * 330-352 and kiv/mask_utils.py:8-38. */
+KIV_API kiv_status kiv_attend_peers(const kiv_store *st, const kiv_query *q, const kiv_mask *mask, void *ws,
+                                    size_t ws_bytes, const int32_t *sel, int32_t sel_stride,
+                                    const kiv_peer_rows *peers, void *out, void *stream);
 /* kiv_attend_merge with the partials exchanged through the arenas: partial is
  * this rank's [B*Hq*Q, D + 4] from kiv_attend. */
 KIV_API kiv_status kiv_attend_exchange_merge(const kiv_store *st, const kiv_query *q, const float *partial,

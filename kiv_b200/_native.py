@@ -103,6 +103,12 @@ SIGNATURES = {
     "kiv_fine_exchange_merge": (c_i32, [P(StoreDesc), P(QueryDesc), c_vp, c_sz, c_vp, c_vp, P(ExchangeDesc),
                                         c_vp, c_vp, c_vp]),
     "kiv_attend_exchange_merge": (c_i32, [P(StoreDesc), P(QueryDesc), c_vp, P(ExchangeDesc), c_vp, c_vp]),
+    "kiv_fine_exchange_supported": (c_i32, [P(StoreDesc), P(QueryDesc)]),
+    "kiv_peer_export": (c_i32, [c_vp, c_vp, P(c_i64)]),
+    "kiv_attend_peers": (c_i32, [P(StoreDesc), P(QueryDesc), P(MaskDesc), c_vp, c_sz, c_vp, c_i32, c_vp, c_vp,
+                                 c_vp]),
+    "kiv_fine_exchange_select": (c_i32, [P(StoreDesc), P(QueryDesc), c_vp, c_sz, P(ExchangeDesc), c_vp, c_vp,
+                                         c_vp]),
 }
 
 _lib = None

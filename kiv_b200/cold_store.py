@@ -87,6 +87,8 @@ class ColdKVStore:
         self._op_tensors: list | None = None
         self._ws: dict[tuple, tuple] = {}
         self._bufs: dict[tuple, torch.Tensor] = {}
+        self._fx_ok: dict[tuple, bool] = {}
+        self._fine_x = False      # the last sharded fine pass was the candidate exchange
         # shared-layer candidate reuse (attribute names of the reference)
         self._cached_candidate_k: torch.Tensor | None = None
         self._cached_candidate_v: torch.Tensor | None = None
@@ -148,9 +150,11 @@ class ColdKVStore:
             self._alloc_cold(self._round_local(cap))
 
     def _round_local(self, global_tokens: int) -> int:
-        """Local token slots that hold the pages of ``global_tokens`` cold tokens."""
+        """Local token slots that hold the pages of ``global_tokens`` cold tokens
+        -- the same on every shard (the largest shard's page count), so the
+        shards' stores, workspaces and exchange arenas have one layout."""
         pages = math.ceil(global_tokens / self._page_size)
-        return max(1, self._local_pages(pages)) * self._page_size
+        return max(1, -(-pages // self._shard_count)) * self._page_size
 
     @property
     def replicated_summaries(self) -> bool:
@@ -604,6 +608,12 @@ class ColdKVStore:
                 ops.call(K.attend, *so, *qa, ws, sel_local, mask_add, bool(causal), 0, 1, out, None)
                 if self._profile is not None:
                     self._profile.record("attend_end")
+            elif self._cold_len > 0 and self._fine_x:
+                # every shard reads the selected rows from their owners' cold tiers
+                pk, pv = self._comm.map_peers([self._k.data_ptr(), self._v.data_ptr()], self.device)
+                ops.call(K.attend_peers, *so, *qa, ws, sel_local, mask_add, bool(causal), pk, pv, out)
+                if self._profile is not None:
+                    self._profile.record("attend_end")
             else:
                 R = B * Hq * Q
                 part = self._buffer("apart", (R, D + 4), torch.float32)
@@ -657,13 +667,43 @@ class ColdKVStore:
         self._comm.all_gather(all_p, pg)
         ops.call(kv.coarse_merge, *so, *qa, ws, all_s, all_p)
 
+    def _fine_exchange_supported(self, qa: tuple) -> bool:
+        """Whether this store/query shape takes the candidate exchange (cached per shape)."""
+        key = (tuple(qa[0].shape), qa[2], qa[3], int(self._k.shape[2]))
+        hit = self._fx_ok.get(key)
+        if hit is None:
+            qd = nat.query_desc(qa[0], qa[1], qa[2], qa[3], qa[4])
+            hit = bool(nat.lib().kiv_fine_exchange_supported(ctypes.byref(self.descriptor()), ctypes.byref(qd)))
+            self._fx_ok[key] = hit
+        return hit
+
     def _sharded_fine(self, qa: tuple, ws, B: int, top_p: int, sel: torch.Tensor | None) -> torch.Tensor:
-        """Local fine pass + exchange + merge; fills ``sel`` (the global list) when given."""
+        """Fine pass of a page-sharded store; fills ``sel`` (the global list) when
+        given and returns the list the attention reads.  With replicated summaries
+        and peer exchange: one scorer + select over every shard's candidates (the
+        keys travel through the arenas), returning the global list (the attention
+        then reads every shard's rows); otherwise a local pass, then the lists'
+        exchange and merge, returning this shard's part of the selection."""
         kv = ops.kiv()
         so = self._op_store()
+        prof = self._profile
+        sel_local = self._buffer("sel_local", (B, top_p), torch.int32)
+        x = self._exchange(qa)
+        self._fine_x = x is not None and self.replicated_summaries and self._fine_exchange_supported(qa)
+        if self._fine_x:
+            # every shard ends with the global selection; the attention reads each
+            # row from its owner (attend_peers), so no local list is needed
+            if sel is None:
+                sel = self._buffer("sel_global_scratch", (B, top_p), torch.int32)
+            if prof is not None:
+                prof.record("fine_score_begin")
+            ops.call(kv.fine_exchange_select, *so, *qa, ws, *x, sel, None)
+            if prof is not None:
+                prof.record("fine_score_end")
+                prof.record("fine_topk_end")
+            return sel
         lt = self._buffer("fl_t", (B, top_p), torch.int32)
         ls = self._buffer("fl_s", (B, top_p), torch.float32)
-        prof = self._profile
         if prof is not None:
             prof.record("fine_score_begin")
         ops.call(kv.fine_score, *so, *qa, ws)
@@ -672,8 +712,6 @@ class ColdKVStore:
         ops.call(kv.fine_topk, *so, *qa, ws, lt, ls)
         if prof is not None:
             prof.record("fine_topk_end")
-        sel_local = self._buffer("sel_local", (B, top_p), torch.int32)
-        x = self._exchange(qa)
         if x is not None:
             ops.call(kv.fine_exchange_merge, *so, *qa, ws, ls, lt, *x, sel, sel_local)
             return sel_local

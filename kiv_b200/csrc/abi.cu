@@ -5,6 +5,8 @@
 
 #include <algorithm>
 
+#include <cuda.h>
+
 #include "exchange.cuh"
 #include "internal.h"
 
@@ -346,9 +348,9 @@ kiv_status kiv_retrieve_attend(const kiv_store *st, const kiv_query *q, const ki
 // ---------------------------------------------------------------- exchange
 size_t kiv_exchange_bytes(const kiv_store *st, const kiv_query *q, int32_t world) {
   if (check_store(st) != KIV_OK || check_query(st, q) != KIV_OK || world < 1 || world > KIV_MAX_PEERS) return 0;
-  int64_t cb, fb, ab;
-  exchange_payloads(st, q, &cb, &fb, &ab);
-  return (size_t)x_layout(cb, fb, ab, world).total;
+  int64_t cb, fb, ab, xb;
+  exchange_payloads(st, q, &cb, &fb, &ab, &xb);
+  return (size_t)x_layout(cb, fb, ab, xb, world).total;
 }
 
 kiv_status kiv_peer_alloc(size_t bytes, void **dev_ptr, void *ipc_handle) {
@@ -378,6 +380,35 @@ kiv_status kiv_peer_open(const void *ipc_handle, void **dev_ptr) {
 
 kiv_status kiv_peer_close(void *dev_ptr) { return cuda_status(cudaIpcCloseMemHandle(dev_ptr), "peer_close"); }
 
+kiv_status kiv_peer_export(const void *dev_ptr, void *ipc_handle, int64_t *offset) {
+  if (!dev_ptr || !ipc_handle || !offset) { set_error("bad peer_export arguments"); return KIV_ERR_ARG; }
+  // the allocation's base (driver entry point: the runtime has no range query)
+  using RangeFn = CUresult (*)(CUdeviceptr *, size_t *, CUdeviceptr);
+  static RangeFn range = nullptr;
+  if (!range) {
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult qr;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &qr) != cudaSuccess ||
+        qr != cudaDriverEntryPointSuccess || !fn) {
+      set_error("cuMemGetAddressRange unavailable");
+      return KIV_ERR_CUDA;
+    }
+    range = reinterpret_cast<RangeFn>(fn);
+  }
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(dev_ptr)) != CUDA_SUCCESS) {
+    set_error("peer_export: %p is not device memory", dev_ptr);
+    return KIV_ERR_ARG;
+  }
+  cudaIpcMemHandle_t h;
+  KIV_TRY(cuda_status(cudaIpcGetMemHandle(&h, reinterpret_cast<void *>(base)), "peer_export: cudaIpcGetMemHandle"));
+  memset(ipc_handle, 0, KIV_IPC_HANDLE_BYTES);
+  memcpy(ipc_handle, &h, sizeof(h));
+  *offset = (int64_t)(reinterpret_cast<CUdeviceptr>(dev_ptr) - base);
+  return KIV_OK;
+}
+
 kiv_status kiv_peer_free(void *dev_ptr) { return cuda_status(cudaFree(dev_ptr), "peer_free"); }
 
 kiv_status kiv_host_alloc(size_t bytes, void **ptr) {
@@ -396,9 +427,9 @@ static kiv_status check_exchange(const kiv_store *st, const kiv_query *q, const 
     set_error("exchange descriptor does not match the store's shard (rank/world)");
     return KIV_ERR_ARG;
   }
-  int64_t cb, fb, ab;
-  exchange_payloads(st, q, &cb, &fb, &ab);
-  const kiv::XLayout L = x_layout(cb, fb, ab, x->world);
+  int64_t cb, fb, ab, xb;
+  exchange_payloads(st, q, &cb, &fb, &ab, &xb);
+  const kiv::XLayout L = x_layout(cb, fb, ab, xb, x->world);
   if (x->arena_bytes < L.total) {
     set_error("exchange arena of %lld bytes, this shape needs %lld", (long long)x->arena_bytes,
               (long long)L.total);
@@ -453,6 +484,55 @@ kiv_status kiv_fine_exchange_merge(const kiv_store *st, const kiv_query *q, void
   kiv::XArgs a;
   KIV_TRY(check_exchange(st, q, x, kiv::X_FINE, st->batch, a));
   return launch_fine_merge(st, q, w, scores, tokens, x->world, sel, sel_local, (cudaStream_t)stream, &a);
+}
+
+int32_t kiv_fine_exchange_supported(const kiv_store *st, const kiv_query *q) {
+  if (check_store(st) != KIV_OK || check_query(st, q) != KIV_OK) return 0;
+  return fine_exchange_eligible(st, q) ? 1 : 0;
+}
+
+kiv_status kiv_fine_exchange_select(const kiv_store *st, const kiv_query *q, void *ws, size_t ws_bytes,
+                                    const kiv_exchange *x, int32_t *sel, int32_t *sel_local, void *stream) {
+  KIV_TRY(check_store(st));
+  KIV_TRY(check_query(st, q));
+  Workspace w;
+  KIV_TRY(check_ws(st, q, ws, ws_bytes, w));
+  if (!sel) { set_error("sel is NULL"); return KIV_ERR_ARG; }
+  if (!fine_exchange_eligible(st, q)) {
+    set_error("candidate exchange needs a page-sharded store with replicated summaries, 16-bit rows, "
+              "page_size 128 and a union of at most %d pages", 8192);
+    return KIV_ERR_UNSUPPORTED;
+  }
+  kiv::XArgs a;
+  KIV_TRY(check_exchange(st, q, x, kiv::X_CAND, (int64_t)st->batch * SEL_CLUSTER, a));
+  cudaStream_t s = (cudaStream_t)stream;
+  KIV_TRY(launch_fine_score_tc_exchange(st, q, w, s, a));
+  return launch_fine_exchange_select(st, q, w, sel, sel_local, s, a);
+}
+
+kiv_status kiv_attend_peers(const kiv_store *st, const kiv_query *q, const kiv_mask *mask, void *ws,
+                            size_t ws_bytes, const int32_t *sel, int32_t sel_stride, const kiv_peer_rows *peers,
+                            void *out, void *stream) {
+  KIV_TRY(check_store(st));
+  KIV_TRY(check_query(st, q));
+  Workspace w;
+  KIV_TRY(check_ws(st, q, ws, ws_bytes, w));
+  if (!sel || sel_stride < 0 || !out || !peers) { set_error("bad attend_peers arguments"); return KIV_ERR_ARG; }
+  if (st->shard_count < 2 || st->host_capacity > 0) {
+    set_error("attend_peers is the page-sharded path without a host tier");
+    return KIV_ERR_ARG;
+  }
+  for (int r = 0; r < st->shard_count; ++r) {
+    if (!peers->cold_k[r] || !peers->cold_v[r] || !aligned16(peers->cold_k[r]) || !aligned16(peers->cold_v[r])) {
+      set_error("peer rows of shard %d missing or not 16-byte aligned", r);
+      return KIV_ERR_ARG;
+    }
+  }
+  if (peers->cold_k[st->shard_rank] != st->cold_k || peers->cold_v[st->shard_rank] != st->cold_v) {
+    set_error("peer rows: this shard's entry must be the store's own cold rows");
+    return KIV_ERR_ARG;
+  }
+  return launch_attend_peers(st, q, mask, w, sel, sel_stride, peers, out, (cudaStream_t)stream);
 }
 
 kiv_status kiv_attend_exchange_merge(const kiv_store *st, const kiv_query *q, const float *partial,

@@ -36,6 +36,11 @@ struct AttnArgs {
   int32_t sel_stride;
   int32_t hot_slice, hot_slices;
   int32_t n_split;
+  // page-sharded store, global selection: every shard's cold rows (the owner
+  // of page p is shard p % shard_count), or null pointers for own rows only
+  const void *peer_k[KIV_MAX_PEERS];
+  const void *peer_v[KIV_MAX_PEERS];
+  int32_t peers;
 };
 
 // reduced [RCH][D] outputs live after the key-subset partials
@@ -140,8 +145,15 @@ attend_split_kernel(AttnArgs<T> a) {
       const int64_t tok = tok_hint >= 0 ? tok_hint : selb[k - hot_count];
       const int64_t p = tok / S;
       const int64_t slot = page_slot(st, a.w, p / st.shard_count) * S + tok % S;
-      pk = cold_k + (bhk * st.cold_capacity + slot) * D;
-      pv = cold_v + (bhk * st.cold_capacity + slot) * D;
+      const T *bk = cold_k, *bv = cold_v;
+      if (a.peers) {
+        // the owner's cold tier (same layout on every shard; NVLink for another shard's)
+        const int own = (int)(p % st.shard_count);
+        bk = reinterpret_cast<const T *>(a.peer_k[own]);
+        bv = reinterpret_cast<const T *>(a.peer_v[own]);
+      }
+      pk = bk + (bhk * st.cold_capacity + slot) * D;
+      pv = bv + (bhk * st.cold_capacity + slot) * D;
     }
   };
   // warp 0 copies the rows of tile t with key index in [lo, hi): lane i takes
@@ -483,8 +495,15 @@ attend_mma_kernel(AttnArgs<T> a) {
       const int64_t tok = tok_hint >= 0 ? tok_hint : selb[k - hot_count];
       const int64_t p = tok / S;
       const int64_t slot = page_slot(st, a.w, p / st.shard_count) * S + tok % S;
-      pk = cold_k + (bhk * st.cold_capacity + slot) * D;
-      pv = cold_v + (bhk * st.cold_capacity + slot) * D;
+      const T *bk = cold_k, *bv = cold_v;
+      if (a.peers) {
+        // the owner's cold tier (same layout on every shard; NVLink for another shard's)
+        const int own = (int)(p % st.shard_count);
+        bk = reinterpret_cast<const T *>(a.peer_k[own]);
+        bv = reinterpret_cast<const T *>(a.peer_v[own]);
+      }
+      pk = bk + (bhk * st.cold_capacity + slot) * D;
+      pv = bv + (bhk * st.cold_capacity + slot) * D;
     }
   };
   auto issue_part = [&](int t, int64_t lo, int64_t hi, bool arrive, int32_t tok_hint) {
@@ -1250,11 +1269,23 @@ template <typename T>
 static kiv_status attend_t(const kiv_store *st, const kiv_query *q, const kiv_mask *m,
                            const Workspace &w, const int32_t *sel, int32_t sel_stride,
                            int32_t hot_slice, int32_t hot_slices, void *out, float *partial_out,
-                           cudaStream_t s) {
+                           cudaStream_t s, const kiv_peer_rows *peers = nullptr) {
   // host tier: the selected rows of host pages reach their staging pages first
   KIV_CHECK(launch_stage_selected(st, w, sel, sel_stride, s));
   const int64_t expected_hot = st->hot_hint > 0 ? st->hot_hint : st->hot_capacity;
-  AttnArgs<T> a;
+  AttnArgs<T> a = {};
+  if (peers) {
+    if (!attend_mma_eligible<T>(st, q)) {
+      set_error("peer-row attention needs 16-bit rows, <= %d query rows per KV head, head_dim % 64 == 0",
+                AM_ROWS);
+      return KIV_ERR_UNSUPPORTED;
+    }
+    a.peers = 1;
+    for (int r = 0; r < st->shard_count; ++r) {
+      a.peer_k[r] = peers->cold_k[r];
+      a.peer_v[r] = peers->cold_v[r];
+    }
+  }
   a.st = *st;
   a.q = *q;
   if (m) a.mask = *m;
@@ -1287,6 +1318,19 @@ static kiv_status attend_t(const kiv_store *st, const kiv_query *q, const kiv_ma
   launch_combine<T>(w.part, rs, 1, a.n_split, st->head_dim, q->num_query_heads, q->query_len, rows,
                     partial_out ? nullptr : reinterpret_cast<T *>(out), partial_out, s);
   return cuda_status(cudaGetLastError(), "attend_combine");
+}
+
+kiv_status launch_attend_peers(const kiv_store *st, const kiv_query *q, const kiv_mask *m, const Workspace &w,
+                               const int32_t *sel, int32_t sel_stride, const kiv_peer_rows *peers, void *out,
+                               cudaStream_t s) {
+  switch (st->dtype) {
+    case KIV_DTYPE_BF16:
+      return attend_t<__nv_bfloat16>(st, q, m, w, sel, sel_stride, 0, 1, out, nullptr, s, peers);
+    case KIV_DTYPE_F16:
+      return attend_t<__half>(st, q, m, w, sel, sel_stride, 0, 1, out, nullptr, s, peers);
+  }
+  set_error("peer-row attention needs a 16-bit store");
+  return KIV_ERR_UNSUPPORTED;
 }
 
 kiv_status launch_attend(const kiv_store *st, const kiv_query *q, const kiv_mask *m,
@@ -1347,12 +1391,15 @@ kiv_status launch_attend_merge(const kiv_store *st, const kiv_query *q, const fl
 }
 
 // per-rank payload bytes of the three exchanges
-void exchange_payloads(const kiv_store *st, const kiv_query *q, int64_t *cb, int64_t *fb, int64_t *ab) {
+void exchange_payloads(const kiv_store *st, const kiv_query *q, int64_t *cb, int64_t *fb, int64_t *ab,
+                       int64_t *xb) {
   const int64_t R = (int64_t)st->batch * q->num_query_heads * q->query_len;
   // one flagged 64-bit word per 32-bit value
   *cb = R * q->top_pages * 16;
   *fb = (int64_t)st->batch * q->top_p * 16;
   *ab = R * partial_stride(st->head_dim) * 8;
+  // candidate exchange: one word per candidate position of every batch row
+  *xb = (int64_t)st->batch * workspace_layout(st, q, nullptr).c_cap * 8;
 }
 
 kiv_status launch_gather(const kiv_store *st, const int32_t *sel, int32_t sel_stride, int32_t P,

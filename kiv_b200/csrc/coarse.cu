@@ -185,11 +185,8 @@ coarse_topk_kernel(kiv_store st, kiv_query q, Workspace w, float *row_scores, in
     if (nsh == 1) {
       atomicOr(&w.pbits[lp >> 5], 1u << (lp & 31));
     } else if (repl) {
-      // lp is a global page: mark it (by its local index) when this shard owns it
-      if (lp % nsh == rank) {
-        const int64_t l = lp / nsh;
-        atomicOr(&w.pbits[l >> 5], 1u << (l & 31));
-      }
+      // lp is a global page; the marks index global pages (every shard holds the whole union)
+      atomicOr(&w.pbits[lp >> 5], 1u << (lp & 31));
     } else if (pos < (uint32_t)K) {
       ls[pos] = key2f(key);
       lpg[pos] = (int32_t)(lp * nsh + rank);
@@ -316,12 +313,8 @@ coarse_rows_topk_kernel(kiv_store st, kiv_query q, Workspace w, float *row_score
   const uint32_t k = (uint32_t)(K < np ? (int64_t)K : np);
   const unsigned lt = (1u << lane) - 1u;
   __syncthreads();
+  // i: a local page, or a global one with replicated summaries (marks index global pages)
   auto mark = [&](int64_t i) {
-    if (repl) {
-      // i is a global page: marked by its local index when this shard owns it
-      if (i % nsh != rank) return;
-      i /= nsh;
-    }
     if (nwords > 0) atomicOr(&bits[i >> 5], 1u << (i & 31));
     else atomicOr(&w.pbits[i >> 5], 1u << (i & 31));
   };
@@ -493,9 +486,13 @@ __global__ void __launch_bounds__(UN_THREADS) union_kernel(kiv_store st, Workspa
   __shared__ int wsum[UN_THREADS / 32];
   if (st_ld(st.state, KIV_ST_UNION_PENDING) == 0) return;
   const int64_t np_global = st_ld(st.state, KIV_ST_COLD_LEN) / st.page_size;
-  const int64_t np = local_pages(np_global, st.shard_rank, st.shard_count);
-  const int u = union_from_bits<UN_THREADS, false>(w.pbits, np, w.uni, (int)w.u_cap, st.shard_rank,
-                                                   st.shard_count, wsum);
+  // marks: one per local page, or per global page with replicated summaries
+  // (this shard's pages of the union kept)
+  const int64_t np = coarse_pages(st, np_global);
+  const bool repl = repl_summaries(st);
+  const int u = union_from_bits<UN_THREADS, false>(w.pbits, np, w.uni, (int)w.u_cap, repl ? 0 : st.shard_rank,
+                                                   repl ? 1 : st.shard_count, wsum, st.shard_rank,
+                                                   repl ? st.shard_count : 1);
   for (int64_t i = threadIdx.x; i < (np + 31) / 32; i += UN_THREADS) w.pbits[i] = 0;
   if (threadIdx.x == 0) {
     st.state[KIV_ST_UNION] = u;

@@ -2,10 +2,12 @@
 //
 // Every rank owns an arena that all ranks map (CUDA IPC over NVLink).  Arena
 // layout (identical on every rank):
-//   header  [3 types][16] u64: word 0 the type's epoch (exchanges done),
+//   header  [4 types][16] u64: word 0 the type's epoch (exchanges done),
 //           word 1 a CTA counter (last CTA of a launch);
 //   regions one per type, two parities each (epoch & 1), holding the lists
-//           of every rank at slot [src], as 64-bit words (flag << 32 | data).
+//           of every rank at slot [src], as 64-bit words (flag << 32 | data);
+//           the candidate region (X_CAND) instead holds one word per
+//           candidate position, written by the rank that owns its page.
 // A merge launch of epoch e: each CTA stores its part of this rank's lists
 // into slot [rank] of parity e & 1 of every arena, each 32-bit value in one
 // 64-bit store together with the flag e + 1 (a single-copy atomic access, so
@@ -22,7 +24,8 @@
 
 namespace kiv {
 
-enum XType { X_COARSE = 0, X_FINE = 1, X_ATTN = 2 };
+enum XType { X_COARSE = 0, X_FINE = 1, X_ATTN = 2, X_CAND = 3 };
+constexpr int X_TYPES = 4;
 constexpr int64_t X_HDR_BYTES = 1024;
 
 struct XArgs {
@@ -36,17 +39,18 @@ struct XArgs {
 // default bound of every wait: 2^31 cycles, about 1.1 s at 1965 MHz
 constexpr int64_t X_DEFAULT_WAIT_CYCLES = 1ll << 31;
 
-// byte offsets of the three regions and the arena size for per-rank payloads
-// (bytes of one rank's lists) cb, fb, ab
+// byte offsets of the regions and the arena size for per-rank payloads
+// (bytes of one rank's lists) cb, fb, ab and the candidate payload xb (bytes
+// of all ranks' candidates together)
 struct XLayout {
-  int64_t off[3], par[3], total;
+  int64_t off[X_TYPES], par[X_TYPES], total;
 };
-__host__ __device__ inline XLayout x_layout(int64_t cb, int64_t fb, int64_t ab, int world) {
+__host__ __device__ inline XLayout x_layout(int64_t cb, int64_t fb, int64_t ab, int64_t xb, int world) {
   XLayout L;
-  const int64_t pay[3] = {cb, fb, ab};
+  const int64_t pay[X_TYPES] = {cb * world, fb * world, ab * world, xb};
   int64_t o = X_HDR_BYTES;
-  for (int t = 0; t < 3; ++t) {
-    L.par[t] = (pay[t] * world + 255) / 256 * 256;
+  for (int t = 0; t < X_TYPES; ++t) {
+    L.par[t] = (pay[t] + 255) / 256 * 256;
     L.off[t] = o;
     o += 2 * L.par[t];
   }

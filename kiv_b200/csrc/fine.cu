@@ -263,15 +263,23 @@ fine_scores_kernel(kiv_store st, kiv_query q, Workspace w, int tr, int stage_q) 
 // full radix select over the keys instead.
 // shard_count == 1: sel[b, :P] = selected token ids (ascending).
 // shard_count > 1: sel / scores hold this shard's local list (tail -1).
-template <int CL>
+// XC (candidate exchange): the keys of every shard's candidates arrive in this
+// shard's arena as flagged words (each read waits, bounded, for its flag);
+// every CTA counts its keys into a histogram and the cluster sums them, then
+// the select runs as above over all candidates.  sel gets the global top-P
+// (ascending, tail -1) on every shard and sel_local this shard's part of it;
+// a wait that gave up selects nothing.
+template <int CL, bool XC>
 __global__ void __launch_bounds__(SL_THREADS)
 fine_select_kernel(kiv_store st, kiv_query q, Workspace w, int32_t *sel, float *scores, int cap, int ucap,
-                   int kcap) {
+                   int kcap, int32_t *sel_local, const __grid_constant__ XArgs x) {
   extern __shared__ uint4 sl_dyn[];
   __shared__ __align__(16) CandSmem<SL_THREADS> cs;
   __shared__ SelectSmem<SL_THREADS> sm;
   __shared__ int s_cnt;
   __shared__ int s_fail;
+  __shared__ int s_xfail;
+  __shared__ int s_wsum[SL_THREADS / 32];
   __shared__ uint64_t bar;
   uint32_t *ckey = reinterpret_cast<uint32_t *>(sl_dyn);
   int32_t *cidx = reinterpret_cast<int32_t *>(ckey + cap);
@@ -285,7 +293,10 @@ fine_select_kernel(kiv_store st, kiv_query q, Workspace w, int32_t *sel, float *
     mbar_init(&bar, 1);
     mbar_fence_init();
     s_fail = 0;
+    s_xfail = 0;
   }
+  if (XC)
+    for (int i = threadIdx.x; i < SEL_BINS; i += SL_THREADS) sm.hist[0][i] = 0;
   __syncthreads();
   // the cold length was published by the eviction, kernels back
   const int64_t cold = st_ld(st.state, KIV_ST_COLD_LEN);
@@ -302,11 +313,13 @@ fine_select_kernel(kiv_store st, kiv_query q, Workspace w, int32_t *sel, float *
   const uint32_t *src = w.agg + (int64_t)b * w.c_cap + lo;
   uint32_t *hb = w.fhist + (int64_t)b * SEL_BINS;
   const bool kstaged = n_cap > 0 && n_cap <= kcap && (reinterpret_cast<uintptr_t>(src) & 15) == 0;
-  if (threadIdx.x == 0) {
-    const uint32_t kb = kstaged ? (uint32_t)((n_cap * 4 + 15) & ~15ll) : 0u;
-    const uint32_t ub = r == 0 && ucap > 0 ? (uint32_t)((ucap * 4 + 15) & ~15) : 0u;
-    mbar_arrive_tx(&bar, SEL_BINS * 4 + kb + ub);
-    bulk_g2s(cs.hist, hb, SEL_BINS * 4, &bar);
+  // XC: the keys come from the arena (below), the histogram is built here
+  const uint32_t hbytes = XC ? 0u : SEL_BINS * 4;
+  const uint32_t kb = kstaged && !XC ? (uint32_t)((n_cap * 4 + 15) & ~15ll) : 0u;
+  const uint32_t ub = r == 0 && ucap > 0 ? (uint32_t)((ucap * 4 + 15) & ~15) : 0u;
+  if (threadIdx.x == 0 && hbytes + kb + ub > 0) {
+    mbar_arrive_tx(&bar, hbytes + kb + ub);
+    if (hbytes) bulk_g2s(cs.hist, hb, hbytes, &bar);
     if (kb) bulk_g2s(skey, src, kb, &bar);
     if (ub) bulk_g2s(suni, w.uni, ub, &bar);
   }
@@ -314,7 +327,8 @@ fine_select_kernel(kiv_store st, kiv_query q, Workspace w, int32_t *sel, float *
   f.U = st_ld(st.state, KIV_ST_UNION);
   f.np_global = cold / S;
   f.partial = cold % S;
-  f.part_owned = f.partial > 0 && (f.np_global % st.shard_count) == st.shard_rank;
+  // XC: the partial page's candidates are in every shard's arena
+  f.part_owned = f.partial > 0 && (XC || (f.np_global % st.shard_count) == st.shard_rank);
   f.per_b = f.U + (f.part_owned ? 1 : 0);
   f.items = (int64_t)st.batch * f.per_b;
   const int64_t C = f.U * S + (f.part_owned ? f.partial : 0);
@@ -332,7 +346,73 @@ fine_select_kernel(kiv_store st, kiv_query q, Workspace w, int32_t *sel, float *
     st_sb = w.fstat[2 * b + 1];
     pending = st_ld(st.state, KIV_ST_UNION_PENDING);
   }
-  if (!mbar_wait_bounded(&bar, 0)) s_fail = 1;
+  if (hbytes + kb + ub > 0 && !mbar_wait_bounded(&bar, 0)) s_fail = 1;
+  const unsigned long long xe = XC ? x_epoch(x, X_CAND) : 0ull;
+  if (XC) {
+    // this CTA's candidates from the arena: independent loads first (one
+    // round trip), then each word's flag checked (reloaded until it arrives)
+    const unsigned long long *words = x_region(x, x.rank, xe) + (int64_t)b * w.c_cap + lo;
+    uint32_t *kdst = kstaged ? skey : const_cast<uint32_t *>(src);
+    const uint32_t flag = x_flag(xe);
+    bool ok = true;
+    constexpr int XB = 16;
+#pragma unroll 1
+    for (int i0 = 0; i0 < n_local; i0 += SL_THREADS * XB) {
+      unsigned long long v[XB];
+#pragma unroll
+      for (int k = 0; k < XB; ++k) {
+        const int i = i0 + k * SL_THREADS + threadIdx.x;
+        v[k] = i < n_local ? ld_relaxed_sys(words + i) : 0ull;
+      }
+#pragma unroll
+      for (int k = 0; k < XB; ++k) {
+        const int i = i0 + k * SL_THREADS + threadIdx.x;
+        if (i < n_local) {
+          const uint32_t key = ll_check(words + i, v[k], flag, ok, x.budget);
+          kdst[i] = key;
+          atomicAdd(&sm.hist[0][key >> 21], 1u);
+        }
+      }
+    }
+    const int anyfail = __syncthreads_or(!ok);
+    if (threadIdx.x == 0) s_xfail = anyfail;
+    cl_sync<CL>();
+    // one failed wait fails the whole cluster
+    bool fail = false;
+#pragma unroll 1
+    for (int o = 0; o < CL; ++o) fail |= *cl_map<CL>(&s_xfail, o) != 0;
+    if (!fail) {
+      // the row's histogram = the sum of the cluster's: CTA r sums its share of
+      // the bins over the cluster and writes the sums into every CTA's copy
+      constexpr int BS = SEL_BINS / CL;
+      for (int i = threadIdx.x; i < BS; i += SL_THREADS) {
+        const int bin = r * BS + i;
+        uint32_t t = 0;
+#pragma unroll
+        for (int o = 0; o < CL; ++o) t += cl_map<CL>(sm.hist[0], o)[bin];
+#pragma unroll
+        for (int o = 0; o < CL; ++o) cl_map<CL>(cs.hist, o)[bin] = t;
+      }
+      cl_sync<CL>();
+    }
+    if (fail) {
+      // keep every CTA's shared memory alive until the cluster has read it
+      cl_sync<CL>();
+      if (threadIdx.x == 0) {
+        if (r == 0) {
+          w.selcnt[b] = 0;
+          atomicOr(reinterpret_cast<unsigned long long *>(st.state + KIV_ST_ERROR),
+                   (unsigned long long)KIV_ERRBIT_WAIT_TIMEOUT);
+          if (b == 0) {
+            st.state[KIV_ST_SEL] = 0;
+            st.state[KIV_ST_SEL_LOCAL] = 0;
+          }
+        }
+      }
+      x_advance(x, X_CAND, xe);
+      return;
+    }
+  }
   const uint32_t *keys = kstaged ? skey : src;
   auto key_at = [&](int i) { return kstaged ? skey[i] : __ldcg(src + i); };
   auto emit_global = [&](int i, uint32_t pos) {   // i: index within this CTA's range
@@ -389,16 +469,37 @@ fine_select_kernel(kiv_store st, kiv_query q, Workspace w, int32_t *sel, float *
       }
     } else {
       uint32_t T = 0, need = 0;
-      radix_threshold<SL_THREADS, CL>(keys, n_local, (uint32_t)P, sm, T, need, hb);
+      radix_threshold<SL_THREADS, CL>(keys, n_local, (uint32_t)P, sm, T, need, XC ? nullptr : hb);
       ordered_emit<SL_THREADS, CL>(keys, n_local, T, need, false, sm, emit_global);
     }
   } else if (P > 0) {
     ordered_emit<SL_THREADS, CL>(keys, n_local, 0u, 0u, true, sm, emit_global);
   }
+  int n_mine = (int)P;
+  if (XC && sel_local) {
+    // this shard's rows of the global list, ascending (the list was written by
+    // the whole cluster)
+    cl_sync<CL>();
+    if (r == 0) {
+      int base = 0;
+#pragma unroll 1
+      for (int p0 = 0; p0 < (int)P; p0 += SL_THREADS) {
+        const int p = p0 + threadIdx.x;
+        const int32_t tok = p < (int)P ? __ldcg(out + p) : -1;
+        const bool mine = tok >= 0 && (tok / S) % st.shard_count == st.shard_rank;
+        int total;
+        const int pos = base + block_excl_sum<SL_THREADS>(mine ? 1 : 0, &total, s_wsum);
+        if (mine) sel_local[(int64_t)b * q.top_p + pos] = tok;
+        base += total;
+      }
+      n_mine = base;
+    }
+  }
   // every CTA has read the histogram (first cluster barrier, or P == 0)
   if (r == 0) {
     __syncthreads();
-    for (int i = threadIdx.x; i < SEL_BINS; i += SL_THREADS) hb[i] = 0;
+    if (!XC)
+      for (int i = threadIdx.x; i < SEL_BINS; i += SL_THREADS) hb[i] = 0;
     if (threadIdx.x == 0) {
       if (st_mk) atomicMax(reinterpret_cast<unsigned long long *>(st.state + KIV_ST_FINE_MAX), st_mk);
       atomicAdd(reinterpret_cast<double *>(st.state + KIV_ST_FINE_SUM), __longlong_as_double((long long)st_sb));
@@ -419,21 +520,22 @@ fine_select_kernel(kiv_store st, kiv_query q, Workspace w, int32_t *sel, float *
       if (threadIdx.x == 0) s_cnt = (int)pending;
       __syncthreads();
       if (s_cnt) {
-        const int64_t np = f.np_global > st.shard_rank
-                               ? (f.np_global - st.shard_rank + st.shard_count - 1) / st.shard_count : 0;
+        const int64_t np = coarse_pages(st, f.np_global);   // bits of the marks
         for (int64_t i = threadIdx.x; i < (np + 31) / 32; i += SL_THREADS) w.pbits[i] = 0;
         if (threadIdx.x == 0) st.state[KIV_ST_UNION_PENDING] = 0;
       }
     }
     if (threadIdx.x == 0) {
-      w.selcnt[b] = (int32_t)P;
+      w.selcnt[b] = (int32_t)n_mine;
       if (b == 0) {
         st.state[KIV_ST_CAND] = C;
         st.state[KIV_ST_SEL] = P;
-        st.state[KIV_ST_SEL_LOCAL] = P;
+        st.state[KIV_ST_SEL_LOCAL] = n_mine;
       }
     }
   }
+  // the arena's candidates of this epoch are read: the launch's last CTA moves the epoch on
+  if (XC) x_advance(x, X_CAND, xe);
 }
 
 // lower_bound over the first n entries of an ascending id list
@@ -688,18 +790,44 @@ kiv_status launch_fine(const kiv_store *st, const kiv_query *q, const Workspace 
   return launch_fine_topk(st, q, w, sel, sel_scores, s);
 }
 
-kiv_status launch_fine_topk(const kiv_store *st, const kiv_query *q, const Workspace &w, int32_t *sel,
-                            float *sel_scores, cudaStream_t s) {
-  // select: one cluster of SEL_CLUSTER CTAs per batch row
+// select: one cluster of SEL_CLUSTER CTAs per batch row (x: candidate exchange)
+static kiv_status launch_select(const kiv_store *st, const kiv_query *q, const Workspace &w, int32_t *sel,
+                                float *sel_scores, int32_t *sel_local, cudaStream_t s, const XArgs *x) {
   const int cap = (int)std::max<int64_t>(16, std::min<int64_t>(SL_CAP, align_up(w.c_cap, 16)));
   const int ucap = (int)std::min<int64_t>(SL_UCAP, align_up(w.u_cap, 4));
   const int kcap = (int)std::min<int64_t>(SL_KCAP, align_up(ceil_div(w.c_cap, SEL_CLUSTER), 16) + 16);
   const size_t smem = (size_t)cap * 13 + (size_t)SL_BND * 8 + (size_t)ucap * 4 + (size_t)kcap * 4;
-  auto kern = fine_select_kernel<SEL_CLUSTER>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  const cudaError_t e = launch_pdl(kern, dim3((unsigned)(st->batch * SEL_CLUSTER)), dim3(SL_THREADS), smem, s,
-                                   SEL_CLUSTER, *st, *q, w, sel, sel_scores, cap, ucap, kcap);
+  cudaError_t e;
+  if (x) {
+    auto kern = fine_select_kernel<SEL_CLUSTER, true>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    e = launch_pdl(kern, dim3((unsigned)(st->batch * SEL_CLUSTER)), dim3(SL_THREADS), smem, s, SEL_CLUSTER, *st,
+                   *q, w, sel, sel_scores, cap, ucap, kcap, sel_local, *x);
+  } else {
+    auto kern = fine_select_kernel<SEL_CLUSTER, false>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    e = launch_pdl(kern, dim3((unsigned)(st->batch * SEL_CLUSTER)), dim3(SL_THREADS), smem, s, SEL_CLUSTER, *st,
+                   *q, w, sel, sel_scores, cap, ucap, kcap, (int32_t *)nullptr, XArgs{});
+  }
   return cuda_status(e, "fine_select");
+}
+
+kiv_status launch_fine_topk(const kiv_store *st, const kiv_query *q, const Workspace &w, int32_t *sel,
+                            float *sel_scores, cudaStream_t s) {
+  return launch_select(st, q, w, sel, sel_scores, nullptr, s, nullptr);
+}
+
+bool fine_exchange_eligible(const kiv_store *st, const kiv_query *q) {
+  const Workspace w = workspace_layout(st, q, nullptr);
+  const int rows_kv = (q->num_query_heads / st->num_kv_heads) * q->query_len;
+  // (<= 16 query rows per KV head: the shapes whose attention reads peer rows too)
+  return repl_summaries(*st) && st->host_capacity == 0 && fine_tc_eligible(st, q) && rows_kv <= 16 &&
+         w.u_cap <= 8192 && (int64_t)st->batch * SEL_CLUSTER <= sm_count();
+}
+
+kiv_status launch_fine_exchange_select(const kiv_store *st, const kiv_query *q, const Workspace &w, int32_t *sel,
+                                       int32_t *sel_local, cudaStream_t s, const XArgs &x) {
+  return launch_select(st, q, w, sel, nullptr, sel_local, s, &x);
 }
 
 kiv_status launch_fine_merge(const kiv_store *st, const kiv_query *q, const Workspace &w,

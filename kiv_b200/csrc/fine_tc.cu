@@ -21,8 +21,17 @@
 // batch row (each group stages its row's queries once).  Used when the store
 // is 16-bit, page_size == 128, head_dim is a multiple of 64 (<= 256) and
 // G*Q <= 32; otherwise fine_scores_kernel runs.
+//
+// Candidate exchange (XC, page-sharded stores with replicated summaries):
+// every shard holds the whole page union (the coarse pass is exact on each
+// shard), scores the union pages it owns, and stores each key at its global
+// candidate position (union position * S + token; the partial page after the
+// union) into every shard's exchange arena, as a flagged 64-bit word.  Each
+// shard's select then reads all candidates and takes the exact global top-P
+// itself, so no list merge follows.
 #include <algorithm>
 
+#include "exchange.cuh"
 #include "internal.h"
 #include "select.cuh"
 #include "tc.cuh"
@@ -41,10 +50,11 @@ struct TcGeom {
 // COARSE == false: fine scoring over candidate pages (key per token, max over rows)
 // COARSE == true:  coarse scoring over page summaries (score per row and page;
 //                  the per-row top-k builds the rows' histograms from them)
-template <bool BF16, bool COARSE>
+// XC: candidate exchange (fine only), keys to every shard's arena (see above)
+template <bool BF16, bool COARSE, bool XC>
 __global__ void __launch_bounds__(TC_THREADS, 1)
 scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_query q, Workspace w,
-                 int ncols, int stages, int union_inline, int cpb) {
+                 int ncols, int stages, int union_inline, int cpb, const __grid_constant__ XArgs x) {
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   extern __shared__ uint8_t tc_dyn[];
   __shared__ uint64_t full[4], empty[4], acc_full[2], acc_empty[2], ubar;
@@ -65,12 +75,14 @@ scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_que
   const int b = blockIdx.x / cpb, cj = blockIdx.x % cpb;
 
   // 1024-byte aligned carve-up: [stages][tile] [H][nbox][qbox] [hist 2048] [union list]
+  // (XC: [own positions] after the union list)
   const uint32_t base_addr = smem_u32(tc_dyn);
   uint8_t *smem = tc_dyn + ((1024 - (base_addr & 1023)) & 1023);
   uint8_t *stage_mem = smem;
   uint8_t *qmem = stage_mem + (size_t)stages * tile_bytes;
   uint32_t *hist = reinterpret_cast<uint32_t *>(qmem + (size_t)H * nbox * qbox_bytes);
   int32_t *ulist = reinterpret_cast<int32_t *>(hist + SEL_BINS);
+  int32_t *own = ulist + w.u_cap;
 
   // ---- prologue: independent of the previous kernel in the stream (with
   // programmatic dependent launch it overlaps that kernel's tail).  The
@@ -128,10 +140,12 @@ scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_que
   f.np_global = cold / S;
   f.partial = cold % S;
   f.part_owned = f.partial > 0 && (f.np_global % st.shard_count) == st.shard_rank;
-  const int64_t np_local = f.np_global > st.shard_rank
-                               ? (f.np_global - st.shard_rank + st.shard_count - 1) / st.shard_count : 0;
+  // page marks: one per local page, or per global page with replicated summaries
+  const int64_t nmark = coarse_pages(st, f.np_global);
+  const bool repl = repl_summaries(st);
+  int64_t n_own = 0;   // XC: this shard's pages of the union
   if (COARSE) {
-    clear_stale_marks(st, w, np_local);
+    clear_stale_marks(st, w, nmark);
     f.U = 0;
   } else if (union_inline) {
     // The page marks of a new coarse pass come in with one bulk copy into the
@@ -139,8 +153,12 @@ scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_que
     // is pending so that both reads share one round trip.  When one is, every
     // CTA builds the sorted union from the marks and CTA 0 also publishes it
     // (the select kernel and the reuse path read it from the workspace).
-    const uint32_t fbytes = (uint32_t)((((np_local + 31) / 32) * 4 + 15) & ~15ll);
-    const bool bulk = np_local > 0 && (int64_t)fbytes <= (int64_t)stages * tile_bytes && fbytes < (1u << 20);
+    // Global marks (replicated summaries) keep this shard's pages, or every
+    // page with the candidate exchange.
+    const int mrank = repl ? 0 : st.shard_rank, mcount = repl ? 1 : st.shard_count;
+    const int fcount = repl && !XC ? st.shard_count : 1;
+    const uint32_t fbytes = (uint32_t)((((nmark + 31) / 32) * 4 + 15) & ~15ll);
+    const bool bulk = nmark > 0 && (int64_t)fbytes <= (int64_t)stages * tile_bytes && fbytes < (1u << 20);
     if (bulk && threadIdx.x == 0) {
       mbar_arrive_tx(&ubar, fbytes);
       bulk_g2s(stage_mem, w.pbits, fbytes, &ubar);
@@ -149,11 +167,11 @@ scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_que
     if (bulk && !mbar_wait_bounded(&ubar, 0)) s_fail = 1;
     if (pending) {
       if (bulk)
-        f.U = union_from_bits<TC_THREADS, true>(reinterpret_cast<const uint32_t *>(stage_mem), np_local, ulist,
-                                                (int)w.u_cap, st.shard_rank, st.shard_count, s_psum);
+        f.U = union_from_bits<TC_THREADS, true>(reinterpret_cast<const uint32_t *>(stage_mem), nmark, ulist,
+                                                (int)w.u_cap, mrank, mcount, s_psum, st.shard_rank, fcount);
       else
-        f.U = union_from_bits<TC_THREADS, false>(w.pbits, np_local, ulist, (int)w.u_cap, st.shard_rank,
-                                                 st.shard_count, s_psum);
+        f.U = union_from_bits<TC_THREADS, false>(w.pbits, nmark, ulist, (int)w.u_cap, mrank, mcount, s_psum,
+                                                 st.shard_rank, fcount);
       if (blockIdx.x == 0) {
         for (int i = threadIdx.x; i < f.U; i += TC_THREADS) w.uni[i] = ulist[i];
         if (threadIdx.x == 0) st.state[KIV_ST_UNION] = f.U;
@@ -161,7 +179,13 @@ scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_que
       pages = ulist;
     } else {
       f.U = st_ld(st.state, KIV_ST_UNION);
+      if (XC) {
+        for (int i = threadIdx.x; i < f.U; i += TC_THREADS) ulist[i] = __ldcg(w.uni + i);
+        __syncthreads();
+        pages = ulist;
+      }
     }
+    if (XC) n_own = owned_positions<TC_THREADS>(ulist, (int)f.U, own, st.shard_rank, st.shard_count, s_psum);
     if (bulk) {
       // the stage ring is written by TMA next: order these generic reads first
       tc::fence_proxy_async_smem();
@@ -170,12 +194,19 @@ scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_que
   } else {
     f.U = st_ld(st.state, KIV_ST_UNION);
   }
-  f.per_b = f.U + (f.part_owned ? 1 : 0);
+  f.per_b = (XC ? n_own : f.U) + (f.part_owned ? 1 : 0);
+  // XC: the exchange epoch of the candidates (advanced by the select that reads them)
+  const unsigned long long xe = XC ? x_epoch(x, X_CAND) : 0ull;
+  // XC: global candidate position of unit u's first token
+  auto unit_pos = [&](int64_t u) -> int64_t {
+    if (!XC) return u * S;
+    return u < n_own ? (int64_t)own[u] * S : f.U * S;
+  };
   // per batch row b.  FINE: one unit per candidate page (tiles = its KV
   // heads); COARSE: one unit per block of 128 finalized local pages (tiles =
   // KV heads).  CTA cj of the row's cpb takes units cj, cj + cpb, ...
   // coarse: the pages this shard scores (all of them with replicated summaries)
-  const int64_t np_scored = COARSE ? coarse_pages(st, f.np_global) : np_local;
+  const int64_t np_scored = nmark;
   const int64_t units = COARSE ? (np_scored + TC_PAGE - 1) / TC_PAGE : f.per_b;
   const int64_t my_units = units > cj ? (units - cj + cpb - 1) / cpb : 0;
   const int64_t my_tiles = my_units * H;
@@ -196,7 +227,8 @@ scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_que
         if (COARSE) {
           y = (int32_t)((bh0 + kvh) * w.np_cap + u * TC_PAGE);
         } else {
-          const int64_t page = u < f.U ? (int64_t)pages[u] : f.np_global;
+          const int64_t nu = XC ? n_own : f.U;
+          const int64_t page = u < nu ? (int64_t)pages[XC ? own[u] : u] : f.np_global;
           const int64_t lp = page_slot(st, w, page / st.shard_count);
           y = (int32_t)((bh0 + kvh) * st.cold_capacity + lp * S);
         }
@@ -282,13 +314,19 @@ scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_que
       if (lane == 0) mbar_arrive(&acc_empty[a]);
       if ((t % H) == H - 1) {
         const int64_t u = cj + (t / H) * cpb;
-        const int n_tok = u < f.U ? TC_PAGE : (int)f.partial;
+        const int n_tok = u < (XC ? n_own : f.U) ? TC_PAGE : (int)f.partial;
         if (tok < n_tok) {
           const uint32_t key = f2key(m);
-          w.agg[(int64_t)b * w.c_cap + u * S + tok] = key;
-          // shared-memory atomic: the warp's keys fall in a few bins, which
-          // costs far less here than aggregating the lanes with a match
-          atomicAdd(&hist[key >> 21], 1u);
+          if (XC) {
+            // this candidate into every shard's arena (the select builds the histogram)
+            const int64_t c = (int64_t)b * w.c_cap + unit_pos(u) + tok;
+            for (int d = 0; d < x.world; ++d) ll_store(x_region(x, d, xe) + c, key, x_flag(xe));
+          } else {
+            w.agg[(int64_t)b * w.c_cap + u * S + tok] = key;
+            // shared-memory atomic: the warp's keys fall in a few bins, which
+            // costs far less here than aggregating the lanes with a match
+            atomicAdd(&hist[key >> 21], 1u);
+          }
           kmax = key > kmax ? key : kmax;
           ksum += m;
         }
@@ -308,7 +346,7 @@ scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_que
   __syncthreads();
   tc::fence_after_sync();
   // publish the histogram and the stats of batch row 0 for the select kernel
-  if (!COARSE) {
+  if (!COARSE && !XC) {
     for (int i = threadIdx.x; i < SEL_BINS; i += TC_THREADS)
       if (hist[i]) atomicAdd(&w.fhist[(int64_t)b * SEL_BINS + i], hist[i]);
   }
@@ -382,9 +420,10 @@ bool fine_tc_eligible(const kiv_store *st, const kiv_query *q) {
          getenv("KIV_DISABLE_TCGEN05") == nullptr;
 }
 
-// tensor-core scoring: coarse (summaries) or fine (candidate pages)
+// tensor-core scoring: coarse (summaries) or fine (candidate pages); x: the
+// candidate exchange (fine only)
 static kiv_status launch_scores_tc(const kiv_store *st, const kiv_query *q, const Workspace &w, cudaStream_t s,
-                                   bool coarse) {
+                                   bool coarse, const XArgs *x = nullptr) {
   KIV_CHECK(encode_fn());
   const int D = st->head_dim;
   const int rows_kv = (q->num_query_heads / st->num_kv_heads) * q->query_len;
@@ -410,11 +449,15 @@ static kiv_status launch_scores_tc(const kiv_store *st, const kiv_query *q, cons
   // fine pass: the union list is built in shared memory unless it is large
   // (with a host tier the union is staged before scoring: built separately)
   const int union_inline = !coarse && w.u_cap <= TC_UNION_INLINE && st->host_capacity == 0 ? 1 : 0;
+  if (x && !union_inline) {
+    set_error("candidate exchange needs the union built in the scorer (union cap %lld)", (long long)w.u_cap);
+    return KIV_ERR_UNSUPPORTED;
+  }
   if (!coarse && !union_inline) {
     KIV_CHECK(launch_union(st, w, s));
     KIV_CHECK(launch_stage_union(st, w, s));
   }
-  const size_t fixed = 1024 + qbytes + SEL_BINS * 4 + (union_inline ? (size_t)w.u_cap * 4 : 0);
+  const size_t fixed = 1024 + qbytes + SEL_BINS * 4 + (union_inline ? (size_t)w.u_cap * 4 * (x ? 2 : 1) : 0);
   const int stages = (int)std::min<size_t>(4, (200 * 1024 - fixed) / tile);
   if (stages < 2) return KIV_ERR_UNSUPPORTED;
   const size_t smem = fixed + (size_t)stages * tile;
@@ -422,18 +465,21 @@ static kiv_status launch_scores_tc(const kiv_store *st, const kiv_query *q, cons
   const int64_t units_cap = coarse ? ceil_div(w.np_cap, TC_PAGE) : w.u_cap + 1;
   const int64_t cpb = std::max<int64_t>(1, std::min<int64_t>(units_cap, sm_count() / st->batch));
   const int64_t grid = (int64_t)st->batch * cpb;
-#define KIV_TC_LAUNCH(BF, CO)                                                                          \
+  const XArgs xa = x ? *x : XArgs{};
+#define KIV_TC_LAUNCH(BF, CO, XC)                                                                      \
   do {                                                                                                 \
-    cudaFuncSetAttribute(scores_tc_kernel<BF, CO>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
-    e = launch_pdl(scores_tc_kernel<BF, CO>, dim3((unsigned)grid), dim3(TC_THREADS), smem, s, 1, map, *st, *q, w, \
-                   ncols, stages, union_inline, (int)cpb);                                              \
+    cudaFuncSetAttribute(scores_tc_kernel<BF, CO, XC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+    e = launch_pdl(scores_tc_kernel<BF, CO, XC>, dim3((unsigned)grid), dim3(TC_THREADS), smem, s, 1, map, *st, *q, \
+                   w, ncols, stages, union_inline, (int)cpb, xa);                                       \
   } while (0)
   const bool bf = st->dtype == KIV_DTYPE_BF16;
   cudaError_t e = cudaSuccess;
-  if (bf && coarse) KIV_TC_LAUNCH(true, true);
-  else if (bf) KIV_TC_LAUNCH(true, false);
-  else if (coarse) KIV_TC_LAUNCH(false, true);
-  else KIV_TC_LAUNCH(false, false);
+  if (bf && coarse) KIV_TC_LAUNCH(true, true, false);
+  else if (bf && x) KIV_TC_LAUNCH(true, false, true);
+  else if (bf) KIV_TC_LAUNCH(true, false, false);
+  else if (coarse) KIV_TC_LAUNCH(false, true, false);
+  else if (x) KIV_TC_LAUNCH(false, false, true);
+  else KIV_TC_LAUNCH(false, false, false);
 #undef KIV_TC_LAUNCH
   return cuda_status(e, coarse ? "coarse_scores_tc" : "fine_scores_tc");
 }
@@ -444,6 +490,11 @@ kiv_status launch_fine_score_tc(const kiv_store *st, const kiv_query *q, const W
 
 kiv_status launch_coarse_score_tc(const kiv_store *st, const kiv_query *q, const Workspace &w, cudaStream_t s) {
   return launch_scores_tc(st, q, w, s, true);
+}
+
+kiv_status launch_fine_score_tc_exchange(const kiv_store *st, const kiv_query *q, const Workspace &w,
+                                         cudaStream_t s, const XArgs &x) {
+  return launch_scores_tc(st, q, w, s, false, &x);
 }
 
 }  // namespace kiv

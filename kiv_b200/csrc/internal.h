@@ -30,7 +30,8 @@ constexpr int SEL_CLUSTER = 8;   // CTAs per cluster in the fine top-P select
 // Scratch carved out of the caller's workspace for one store / query shape.
 struct Workspace {
   float *scores;       // [R, np_cap]        coarse scores
-  uint32_t *pbits;     // [np_cap / 32]      page marks of the union (one bit per local page)
+  uint32_t *pbits;     // [np_cap / 32]      page marks of the union (one bit per local page; per
+                       //                    global page with replicated summaries)
   int32_t *uni;        // [u_cap]            union pages (global ids, ascending)
   uint32_t *agg;       // [B, c_cap]         fine keys (monotone u32 of the max score)
   int32_t *selcnt;     // [B]                selected tokens of this shard per batch row
@@ -109,6 +110,16 @@ bool prefill_tc_eligible(const kiv_store *st, const kiv_query *q);  // ... and t
 kiv_status launch_prefill_coarse_scores(const kiv_store *st, const kiv_query *q, const Workspace &w, cudaStream_t s);
 kiv_status launch_prefill_fine_scores(const kiv_store *st, const kiv_query *q, const Workspace &w, cudaStream_t s);
 kiv_status launch_coarse_score_tc(const kiv_store *st, const kiv_query *q, const Workspace &w, cudaStream_t s);
+// candidate exchange (page-sharded, replicated summaries): the scorer stores
+// every key into every shard's arena, the select takes the global top-P
+kiv_status launch_fine_score_tc_exchange(const kiv_store *st, const kiv_query *q, const Workspace &w,
+                                         cudaStream_t s, const XArgs &x);
+bool fine_exchange_eligible(const kiv_store *st, const kiv_query *q);
+kiv_status launch_attend_peers(const kiv_store *st, const kiv_query *q, const kiv_mask *m, const Workspace &w,
+                               const int32_t *sel, int32_t sel_stride, const kiv_peer_rows *peers, void *out,
+                               cudaStream_t s);
+kiv_status launch_fine_exchange_select(const kiv_store *st, const kiv_query *q, const Workspace &w, int32_t *sel,
+                                       int32_t *sel_local, cudaStream_t s, const XArgs &x);
 kiv_status launch_fine_topk(const kiv_store *st, const kiv_query *q, const Workspace &w, int32_t *sel,
                             float *sel_scores, cudaStream_t s);
 kiv_status launch_fine_merge(const kiv_store *st, const kiv_query *q, const Workspace &w,
@@ -123,7 +134,8 @@ kiv_status launch_attend(const kiv_store *st, const kiv_query *q, const kiv_mask
 kiv_status launch_attend_merge(const kiv_store *st, const kiv_query *q, const float *partials,
                                int32_t n, void *out, cudaStream_t s, const XArgs *x = nullptr);
 // per-rank payload bytes of the three exchanges (coarse lists, fine lists, attention partial)
-void exchange_payloads(const kiv_store *st, const kiv_query *q, int64_t *cb, int64_t *fb, int64_t *ab);
+void exchange_payloads(const kiv_store *st, const kiv_query *q, int64_t *cb, int64_t *fb, int64_t *ab,
+                       int64_t *xb);
 
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 

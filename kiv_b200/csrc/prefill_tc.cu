@@ -114,11 +114,9 @@ prefill_scores_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
   const int64_t np_global = cold / S;
   const int64_t partial = cold % S;
   const bool part_owned = partial > 0 && (np_global % st.shard_count) == st.shard_rank;
-  const int64_t np_local = np_global > st.shard_rank
-                               ? (np_global - st.shard_rank + st.shard_count - 1) / st.shard_count : 0;
   int64_t U = 0;
   if (COARSE) {
-    clear_stale_marks(st, w, np_local);
+    clear_stale_marks(st, w, coarse_pages(st, np_global));   // bits of the page marks
     if (blockIdx.x == 0 && threadIdx.x == 0) {
       st.state[KIV_ST_COARSE_MAX] = 0;
       st.state[KIV_ST_COARSE_SUM] = 0;

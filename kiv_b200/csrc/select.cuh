@@ -437,16 +437,27 @@ __device__ __forceinline__ int block_excl_sum(int v, int *total, int *wsum) {
   return before + x - v;
 }
 
+// Marks of word wi (pages 32 wi .. 32 wi + 31) that belong to shard `rank`
+// of `count` (page % count == rank).
+__device__ __forceinline__ uint32_t owner_mask(int64_t wi, int rank, int count) {
+  if (count <= 1) return ~0u;
+  uint32_t m = 0;
+  for (int j = (int)((rank - (wi * 32) % count + count) % count); j < 32; j += count) m |= 1u << j;
+  return m;
+}
+
 // Sorted union of the marked pages (bit i of bits[i / 32] set = local page i,
 // i < np) as global page ids (local page i -> i * nshard + rank) into
-// list[0, cap); returns the count.  bits is shared memory when SMEM, else
-// global.  Every thread of the CTA calls it.  Each thread owns UB_WORDS
-// consecutive words (UB_WORDS * 32 pages) per tile; the code is kept small
-// because it runs once per launch on cold instruction caches.
+// list[0, cap); returns the count.  With fcount > 1 the bitmap indexes global
+// pages (nshard = 1) and only the pages of shard frank (page % fcount ==
+// frank) are kept.  bits is shared memory when SMEM, else global.  Every
+// thread of the CTA calls it.  Each thread owns UB_WORDS consecutive words
+// (UB_WORDS * 32 pages) per tile; the code is kept small because it runs once
+// per launch on cold instruction caches.
 constexpr int UB_WORDS = 2;
 template <int BLOCK, bool SMEM>
 __device__ int union_from_bits(const uint32_t *bits, int64_t np, int32_t *list, int cap, int rank, int nshard,
-                               int *wsum) {
+                               int *wsum, int frank = 0, int fcount = 1) {
   const int64_t nw = (np + 31) / 32;
   int base = 0;
 #pragma unroll 1
@@ -460,6 +471,7 @@ __device__ int union_from_bits(const uint32_t *bits, int64_t np, int32_t *list, 
       uint32_t x = wi < nw ? (SMEM ? bits[wi] : __ldcg(bits + wi)) : 0u;
       const int64_t valid = np - wi * 32;            // pages of this word below np
       if (valid < 32) x &= valid > 0 ? (1u << valid) - 1u : 0u;
+      if (fcount > 1) x &= owner_mask(wi, frank, fcount);
       v[j] = x;
       c += __popc(x);
     }
@@ -480,6 +492,34 @@ __device__ int union_from_bits(const uint32_t *bits, int64_t np, int32_t *list, 
   }
   __syncthreads();
   return base < cap ? base : cap;
+}
+
+// Positions g < n (ascending) of the pages list[g] that belong to shard
+// `rank` of `count`, into out; returns their number.  Every thread of the CTA
+// calls it; ends with a barrier.
+template <int BLOCK>
+__device__ int owned_positions(const int32_t *list, int n, int32_t *out, int rank, int count, int *wsum) {
+  constexpr int IPT = 4;
+  int base = 0;
+#pragma unroll 1
+  for (int t0 = 0; t0 < n; t0 += BLOCK * IPT) {
+    const int i0 = t0 + threadIdx.x * IPT;
+    bool f[IPT];
+    int c = 0;
+#pragma unroll
+    for (int j = 0; j < IPT; ++j) {
+      f[j] = i0 + j < n && list[i0 + j] % count == rank;
+      c += f[j] ? 1 : 0;
+    }
+    int total;
+    int pos = base + block_excl_sum<BLOCK>(c, &total, wsum);
+#pragma unroll
+    for (int j = 0; j < IPT; ++j)
+      if (f[j]) out[pos++] = i0 + j;
+    base += total;
+  }
+  __syncthreads();
+  return base;
 }
 
 // Largest key and float sum of keys[0, n) of this CTA, added into two state

@@ -243,6 +243,27 @@ void attend(at::TensorList store, at::IntArrayRef geom, const Tensor &q, double 
         "attend");
 }
 
+void attend_peers(at::TensorList store, at::IntArrayRef geom, const Tensor &q, double scaling, int64_t top_pages,
+                  int64_t top_p, double softcap, const Tensor &ws, const Tensor &sel,
+                  const c10::optional<Tensor> &mask_add, bool causal, at::IntArrayRef peer_k, at::IntArrayRef peer_v,
+                  const Tensor &out) {
+  const kiv_store st = make_store(store, geom);
+  const kiv_query qd = make_query(q, scaling, top_pages, top_p, softcap);
+  const kiv_mask md = make_mask(mask_add, causal);
+  TORCH_CHECK(peer_k.size() == (size_t)st.shard_count && peer_v.size() == (size_t)st.shard_count &&
+                  st.shard_count <= KIV_MAX_PEERS,
+              "kiv: attend_peers needs one cold_k and cold_v address per shard");
+  kiv_peer_rows pr = {};
+  for (int r = 0; r < st.shard_count; ++r) {
+    pr.cold_k[r] = reinterpret_cast<const void *>(static_cast<uintptr_t>(peer_k[r]));
+    pr.cold_v[r] = reinterpret_cast<const void *>(static_cast<uintptr_t>(peer_v[r]));
+  }
+  c10::cuda::CUDAGuard g(q.device());
+  check(kiv_attend_peers(&st, &qd, &md, ws.data_ptr(), (size_t)ws.nbytes(), sel.data_ptr<int32_t>(),
+                         (int32_t)sel.size(1), &pr, out.data_ptr(), stream_of(q)),
+        "attend_peers");
+}
+
 void attend_merge(at::TensorList store, at::IntArrayRef geom, const Tensor &q, double scaling, int64_t top_pages,
                   int64_t top_p, double softcap, const Tensor &partials, const Tensor &out) {
   const kiv_store st = make_store(store, geom);
@@ -290,6 +311,20 @@ void fine_exchange_merge(at::TensorList store, at::IntArrayRef geom, const Tenso
   check(kiv_fine_exchange_merge(&st, &qd, ws.data_ptr(), (size_t)ws.nbytes(), scores.data_ptr<float>(),
                                 tokens.data_ptr<int32_t>(), &x, s, sel_local.data_ptr<int32_t>(), stream_of(q)),
         "fine_exchange_merge");
+}
+
+void fine_exchange_select(at::TensorList store, at::IntArrayRef geom, const Tensor &q, double scaling,
+                          int64_t top_pages, int64_t top_p, double softcap, const Tensor &ws, at::IntArrayRef arenas,
+                          int64_t arena_bytes, int64_t wait_cycles, const Tensor &sel,
+                          const c10::optional<Tensor> &sel_local) {
+  const kiv_store st = make_store(store, geom);
+  const kiv_query qd = make_query(q, scaling, top_pages, top_p, softcap);
+  const kiv_exchange x = make_exchange(st, arenas, arena_bytes, wait_cycles);
+  c10::cuda::CUDAGuard g(q.device());
+  int32_t *sl = sel_local.has_value() && sel_local->defined() ? sel_local->data_ptr<int32_t>() : nullptr;
+  check(kiv_fine_exchange_select(&st, &qd, ws.data_ptr(), (size_t)ws.nbytes(), &x, sel.data_ptr<int32_t>(), sl,
+                                 stream_of(q)),
+        "fine_exchange_select");
 }
 
 void attend_exchange_merge(at::TensorList store, at::IntArrayRef geom, const Tensor &q, double scaling,
@@ -380,6 +415,12 @@ void coarse_exchange_merge_meta(at::TensorList, at::IntArrayRef, const Tensor &,
 void fine_exchange_merge_meta(at::TensorList, at::IntArrayRef, const Tensor &, double, int64_t, int64_t, double,
                               const Tensor &, const Tensor &, const Tensor &, at::IntArrayRef, int64_t, int64_t,
                               const c10::optional<Tensor> &, const Tensor &) {}
+void fine_exchange_select_meta(at::TensorList, at::IntArrayRef, const Tensor &, double, int64_t, int64_t, double,
+                               const Tensor &, at::IntArrayRef, int64_t, int64_t, const Tensor &,
+                               const c10::optional<Tensor> &) {}
+void attend_peers_meta(at::TensorList, at::IntArrayRef, const Tensor &, double, int64_t, int64_t, double,
+                       const Tensor &, const Tensor &, const c10::optional<Tensor> &, bool, at::IntArrayRef,
+                       at::IntArrayRef, const Tensor &) {}
 void attend_exchange_merge_meta(at::TensorList, at::IntArrayRef, const Tensor &, double, int64_t, int64_t, double,
                                 const Tensor &, at::IntArrayRef, int64_t, int64_t, const Tensor &) {}
 
@@ -422,6 +463,13 @@ TORCH_LIBRARY(kiv, m) {
         "Tensor tokens, int[] arenas, int arena_bytes, int wait_cycles, Tensor(c!)? sel, Tensor(d!) sel_local) -> ()");
   m.def("attend_exchange_merge(Tensor(a!)[] store, int[] geom, " KIV_Q ", Tensor partial, int[] arenas, "
         "int arena_bytes, int wait_cycles, Tensor(b!) out) -> ()");
+  // Replaces, for page-sharded stores: kiv/cold_store.py:283-371 steps 2-3 (fine pass over the whole union)
+  m.def("fine_exchange_select(Tensor(a!)[] store, int[] geom, " KIV_Q ", Tensor(b!) ws, int[] arenas, "
+        "int arena_bytes, int wait_cycles, Tensor(c!) sel, Tensor(d!)? sel_local) -> ()");
+  // Replaces, for page-sharded stores: kiv/middleware.py:330-352, kiv/mask_utils.py:8-38 (rows read from
+  // every shard's cold tier; peer addresses as int[])
+  m.def("attend_peers(Tensor(a!)[] store, int[] geom, " KIV_Q ", Tensor(b!) ws, Tensor sel, Tensor? mask_add, "
+        "bool causal, int[] peer_k, int[] peer_v, Tensor(c!) out) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(kiv, CUDA, m) {
@@ -440,6 +488,8 @@ TORCH_LIBRARY_IMPL(kiv, CUDA, m) {
   m.impl("coarse_exchange_merge", &coarse_exchange_merge);
   m.impl("fine_exchange_merge", &fine_exchange_merge);
   m.impl("attend_exchange_merge", &attend_exchange_merge);
+  m.impl("fine_exchange_select", &fine_exchange_select);
+  m.impl("attend_peers", &attend_peers);
 }
 
 TORCH_LIBRARY_IMPL(kiv, Meta, m) {
@@ -458,6 +508,8 @@ TORCH_LIBRARY_IMPL(kiv, Meta, m) {
   m.impl("coarse_exchange_merge", &coarse_exchange_merge_meta);
   m.impl("fine_exchange_merge", &fine_exchange_merge_meta);
   m.impl("attend_exchange_merge", &attend_exchange_merge_meta);
+  m.impl("fine_exchange_select", &fine_exchange_select_meta);
+  m.impl("attend_peers", &attend_peers_meta);
 }
 
 TORCH_LIBRARY_IMPL(kiv, CompositeExplicitAutograd, m) { m.impl("workspace_layout", &workspace_layout); }

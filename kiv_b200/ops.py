@@ -68,4 +68,5 @@ def call(op, *args):
 
 OP_NAMES = ("state_reset", "append_evict", "workspace_layout", "coarse_select", "coarse_merge", "fine_score",
             "fine_topk", "fine_select", "fine_merge", "gather_rows", "attend", "attend_merge", "retrieve_attend",
-            "coarse_exchange_merge", "fine_exchange_merge", "attend_exchange_merge")
+            "coarse_exchange_merge", "fine_exchange_merge", "attend_exchange_merge", "fine_exchange_select",
+            "attend_peers")

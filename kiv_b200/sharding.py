@@ -8,19 +8,24 @@ everything after it is per sequence.  Page sharding (``shard_group``) splits
 one sequence's cold pages:
 
 The cold tier of a layer is partitioned by page over the GPUs of one box (page
-p lives on rank p % world).  A decode layer-step then needs three small
-exchanges of a few KB to tens of KB (latency-bound): per-row coarse
-candidates (score, page), per-batch-row fine candidates (score, token) and
-per-row attention partials (out, max, sum).  Each rank merges the gathered
-lists identically, so every rank ends with the exact global top-k and the same
-merged output.
+p lives on rank p % world), and every rank keeps every page's summary, so the
+coarse pass is exact on each rank.  On CUDA the fine pass then exchanges the
+candidates themselves: each rank scores its pages of the union and stores the
+keys into every rank's exchange arena over NVLink, every rank takes the exact
+global top-P (``kiv_fine_exchange_select``), and the attention reads each
+selected row from its owner's cold tier through a CUDA IPC mapping
+(``map_peers``, ``kiv_attend_peers``), so every rank computes the full output
+with no further exchange.  Shapes outside those kernels (and the collective
+transport) exchange lists instead -- per-batch-row fine candidates (score,
+token), then per-row attention partials (out, max, sum) -- and every rank
+merges them identically.
 
-On CUDA the exchanges go through peer memory: every rank allocates an
-exchange arena, the ranks swap CUDA IPC handles once over the process group,
-and the merge kernels store their lists straight into the peers' arenas over
-NVLink as words that carry the exchange's flag, and wait (bounded) until every
-rank's words carry it (``kiv_*_exchange_merge`` in the C ABI).  ``all_gather`` / ``all_reduce_sum`` (the process group's collectives)
-remain for the API paths that return tensors and for CPU process groups.
+Every rank allocates an exchange arena, the ranks swap CUDA IPC handles once
+over the process group, and the kernels store into the peers' arenas as words
+that carry the exchange's flag and wait (bounded) until every rank's words
+carry it.  ``all_gather`` / ``all_reduce_sum`` (the process group's
+collectives) remain for the API paths that return tensors and for CPU process
+groups.
 """
 
 from __future__ import annotations
@@ -39,6 +44,8 @@ class ShardComm:
         self.rank = dist.get_rank(group)
         self.size = dist.get_world_size(group)
         self._arenas: dict = {}
+        self._peer_maps: dict = {}
+        self._peer_bases: dict = {}      # (rank, its allocation base) -> (mapped base, device)
 
     def exchange(self, nbytes: int, device: torch.device):
         """The exchange descriptor of arenas of ``nbytes`` (every rank calls this
@@ -73,17 +80,64 @@ class ShardComm:
         self._arenas[key] = (desc, own.value, opened, device)
         return desc
 
-    def close(self) -> None:
-        """Unmap the peers' arenas and free this rank's (after all exchanges are done)."""
+    def map_peers(self, ptrs: list[int], device: torch.device) -> list[list[int]]:
+        """Every rank's address, as mapped in this process, of each device buffer
+        in ``ptrs`` (this rank's buffers; every rank calls this collectively with
+        its buffers of the same roles): ``out[i][r]`` is rank r's buffer i.  Each
+        peer allocation is mapped once (CUDA IPC); ``close`` unmaps them."""
         from . import _native as nat
 
-        L = nat.lib() if self._arenas else None
+        key = (tuple(int(p) for p in ptrs), device.index)
+        hit = self._peer_maps.get(key)
+        if hit is not None:
+            return hit
+        L = nat.lib()
+        mine = []
+        with torch.cuda.device(device):
+            for p in ptrs:
+                h = (ctypes.c_ubyte * nat.IPC_HANDLE_BYTES)()
+                off = ctypes.c_int64()
+                nat.check(L.kiv_peer_export(ctypes.c_void_p(int(p)), h, ctypes.byref(off)), "peer_export")
+                mine.append((bytes(h), int(p) - off.value, off.value))
+            everyone = [None] * self.size
+            dist.all_gather_object(everyone, mine, group=self.group)
+            out = [[0] * self.size for _ in ptrs]
+            for r, entries in enumerate(everyone):
+                for i, (hb, base, off) in enumerate(entries):
+                    if r == self.rank:
+                        out[i][r] = int(ptrs[i])
+                        continue
+                    got = self._peer_bases.get((r, base))
+                    if got is None:
+                        mp = ctypes.c_void_p()
+                        buf = (ctypes.c_ubyte * nat.IPC_HANDLE_BYTES).from_buffer_copy(hb)
+                        nat.check(L.kiv_peer_open(buf, ctypes.byref(mp)), "peer_open")
+                        got = (mp.value, device)
+                        self._peer_bases[(r, base)] = got
+                    out[i][r] = got[0] + off
+            dist.barrier(group=self.group)
+        self._peer_maps[key] = out
+        return out
+
+    def close(self) -> None:
+        """Unmap the peers' arenas and buffers and free this rank's arenas (after
+        all exchanges are done)."""
+        from . import _native as nat
+
+        L = nat.lib() if (self._arenas or self._peer_bases) else None
         for desc, own, opened, device in self._arenas.values():
             with torch.cuda.device(device):
                 torch.cuda.synchronize(device)
                 for p in opened:
                     L.kiv_peer_close(ctypes.c_void_p(p))
-        if self._arenas:
+        for mapped, device in self._peer_bases.values():
+            with torch.cuda.device(device):
+                torch.cuda.synchronize(device)
+                L.kiv_peer_close(ctypes.c_void_p(mapped))
+        had_peers = bool(self._peer_bases)
+        self._peer_bases.clear()
+        self._peer_maps.clear()
+        if self._arenas or had_peers:
             dist.barrier(group=self.group)
         for desc, own, opened, device in self._arenas.values():
             with torch.cuda.device(device):

@@ -15,7 +15,7 @@ NAMES = {0: "evict wait", 1: "evict end", 2: "coarse scorer wait", 3: "coarse sc
          5: "top-k staged", 9: "top-k end", 10: "fine scorer wait", 11: "fine union built", 12: "fine scorer end",
          13: "fine select wait", 14: "fine select end", 17: "fine exchange wait", 18: "fine lists in",
          19: "fine exchange end", 15: "attention cold wait", 16: "attention end", 20: "partials exchange wait",
-         21: "partials in", 22: "partials exchange end"}
+         21: "partials in", 22: "partials exchange end", 23: "candidates in (exchange)"}
 
 
 def load(pkg):

@@ -70,27 +70,31 @@ def _run_step(shape, dev, shard_group):
     scaling = spec.head_dim ** -0.5
     sel, P = store.retrieve_indices(q, scaling, cfg)
     from tests.gpu_helpers import kernel_union
-    union = kernel_union(store, 1, spec.num_query_heads, 1, cfg)     # this shard's pages of the union
+    # the union the fine pass built: the whole union with the candidate
+    # exchange, else this shard's pages of it
+    union = kernel_union(store, 1, spec.num_query_heads, 1, cfg)
+    whole = shard_group is not None and any(store._fx_ok.values())
     out = store.attend(q, scaling, cfg)
     torch.cuda.synchronize(dev)
     err = store.read_state()[7]
     summ = store.page_summaries().float().cpu().numpy()
     return (sel[:, :P].cpu().numpy(), out.float().cpu().numpy(), int(err),
-            (spec, prob, top_pages, top_p, summ, union))
+            (spec, prob, top_pages, top_p, summ, union, whole))
 
 
 def _union_check(problem, rank):
-    """This shard's pages of the coarse union against the oracle's union
-    (pages p % WORLD == rank), ties within 1e-6 of a row's k-th score aside."""
+    """The fine pass's coarse union against the oracle's union (all of it with
+    the candidate exchange, else pages p % WORLD == rank), ties within 1e-6
+    of a row's k-th score aside."""
     from tests.gpu_helpers import coarse_union_mismatch, oracle_decode
 
-    spec, prob, top_pages, top_p, summ, union = problem
+    spec, prob, top_pages, top_p, summ, union, whole = problem
     f32 = lambda t: t.float().numpy()
     ol = oracle_decode(spec, f32(prob.prefill_k), f32(prob.prefill_v), f32(prob.step_k), f32(prob.step_v),
                        storage="bf16")
     np.testing.assert_array_equal(summ, ol.store.summaries)
     ref, _, sc = ol.store.coarse(f32(prob.query), spec.head_dim ** -0.5, top_pages)
-    mine = np.array([p for p in ref.tolist() if p % WORLD == rank], np.int64)
+    mine = np.array([p for p in ref.tolist() if whole or p % WORLD == rank], np.int64)
     k = min(top_pages, ol.store.num_pages)
     bad = coarse_union_mismatch(union, mine, sc, k)
     assert bad == [], f"rank {rank}: union pages differ from the oracle's beyond ties: {bad[:6]} " \
@@ -102,7 +106,7 @@ def _oracle_check(sel, out, problem):
     from oracle.kiv_oracle import _group_rows, eager_attention, topk_set_mismatch
     from tests.gpu_helpers import oracle_decode, rel_err, rel_err_rows
 
-    spec, prob, top_pages, top_p, summ, _ = problem
+    spec, prob, top_pages, top_p, summ, _, _ = problem
     f32 = lambda t: t.float().numpy()
     ol = oracle_decode(spec, f32(prob.prefill_k), f32(prob.prefill_v), f32(prob.step_k), f32(prob.step_v),
                        storage="bf16")
@@ -154,6 +158,8 @@ def _worker(rank, port, out_dir, shape, exchange):
         sel_sh, out_sh, err_sh, problem = _run_step(shape, dev, comm)
         log("sharded step done")
         try:
+            # peer exchange takes the candidate exchange (one scorer + select, no merge)
+            assert problem[-1] == (exchange == "peer"), (exchange, problem[-1])
             _union_check(problem, rank)
         except AssertionError as e:
             failure = e
