@@ -67,6 +67,11 @@ class ExchangeDesc(ctypes.Structure):
                 ("wait_cycles", c_i64)]
 
 
+class PeerRows(ctypes.Structure):
+    """kiv_peer_rows: every shard's cold_k / cold_v as mapped in this process."""
+    _fields_ = [("cold_k", c_vp * MAX_PEERS), ("cold_v", c_vp * MAX_PEERS)]
+
+
 P = ctypes.POINTER
 # name -> (restype, argtypes)
 SIGNATURES = {
@@ -105,8 +110,8 @@ SIGNATURES = {
     "kiv_attend_exchange_merge": (c_i32, [P(StoreDesc), P(QueryDesc), c_vp, P(ExchangeDesc), c_vp, c_vp]),
     "kiv_fine_exchange_supported": (c_i32, [P(StoreDesc), P(QueryDesc)]),
     "kiv_peer_export": (c_i32, [c_vp, c_vp, P(c_i64)]),
-    "kiv_attend_peers": (c_i32, [P(StoreDesc), P(QueryDesc), P(MaskDesc), c_vp, c_sz, c_vp, c_i32, c_vp, c_vp,
-                                 c_vp]),
+    "kiv_attend_peers": (c_i32, [P(StoreDesc), P(QueryDesc), P(MaskDesc), c_vp, c_sz, c_vp, c_i32, P(PeerRows),
+                                 c_vp, c_vp]),
     "kiv_fine_exchange_select": (c_i32, [P(StoreDesc), P(QueryDesc), c_vp, c_sz, P(ExchangeDesc), c_vp, c_vp,
                                          c_vp]),
 }

@@ -43,11 +43,13 @@ int main(void) {{
   printf("kiv_query %zu\\n", sizeof(kiv_query));
   printf("kiv_mask %zu\\n", sizeof(kiv_mask));
   printf("kiv_exchange %zu\\n", sizeof(kiv_exchange));
+  printf("kiv_peer_rows %zu\\n", sizeof(kiv_peer_rows));
   F(kiv_store, cold_capacity) F(kiv_store, hot_capacity) F(kiv_store, cold_k) F(kiv_store, state)
   F(kiv_store, flags) F(kiv_store, page_sums)
   F(kiv_query, stride_t) F(kiv_query, scaling) F(kiv_query, top_p)
   F(kiv_mask, stride_t) F(kiv_mask, causal)
   F(kiv_exchange, arena) F(kiv_exchange, arena_bytes)
+  F(kiv_peer_rows, cold_v)
   return 0;
 }}''')
     exe = tmp_path / "layout"
@@ -57,11 +59,12 @@ int main(void) {{
     assert int(out["kiv_query"]) == ctypes.sizeof(nat.QueryDesc)
     assert int(out["kiv_mask"]) == ctypes.sizeof(nat.MaskDesc)
     assert int(out["kiv_exchange"]) == ctypes.sizeof(nat.ExchangeDesc)
+    assert int(out["kiv_peer_rows"]) == ctypes.sizeof(nat.PeerRows)
     for key, val in out.items():
         if "." in key:
             struct, field = key.split(".")
             cls = {"kiv_store": nat.StoreDesc, "kiv_query": nat.QueryDesc, "kiv_mask": nat.MaskDesc,
-                   "kiv_exchange": nat.ExchangeDesc}[struct]
+                   "kiv_exchange": nat.ExchangeDesc, "kiv_peer_rows": nat.PeerRows}[struct]
             assert getattr(cls, field).offset == int(val), key
 
 
@@ -111,3 +114,38 @@ def test_null_arguments_rejected():
     assert lib.kiv_coarse_select(ctypes.byref(st), ctypes.byref(q), None, 0, None, None, None) == 1
     q = nat.QueryDesc(4096, 0, 64, 64, 8, 1, 1.0, 0.0, 4, 4)
     assert lib.kiv_fine_select(ctypes.byref(st), ctypes.byref(q), None, 0, None, None, None) == 2
+
+
+def test_candidate_exchange_shapes_and_peer_attention_arguments():
+    """kiv_fine_exchange_supported is a host-side shape query; kiv_attend_peers
+    and kiv_fine_exchange_select reject bad arguments before launching."""
+    lib = nat.load_library()
+    q = nat.QueryDesc(4096, 0, 64, 64, 8, 1, 0.125, 0.0, 4, 64)
+    # bf16 page-sharded store with replicated summaries: eligible
+    repl = _store(shard_count=2, flags=nat.STORE_REPL_SUMMARIES, page_sums=20480)
+    assert lib.kiv_fine_exchange_supported(ctypes.byref(repl), ctypes.byref(q)) == 1
+    # one shard, no replicated summaries, fp32 rows, or more than 16 query rows per KV head: not
+    assert lib.kiv_fine_exchange_supported(ctypes.byref(_store()), ctypes.byref(q)) == 0
+    plain = _store(shard_count=2)
+    assert lib.kiv_fine_exchange_supported(ctypes.byref(plain), ctypes.byref(q)) == 0
+    f32 = _store(shard_count=2, flags=nat.STORE_REPL_SUMMARIES, page_sums=20480, dtype=0)
+    assert lib.kiv_fine_exchange_supported(ctypes.byref(f32), ctypes.byref(q)) == 0
+    wide = nat.QueryDesc(4096, 0, 64, 64, 40, 1, 0.125, 0.0, 4, 64)   # 20 rows per KV head
+    assert lib.kiv_fine_exchange_supported(ctypes.byref(repl), ctypes.byref(wide)) == 0
+    # peer-row attention: NULL peers, one shard, or a missing peer entry are rejected
+    ws_bytes = lib.kiv_workspace_bytes(ctypes.byref(repl), ctypes.byref(q))
+    ws = 1 << 20
+    assert lib.kiv_attend_peers(ctypes.byref(repl), ctypes.byref(q), None, ws, ws_bytes, 4096, 64, None,
+                                8192, None) == 1
+    peers = nat.PeerRows()
+    peers.cold_k[0], peers.cold_v[0] = 4096, 8192            # own entry; shard 1 missing
+    assert lib.kiv_attend_peers(ctypes.byref(repl), ctypes.byref(q), None, ws, ws_bytes, 4096, 64,
+                                ctypes.byref(peers), 8192, None) == 1
+    assert "shard 1" in lib.kiv_last_error().decode()
+    one = _store()
+    peers.cold_k[1], peers.cold_v[1] = 40960, 81920
+    assert lib.kiv_attend_peers(ctypes.byref(one), ctypes.byref(q), None, ws, ws_bytes, 4096, 64,
+                                ctypes.byref(peers), 8192, None) == 1
+    # the candidate exchange without an exchange descriptor
+    assert lib.kiv_fine_exchange_select(ctypes.byref(repl), ctypes.byref(q), ws, ws_bytes, None, 4096, None,
+                                        None) == 1
