@@ -369,3 +369,91 @@ def test_page_sharded_save_and_resume():
                         p.kill()
                 pytest.fail("ranks did not finish in 300 s")
         assert all(os.path.exists(os.path.join(d, f"ok{r}")) for r in range(WORLD))
+
+
+def _steps_worker(rank, port, out_dir):
+    """Many decode steps of a batch-2 page-sharded cache (peer transport:
+    candidate exchange + peer-row attention) against the same steps on one GPU:
+    pages complete on the way (running page sums, summaries), both exchange
+    parities and many epochs are used."""
+    import datetime
+
+    import torch.distributed as dist
+    from transformers import PretrainedConfig
+
+    from kiv_b200 import KIVConfig, ModelTopology, TieredKVCache
+    from kiv_b200.sharding import ShardComm
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["KIV_SHARD_EXCHANGE"] = "peer"
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    B, HQ, HKV, D, PRE, STEPS = 2, 8, 2, 128, 4096 + 60, 140
+    cfg = KIVConfig(hot_budget=256, page_size=128, top_pages=8, top_p=128, telemetry=False)
+    topo = ModelTopology.manual(global_layer_indices=(0,), num_query_heads=HQ, num_kv_heads=HKV, head_dim=D,
+                                num_hidden_layers=1)
+    g = torch.Generator().manual_seed(31)
+    pre_k = torch.randn(B, HKV, PRE, D, generator=g).to(torch.bfloat16)
+    pre_v = torch.randn(B, HKV, PRE, D, generator=g).to(torch.bfloat16)
+    ks = torch.randn(STEPS, B, HKV, 1, D, generator=g).to(torch.bfloat16)
+    vs = torch.randn(STEPS, B, HKV, 1, D, generator=g).to(torch.bfloat16)
+    qs = torch.randn(STEPS, B, HQ, 1, D, generator=g).to(torch.bfloat16)
+    scaling = D ** -0.5
+
+    def build(group):
+        c = TieredKVCache(PretrainedConfig(num_hidden_layers=1), cfg, topo, dev, shard_group=group)
+        c.update(pre_k.to(dev), pre_v.to(dev), 0)
+        c.mark_prefill_complete()
+        return c
+
+    dist.init_process_group("nccl", rank=rank, world_size=WORLD, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    comm = ShardComm()
+    try:
+        single = build(None) if rank == 0 else None
+        sharded = build(comm)
+        pages0 = sharded.get_cold_store(0).num_pages
+        worst = 0.0
+        for s in range(STEPS):
+            outs = []
+            for c in ([sharded, single] if rank == 0 else [sharded]):
+                c.update(ks[s].to(dev), vs[s].to(dev), 0)
+                st = c.get_cold_store(0)
+                sel, P = st.retrieve_indices(qs[s].to(dev), scaling, cfg)
+                out = st.attend(qs[s].to(dev), scaling, cfg)
+                outs.append((sel[:, :P].cpu(), out.float().cpu(), st))
+            if rank == 0:
+                (s_sel, s_out, s_st), (o_sel, o_out, o_st) = outs
+                assert s_st.read_state()[7] == 0 and o_st.read_state()[7] == 0, f"step {s}: error bits"
+                assert torch.equal(s_sel, o_sel), f"step {s}: sharded selection differs from one GPU"
+                rel = float((s_out - o_out).abs().max() / o_out.abs().max().clamp_min(1e-30))
+                worst = max(worst, rel)
+                assert rel <= 1e-2, f"step {s}: output rel {rel}"
+        assert any(sharded.get_cold_store(0)._fx_ok.values()), "the candidate exchange did not run"
+        assert sharded.get_cold_store(0).num_pages > pages0, "no page completed during the steps"
+        if rank == 0:
+            with open(os.path.join(out_dir, "ok"), "w") as f:
+                f.write(f"{worst}")
+        dist.barrier()
+        comm.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_decode_steps_match_single_gpu():
+    if torch.cuda.device_count() < WORLD:
+        pytest.skip(f"needs {WORLD} GPUs")
+    import torch.multiprocessing as mp
+
+    with tempfile.TemporaryDirectory() as d:
+        ctx = mp.start_processes(_steps_worker, args=(_free_port(), d), nprocs=WORLD, join=False,
+                                 start_method="spawn")
+        deadline = time.time() + 300
+        while not ctx.join(timeout=5):
+            if time.time() > deadline:
+                for p in ctx.processes:
+                    if p.is_alive():
+                        p.kill()
+                pytest.fail("ranks did not finish in 300 s")
+        assert os.path.exists(os.path.join(d, "ok"))
