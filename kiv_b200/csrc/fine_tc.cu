@@ -129,6 +129,27 @@ scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_que
   // ---- the previous kernel's results (state, union) are needed from here on;
   // the cold length too (an eviction may be the kernel right before this one)
   griddep_wait();
+  const int64_t bh0 = (int64_t)b * H;
+  // coarse pass: this CTA's first tile (page block cj of KV head 0 -- inside
+  // the summaries' capacity, cj < cpb <= blocks of np_cap) is loaded before
+  // the cold length is known; pages past it are masked in the epilogue
+  const bool coarse_first = COARSE && warp == 4 && lane == 0;
+  if (coarse_first) {
+    mbar_arrive_tx(&full[0], tile_bytes);
+    for (int j = 0; j < nbox; ++j)
+      tc::tma_load_2d(stage_mem + (size_t)j * TC_PAGE * 128, &kmap, 64 * j, (int32_t)(bh0 * w.np_cap + cj * TC_PAGE),
+                      &full[0]);
+  }
+  // fine pass: the whole page-mark bitmap (its capacity, so the copy does not
+  // wait for the cold length) comes in with one bulk copy into the still
+  // unused stage ring, in flight while the state words load
+  const uint32_t fbytes = (uint32_t)((((w.np_cap + 31) / 32) * 4 + 15) & ~15ll);
+  const bool bulk = !COARSE && union_inline && (int64_t)fbytes <= (int64_t)stages * tile_bytes &&
+                    fbytes < (1u << 20);
+  if (bulk && threadIdx.x == 0) {
+    mbar_arrive_tx(&ubar, fbytes);
+    bulk_g2s(stage_mem, w.pbits, fbytes, &ubar);
+  }
   const int64_t cold = st_ld(st.state, KIV_ST_COLD_LEN);
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     st.state[COARSE ? KIV_ST_COARSE_MAX : KIV_ST_FINE_MAX] = 0;
@@ -148,21 +169,15 @@ scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_que
     clear_stale_marks(st, w, nmark);
     f.U = 0;
   } else if (union_inline) {
-    // The page marks of a new coarse pass come in with one bulk copy into the
-    // (still unused) stage ring, issued before knowing whether a coarse pass
-    // is pending so that both reads share one round trip.  When one is, every
-    // CTA builds the sorted union from the marks and CTA 0 also publishes it
-    // (the select kernel and the reuse path read it from the workspace).
+    // The page marks of a new coarse pass (copied above, before knowing
+    // whether a coarse pass is pending, so that the reads share one round
+    // trip): when one is, every CTA builds the sorted union from the marks
+    // and CTA 0 also publishes it (the select kernel and the reuse path read
+    // it from the workspace).
     // Global marks (replicated summaries) keep this shard's pages, or every
     // page with the candidate exchange.
     const int mrank = repl ? 0 : st.shard_rank, mcount = repl ? 1 : st.shard_count;
     const int fcount = repl && !XC ? st.shard_count : 1;
-    const uint32_t fbytes = (uint32_t)((((nmark + 31) / 32) * 4 + 15) & ~15ll);
-    const bool bulk = nmark > 0 && (int64_t)fbytes <= (int64_t)stages * tile_bytes && fbytes < (1u << 20);
-    if (bulk && threadIdx.x == 0) {
-      mbar_arrive_tx(&ubar, fbytes);
-      bulk_g2s(stage_mem, w.pbits, fbytes, &ubar);
-    }
     const bool pending = st_ld(st.state, KIV_ST_UNION_PENDING) != 0;
     if (bulk && !mbar_wait_bounded(&ubar, 0)) s_fail = 1;
     if (pending) {
@@ -210,12 +225,14 @@ scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, kiv_store st, kiv_que
   const int64_t units = COARSE ? (np_scored + TC_PAGE - 1) / TC_PAGE : f.per_b;
   const int64_t my_units = units > cj ? (units - cj + cpb - 1) / cpb : 0;
   const int64_t my_tiles = my_units * H;
-  const int64_t bh0 = (int64_t)b * H;
 
   if (warp == 4) {
     if (lane == 0) {
       // ------------------------------------------------ TMA producer
-      for (int64_t t = 0; t < my_tiles; ++t) {
+      // (coarse: tile 0 is in flight already; with no tile to score, it is
+      // waited for before the CTA exits)
+      if (COARSE && my_tiles == 0 && !mbar_wait_bounded(&full[0], 0)) s_fail = 1;
+      for (int64_t t = COARSE ? 1 : 0; t < my_tiles; ++t) {
         const int s = (int)(t % stages);
         if (t >= stages && !mbar_wait_bounded(&empty[s], (uint32_t)((t / stages - 1) & 1))) {
           s_fail = 1;
