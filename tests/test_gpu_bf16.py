@@ -28,6 +28,9 @@ SHAPES = {
     # c3 (Llama-3-8B shape, batched decode) with 4 sequences and a shorter cold tier
     "c3": (SynthSpec(batch=4, num_query_heads=32, num_kv_heads=8, head_dim=128, cold_tokens=16384 + 37,
                      hot_budget=1024), dict(top_pages=32, top_p=512)),
+    # six sequences (the SMs do not divide evenly over them)
+    "c3b6": (SynthSpec(batch=6, num_query_heads=32, num_kv_heads=8, head_dim=128, cold_tokens=8192 + 37,
+                       hot_budget=512), dict(top_pages=16, top_p=256)),
 }
 
 
