@@ -687,7 +687,6 @@ class ColdKVStore:
         kv = ops.kiv()
         so = self._op_store()
         prof = self._profile
-        sel_local = self._buffer("sel_local", (B, top_p), torch.int32)
         x = self._exchange(qa)
         self._fine_x = x is not None and self.replicated_summaries and self._fine_exchange_supported(qa)
         if self._fine_x:
@@ -702,6 +701,7 @@ class ColdKVStore:
                 prof.record("fine_score_end")
                 prof.record("fine_topk_end")
             return sel
+        sel_local = self._buffer("sel_local", (B, top_p), torch.int32)
         lt = self._buffer("fl_t", (B, top_p), torch.int32)
         ls = self._buffer("fl_s", (B, top_p), torch.float32)
         if prof is not None:
