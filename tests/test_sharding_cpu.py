@@ -163,3 +163,26 @@ def test_sharded_layer_step_on_gloo_ranks():
     with tempfile.TemporaryDirectory() as d:
         mp.start_processes(_worker, args=(_free_port(), d), nprocs=WORLD, join=True, start_method="spawn")
         assert os.path.exists(os.path.join(d, "ok"))
+
+
+def test_every_shard_allocates_the_same_cold_capacity():
+    """Page-sharded stores size their cold slots by the largest shard's page
+    count, so every shard's store, workspace and exchange arena share one
+    layout (the candidate exchange indexes the arenas by global candidate
+    position, and the peer-row attention reads other shards' rows with this
+    shard's strides)."""
+    from kiv_b200 import ColdKVStore, KIVConfig, ModelTopology
+
+    cfg = KIVConfig(hot_budget=256, page_size=128, top_pages=8, top_p=128)
+    topo = ModelTopology.manual(global_layer_indices=(0,), num_query_heads=8, num_kv_heads=1, head_dim=128,
+                                num_hidden_layers=1)
+    for world in (2, 3, 4, 8):
+        stores = [ColdKVStore(cfg, topo, torch.device("cpu"), shard_rank=r, shard_count=world, comm=object())
+                  for r in range(world)]
+        for tokens in (1, 127, 128, 129, 1000, 4096 + 60, 1 << 20, (1 << 20) + 5):
+            caps = {s._round_local(tokens) for s in stores}
+            assert len(caps) == 1, (world, tokens, caps)
+            cap = caps.pop()
+            pages = -(-tokens // 128)
+            # enough slots for the pages of the shard holding the most
+            assert cap >= max(1, -(-pages // world)) * 128 and cap % 128 == 0
