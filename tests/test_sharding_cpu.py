@@ -186,3 +186,59 @@ def test_every_shard_allocates_the_same_cold_capacity():
             pages = -(-tokens // 128)
             # enough slots for the pages of the shard holding the most
             assert cap >= max(1, -(-pages // world)) * 128 and cap % 128 == 0
+
+
+def _cand_worker(rank, port, out_dir, world):
+    """The candidate exchange on gloo ranks: every rank holds the whole union
+    (replicated summaries), scores the candidates whose page it owns, and
+    writes each key at its global candidate position (union position x S +
+    token, then the partial page) into a position-indexed array that stands
+    for the arenas (here: a sum over the ranks, every position written by
+    exactly one); every rank then takes the top-P over all positions, which
+    must be the unsharded selection."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from kiv_b200.sharding import ShardComm, shard_of_page
+        comm = ShardComm()
+        ost, q, hk, hv = _problem(seed=11)
+        scaling, top_pages, top_p = 0.25, 6, 50
+        S = ost.page_size
+        union, _, _ = ost.coarse(q, scaling, top_pages)        # the same on every rank
+        cand = ost.candidates(union)                             # global candidate positions
+        agg_ref, sel_ref = ost.fine(q, scaling, cand, top_p)
+        B, C = agg_ref.shape
+        owner = np.array([shard_of_page(int(c) // S, world) for c in cand])
+        mine = np.nonzero(owner == rank)[0]
+        keys = np.zeros((B, C), np.float64)
+        wrote = np.zeros(C, np.int64)
+        if mine.size:
+            agg_mine, _ = ost.fine(q, scaling, cand[mine], top_p)
+            keys[:, mine] = agg_mine
+            wrote[mine] = 1
+        keys_t, wrote_t = torch.from_numpy(keys), torch.from_numpy(wrote)
+        comm.all_reduce_sum(keys_t)
+        comm.all_reduce_sum(wrote_t)
+        assert (wrote_t.numpy() == 1).all(), "every candidate position is written by exactly one rank"
+        allk = keys_t.numpy()
+        # (the oracle's float32 products over a subset of the candidates may round
+        # differently in the last place from the whole set's)
+        np.testing.assert_allclose(allk, agg_ref, rtol=1e-6, atol=1e-6)
+        P = sel_ref.shape[1]
+        for b in range(B):
+            got = np.sort(cand[topk_total_order(allk[b], P)])
+            assert got.tolist() == sel_ref[b].tolist()
+        if rank == 0:
+            with open(os.path.join(out_dir, "ok"), "w") as f:
+                f.write("ok")
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_candidate_exchange_on_gloo_ranks(world):
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_cand_worker, args=(_free_port(), d, world), nprocs=world, join=True,
+                           start_method="spawn")
+        assert os.path.exists(os.path.join(d, "ok"))
